@@ -1,0 +1,215 @@
+"""CPU restatement of SageAttention-2 semantics as the reference uses them — TEST INFRASTRUCTURE ONLY.
+
+This module is the checker for the CUDA path. It is imported by `tests/`, by
+`__graft_entry__.smoke()` and by the CPU legs of `bench.py`; the product never calls it.
+
+Parity status:
+  * Quantizers (Q per-warp int8, K mean-smoothed per-64-token int8, V per-channel e4m3) are
+    PINNED: `tests/golden/make_golden.py` runs the reference's own torch quantizers
+    (`experiments/modules/sage_kvq.py:57-75`) in the build container and commits their outputs;
+    `tests/test_oracle_golden.py` checks this file against them bit for bit.
+  * The attention kernel emulation (`attn_from_codes`) follows the kernel semantics the reference
+    documents (`experiments/bench_attn/splitkv/README.md:51-69`,
+    `experiments/bench_attn/h2_tiles/cfg_fixedmax.patch:90-93`, `phi_calib.md:12-13`,
+    `sage_kvq.py:15-19`). SageAttention itself is not vendored and has no CPU build, so this part
+    is checked by tolerance (cosine / max-abs), not bits: parity of the attention output is
+    unpinned by golden vectors, as in the reference, whose own tests replace Sage by SDPA.
+
+All citations are paths inside the reference project.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+# sage_kvq.py:29-35 — tile constants of the sm89 kernel the reference calls
+BLK_K, BLK_Q, WARP_Q = 64, 128, 32
+# sage_kvq.py:30-31 / sage_preq.py:66 — V scale ceiling for the fp32+fp16 PV accumulator
+V_SCALE_MAX = 2.25
+# splitkv/README.md:58, cfg_fixedmax.patch:13 — log2-domain offset that puts the row max of P at 448
+S_FP8_OFFSET = 8.807
+LOG2E = 1.4426950408889634
+# sage_kvq.py:34-35 — Sage's V layout permutes every 16 tokens like this
+V_PERM = [0, 1, 8, 9, 2, 3, 10, 11, 4, 5, 12, 13, 6, 7, 14, 15]
+
+
+def quant_int8(x: torch.Tensor, blk: int, pad_to: int, mean: torch.Tensor | None = None):
+    """Restates `sage_kvq._quant_int8` (sage_kvq.py:57-66) and Sage's QuantInt8Kernel.
+
+    x [B, n, H, D] (bf16) -> (codes int8 [B, n, H, D], scale f32 [B, H, ceil(n/pad_to)*pad_to/blk]).
+    Tokens past n count as zero (after the mean is subtracted). Codes are
+    round-half-even(x * (127/amax)) saturated to [-128, 127] in fp32; scale = amax/127 with
+    amax floored at 1e-7. The reference writes `127.0 / amax`, which torch evaluates as
+    reciprocal(amax) * 127 (two fp32 roundings, not one division); `amax / 127.0` is a true
+    fp32 division. Both are reproduced exactly here and in the CUDA kernels.
+    """
+    b, n, h, d = x.shape
+    xf = x.float() if mean is None else x.float() - mean.float()
+    lp = (n + pad_to - 1) // pad_to * pad_to
+    xf = F.pad(xf, (0, 0, 0, 0, 0, lp - n)).view(b, lp // blk, blk, h, d)
+    amax = xf.abs().amax(dim=(2, 4)).clamp_min(1e-7)
+    inv = torch.reciprocal(amax) * 127.0               # == torch's `127.0 / amax`
+    xq = (xf * inv[:, :, None, :, None]).round().clamp(-128, 127).to(torch.int8)
+    scale = (amax / 127.0).transpose(1, 2).contiguous()
+    return xq.view(b, lp, h, d)[:, :n], scale
+
+
+def quant_q(q: torch.Tensor):
+    """Q: one scale per (batch, head, 32-token group), Lq padded to 128 (per_warp_int8 with
+    BLKQ=128, WARPQ=32; call at sage_preq.py:116, restated at sage_kvq.py:104)."""
+    return quant_int8(q, WARP_Q, BLK_Q)
+
+
+def k_mean(k: torch.Tensor) -> torch.Tensor:
+    """km = mean of K over the window's tokens, rounded to K's dtype (sage_preq.py:115,
+    `k.mean(dim=1, keepdim=True)`). The sum is taken in float64, i.e. the exact mean of the bf16
+    inputs rounded once; torch's own fp32 reduction can differ from it by one bf16 ulp at a
+    rounding boundary (tests allow that one ulp against the reference and demand bits here)."""
+    return k.double().mean(dim=1, keepdim=True).to(k.dtype)
+
+
+def quant_k(k: torch.Tensor, km: torch.Tensor):
+    """K: subtract km, one scale per (batch, head, 64-token block) (sage_preq.py:116 with
+    BLKK=64; sage_kvq.py:85)."""
+    return quant_int8(k, BLK_K, BLK_K, km)
+
+
+def v_amax(v: torch.Tensor) -> torch.Tensor:
+    """Per-(batch, head, channel) max |v| over the window (sage_preq.py:47-63 min/max table,
+    sage_kvq.py:97 without the experimental V_MARGIN). Zero padding never raises it."""
+    return v.float().abs().amax(dim=1)
+
+
+def e4m3_rn_satfinite(x: torch.Tensor) -> torch.Tensor:
+    """fp32 -> e4m3 code (uint8), round-to-nearest-even, saturating to +-448 like the
+    `cvt.rn.satfinite.e4m3x2.f32` the CUDA kernels use (torch's cast alone turns >=464 into NaN)."""
+    return x.clamp(-448.0, 448.0).to(torch.float8_e4m3fn).view(torch.uint8)
+
+
+def e4m3_to_float(codes: torch.Tensor) -> torch.Tensor:
+    return codes.view(torch.float8_e4m3fn).float()
+
+
+def quant_v(v: torch.Tensor, amax: torch.Tensor):
+    """V: e4m3 codes of v * (2.25/amax) per (batch, head, channel), clamped to +-2.25
+    (sage_kvq.py:69-75, sage_preq.py:54,67-77). Returns codes in the natural token order
+    [B, n, H, D] (uint8) and v_scale = amax/2.25 [B, H, D]. Sage stores the same codes
+    transposed and permuted (`sage_layout`); the CUDA path stores them as V^T per head."""
+    recp = torch.reciprocal(amax) * V_SCALE_MAX        # == torch's `V_SCALE_MAX / v_amax`
+    x = v.float() * recp[:, None]
+    codes = x.clamp(-V_SCALE_MAX, V_SCALE_MAX).to(torch.float8_e4m3fn).view(torch.uint8)
+    return codes, amax / V_SCALE_MAX
+
+
+def sage_layout(v_codes: torch.Tensor) -> torch.Tensor:
+    """Natural-order V codes [B, n, H, D] (n % 16 == 0) -> Sage's [B, D, H, n] with the 16-token
+    permutation (sage_kvq.py:73-75)."""
+    b, n, h, d = v_codes.shape
+    vp = v_codes.view(b, n // 16, 16, h, d)[:, :, V_PERM].reshape(b, n, h, d)
+    return vp.permute(0, 3, 2, 1)
+
+
+def quantize_qkv(q, k, v):
+    """The quantization half of `sageattn(q, k, v, "NHD")` as the reference drives it
+    (attention.py:34 -> per_warp_int8 + per_channel_fp8, sage_preq.py:115-124)."""
+    qc, qs = quant_q(q)
+    km = k_mean(k)
+    kc, ks = quant_k(k, km)
+    am = v_amax(v)
+    vc, vs = quant_v(v, am)
+    return dict(q_codes=qc, q_scale=qs, km=km, k_codes=kc, k_scale=ks, v_codes=vc, v_scale=vs,
+                v_amax=am)
+
+
+def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_scale=None,
+                    tile=BLK_K, pv_accum="fp16", rows=None, heads=None):
+    """Torch emulation of Sage's `qk_int8_sv_f8_accum_f16_fuse_v_scale_attn_inst_buf` (the call at
+    sage_preq.py:126-127 / sage_kvq.py:107-110), non-causal, per-warp Q granularity.
+
+    Semantics (splitkv/README.md:51-69, cfg_fixedmax.patch:90-93, sage_kvq.py:15-19):
+      s      = (q_i8 . k_i8) * q_scale[row/32] * k_scale[key/64]        (int32 product is exact)
+      per key tile of `tile` keys, in order: m = running row max of s;
+      P      = exp2((s - m) * sm_scale * log2e + 8.807)                  (fp32, <= 448)
+      d      = d * exp2((m_old - m) * sm_scale * log2e) + sum(P)         (fp32 P, before fp8)
+      O      = O * same factor + e4m3(P) @ e4m3(V)                       (fp16 inside a tile when
+                                                                           pv_accum == "fp16")
+      out    = O / d * v_scale
+    Returns fp32 [B, Lq, H, D]. `rows` / `heads` restrict the computation to a subset (query rows
+    are independent, so the subset equals the same rows of the full result).
+    """
+    b, lq, h, d = q_codes.shape
+    lk = k_codes.shape[1]
+    if sm_scale is None:
+        sm_scale = d ** -0.5
+    sm_log2 = torch.tensor(sm_scale * LOG2E, dtype=torch.float32)
+    rows = torch.arange(lq) if rows is None else torch.as_tensor(rows)
+    heads = range(h) if heads is None else heads
+    out = torch.zeros(b, lq, h, d, dtype=torch.float32)
+    vq_all = e4m3_to_float(v_codes)                                    # [B, Lk, H, D]
+    off = torch.tensor(S_FP8_OFFSET, dtype=torch.float32)
+    for bi in range(b):
+        for hi in heads:
+            qf = q_codes[bi, rows, hi].float()                          # [R, D]
+            qs = q_scale[bi, hi][rows // WARP_Q]                         # [R]
+            kf = k_codes[bi, :, hi].float()                             # [Lk, D]
+            vf = vq_all[bi, :, hi]                                       # [Lk, D]
+            r = qf.shape[0]
+            m = torch.full((r,), -math.inf)
+            dsum = torch.zeros(r)
+            acc = torch.zeros(r, d)
+            for t0 in range(0, lk, tile):
+                t1 = min(t0 + tile, lk)
+                s_int = qf @ kf[t0:t1].T                                 # exact integers
+                ks = k_scale[bi, hi][torch.arange(t0, t1) // BLK_K]      # [T]
+                s = s_int * (qs[:, None] * ks[None, :])                  # dequantized, fp32
+                m_new = torch.maximum(m, s.max(dim=1).values)
+                alpha = torch.exp2((m - m_new) * sm_log2)
+                p = torch.exp2((s - m_new[:, None]) * sm_log2 + off)
+                dsum = dsum * alpha + p.sum(dim=1)
+                pq = e4m3_to_float(e4m3_rn_satfinite(p))
+                if pv_accum == "fp16":
+                    tile_acc = torch.zeros(r, d)
+                    for c0 in range(0, t1 - t0, 32):                     # m16n8k32 steps
+                        c1 = min(c0 + 32, t1 - t0)
+                        tile_acc = (tile_acc + pq[:, c0:c1] @ vf[t0 + c0:t0 + c1]).half().float()
+                else:
+                    tile_acc = pq @ vf[t0:t1]
+                acc = acc * alpha[:, None] + tile_acc
+                m = m_new
+            o = acc * (1.0 / dsum)[:, None] * v_scale[bi, hi][None, :]
+            out[bi, rows, hi] = o
+    return out
+
+
+def sage_attention(q, k, v, sm_scale=None, **kw):
+    """`sageattn(q, k, v, tensor_layout="NHD", is_causal=False, sm_scale)` (attention.py:34),
+    emulated on the CPU: quantize, then the kernel emulation. Returns bf16 [B, Lq, H, D]."""
+    qq = quantize_qkv(q, k, v)
+    o = attn_from_codes(qq["q_codes"], qq["q_scale"], qq["k_codes"], qq["k_scale"],
+                        qq["v_codes"], qq["v_scale"], sm_scale=sm_scale, **kw)
+    return o.to(q.dtype)
+
+
+def sdpa_fp32(q, k, v, sm_scale=None, rows=None, heads=None):
+    """Unquantized fp32 attention, the accuracy baseline reported beside every comparison."""
+    b, lq, h, d = q.shape
+    if sm_scale is None:
+        sm_scale = d ** -0.5
+    rows = torch.arange(lq) if rows is None else torch.as_tensor(rows)
+    heads = list(range(h)) if heads is None else list(heads)
+    out = torch.zeros(b, lq, h, d, dtype=torch.float32)
+    for bi in range(b):
+        for hi in heads:
+            s = (q[bi, rows, hi].float() @ k[bi, :, hi].float().T) * sm_scale
+            out[bi, rows, hi] = torch.softmax(s, dim=-1) @ v[bi, :, hi].float()
+    return out
+
+
+def compare(a: torch.Tensor, b: torch.Tensor) -> dict:
+    """Error metrics used throughout (splitkv/check.py:48-56)."""
+    a, b = a.float().flatten(), b.float().flatten()
+    dlt = (a - b).abs()
+    return dict(cos=F.cosine_similarity(a, b, dim=0).item(), max_abs=dlt.max().item(),
+                rel_l2=((a - b).norm() / b.norm()).item())
