@@ -1,0 +1,146 @@
+/* lbq — B200 (sm_100a) quantized attention for the LingBot-World causal DiT.
+ *
+ * C ABI of `liblbq.so`. Every entry point takes plain device pointers, element counts and strides
+ * and a `cudaStream_t` (passed as `void*`); it validates its arguments, launches on that stream
+ * only (no synchronisation, no allocation), and returns 0 or an LBQ_ERR_* code. On error,
+ * `lbq_last_error()` describes the failure (thread-local). The caller allocates every buffer.
+ *
+ * Tensors follow the reference's "NHD" activations: q/k/v/out are [B, L, H, 128] bf16 with
+ * arbitrary element strides for B, L and H (the channel stride must be 1, base addresses and the
+ * three strides 16-byte aligned).
+ *
+ * Quantized window layout (produced by the quantizers, consumed by lbq_attn_fwd):
+ *   q_codes  int8 [B][H][q_pad][128]        q_pad   = round_up(q_len, 128)
+ *   q_scale  f32  [B][H][q_pad/32]
+ *   k_codes  int8 [S][B][H][seg_pad][128]   seg_pad = round_up(seg_len, 128)
+ *   k_scale  f32  [S][B][H][seg_pad/64]
+ *   vt_codes u8   [S][B][H][128][seg_pad]   (e4m3, keys contiguous per channel)
+ *   v_scale  f32  [B][H][128]
+ *   km       bf16 [B][H][128]
+ * S is the number of KV segments: 1 on one GPU; one per rank after the all-gather of a sequence
+ * split (segment s holds tokens [s*seg_len, min((s+1)*seg_len, kv_len)) of the window).
+ * Paths in citations are inside the reference project (kaarelkaarelson/lingbot-world-v2-realtime).
+ */
+#ifndef LBQ_H_
+#define LBQ_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LBQ_API __attribute__((visibility("default")))
+#else
+#define LBQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LBQ_OK 0
+#define LBQ_ERR_ARG 1          /* bad shape, stride, length or null pointer */
+#define LBQ_ERR_ALIGN 2        /* pointer or stride not 16-byte aligned */
+#define LBQ_ERR_CUDA 3         /* CUDA runtime / driver error (launch, tensor map) */
+#define LBQ_ERR_UNSUPPORTED 4  /* head_dim != 128, causal, ... */
+
+/* Version of this ABI (major * 100 + minor). */
+LBQ_API int lbq_abi_version(void);
+
+/* Message of the last error on this thread ("" if none). */
+LBQ_API const char* lbq_last_error(void);
+
+/* Device status word of the current device: 0, or the code of the first device-side wait that
+ * gave up (a pipeline stalled past its time limit; the kernel returned early and its output is
+ * invalid). Synchronous. `clear` != 0 resets it to 0 afterwards. */
+LBQ_API int lbq_device_status(int clear, int* status_out);
+
+/* Per-64-token-block statistics of a bf16 K/V window: ksum (fp64 sum of K per channel) and vamax
+ * (max |V| per channel) for blocks [blk_begin, blk_end) of tokens [0, kv_len).
+ * Tables are [B][max_blocks][H][128]. Block b covers tokens [64b, min(64b+64, kv_len)).
+ * Replaces the per-64-token V min/max table of lingbot/layers/sage_preq.py:36-44,87-98
+ * (`_blk_minmax`, `_update`) and extends it with the K sums the mean-smoothing needs. */
+LBQ_API int lbq_kv_block_stats(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h,
+                       const void* v, int64_t sv_b, int64_t sv_l, int64_t sv_h,
+                       int batch, int heads, int64_t kv_len, int blk_begin, int blk_end,
+                       int64_t max_blocks, double* ksum, float* vamax, void* stream);
+
+/* Reduce the block statistics of blocks [blk_begin, blk_end) into per-(batch, head, channel)
+ * totals: ksum_total (fp64) and vamax_total. With several ranks, each reduces its own blocks and
+ * the totals are all-reduced (sum / max) before quantizing.
+ * Replaces the window reductions of sage_preq.py:47-63 (`_v_scale`) and :115 (`k.mean`). */
+LBQ_API int lbq_kv_window_sums(const double* ksum, const float* vamax, int batch, int heads, int blk_begin,
+                       int blk_end, int64_t max_blocks, double* ksum_total, float* vamax_total,
+                       void* stream);
+
+/* Q quantizer: int8 per (batch, head, 32-token group), Lq padded to 128 (rows >= q_len encode 0).
+ * Replaces the Q half of sageattention.quant.per_warp_int8(q, k, km, "NHD", BLKQ=128, WARPQ=32,
+ * BLKK=64) called at lingbot/layers/sage_preq.py:116 (semantics restated at
+ * experiments/modules/sage_kvq.py:57-66,104). */
+LBQ_API int lbq_quant_q(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, int batch, int heads,
+                int q_len, int8_t* q_codes, float* q_scale, void* stream);
+
+/* K/V quantizer for one segment of the window: tokens [tok0, tok0 + seg_valid) of k/v become
+ * segment `seg` of the code buffers (num_segments segments in total). km = bf16(ksum_total /
+ * kv_len_total); K codes per 64-token block of (k - km); V codes e4m3 of v * (2.25/vamax_total).
+ * `km_out` (nullable) and `v_scale` are written when `write_totals` != 0.
+ * Replaces the K half of per_warp_int8 (sage_preq.py:115-116) and Sage's V
+ * transpose/pad/permute + per-channel fp8 quantization (sage_preq.py:67-77, 121-124;
+ * sage_kvq.py:69-75). */
+LBQ_API int lbq_quant_kv(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h,
+                 const void* v, int64_t sv_b, int64_t sv_l, int64_t sv_h,
+                 int batch, int heads, int64_t tok0, int seg, int num_segments, int seg_valid,
+                 int seg_len, int64_t kv_len_total, const double* ksum_total,
+                 const float* vamax_total, int8_t* k_codes, float* k_scale, uint8_t* vt_codes,
+                 void* km_out, float* v_scale, int write_totals, void* stream);
+
+/* Scratch bytes lbq_quant_qkv needs for batch x heads and kv_len tokens. */
+LBQ_API size_t lbq_quant_qkv_workspace(int batch, int heads, int64_t kv_len);
+
+/* The whole per-call quantization of sageattn(q, k, v, "NHD") (lingbot/layers/attention.py:34):
+ * block stats -> window sums -> Q, K, V codes, in 5 launches, with a caller-provided workspace of
+ * lbq_quant_qkv_workspace() bytes. One segment. */
+LBQ_API int lbq_quant_qkv(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, int q_len,
+                  const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h,
+                  const void* v, int64_t sv_b, int64_t sv_l, int64_t sv_h, int64_t kv_len,
+                  int batch, int heads, int8_t* q_codes, float* q_scale, int8_t* k_codes,
+                  float* k_scale, uint8_t* vt_codes, float* v_scale, void* km_out,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Re-quantize a bf16 KV cache window [0, kv_len) whose block statistics are current (kept by
+ * lbq_kv_block_stats on every write): window sums + K/V codes, one segment, in 3 launches.
+ * `sums_ws` holds B*H*128 doubles followed by B*H*128 floats.
+ * Replaces the per-call re-quantization of the cache window done by sageattn / sage_preq.attend
+ * (lingbot/layers/sage_preq.py:107-124) and sage_kvq.requant_all (experiments/modules/sage_kvq.py:93-98). */
+LBQ_API int lbq_requant_cache(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h,
+                      const void* v, int64_t sv_b, int64_t sv_l, int64_t sv_h,
+                      int batch, int heads, int64_t kv_len, int64_t max_blocks,
+                      const double* ksum, const float* vamax, void* sums_ws,
+                      int8_t* k_codes, float* k_scale, uint8_t* vt_codes, float* v_scale,
+                      void* km_out, void* stream);
+
+/* Attention over quantized codes (non-causal). out [B, q_len, H, 128] bf16 with element strides
+ * so_*. sm_scale <= 0 means 1/sqrt(128). num_splits > 1 splits the key range (flash-decoding):
+ * partial results go to o_part (f32, [splits][B*H][q_pad][128]) and ml_part (f32 pairs,
+ * [splits][B*H][q_pad]) and lbq_splitkv_combine finishes them; num_splits is clamped so that no
+ * split is empty (the value used is written to *splits_used when non-null).
+ * Replaces sm89_compile.qk_int8_sv_f8_accum_f16_fuse_v_scale_attn_inst_buf(q_i8, k_i8, v_fp8, o,
+ * q_s, k_s, v_s, 0, 0, 2, sm_scale, 0) called at lingbot/layers/sage_preq.py:126-127 and
+ * experiments/modules/sage_kvq.py:107-110, with the split-KV variant designed in
+ * experiments/bench_attn/splitkv/README.md. */
+LBQ_API int lbq_attn_fwd(const int8_t* q_codes, const float* q_scale, int q_len,
+                 const int8_t* k_codes, const float* k_scale, const uint8_t* vt_codes,
+                 const float* v_scale, int64_t kv_len, int num_segments, int seg_len,
+                 int batch, int heads, float sm_scale, void* out, int64_t so_b, int64_t so_l,
+                 int64_t so_h, int num_splits, float* o_part, float* ml_part, int* splits_used,
+                 void* stream);
+
+/* Flash-decoding merge of lbq_attn_fwd's split partials into out (bf16), applying the V scale.
+ * The combine kernel of experiments/bench_attn/splitkv/README.md:67-69 (`splitkv_combine_kernel`). */
+LBQ_API int lbq_splitkv_combine(const float* o_part, const float* ml_part, int num_splits,
+                        const float* v_scale, int batch, int heads, int q_len, void* out,
+                        int64_t so_b, int64_t so_l, int64_t so_h, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LBQ_H_ */

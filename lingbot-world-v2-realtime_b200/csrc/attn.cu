@@ -1,0 +1,384 @@
+// Quantized attention forward for sm_100a: INT8 Q.K^T and FP8 P.V on tcgen05, accumulators in
+// tensor memory, operands staged by TMA, warp-specialised.
+//
+// Semantics are those of SageAttention-2's `qk_int8_sv_f8_accum_f16_fuse_v_scale_attn_inst_buf`
+// as the reference calls it (lingbot/layers/sage_preq.py:126-127 with qk_quant_gran=2, i.e. one
+// Q scale per 32 rows; documented in experiments/bench_attn/splitkv/README.md:51-69 and
+// h2_tiles/cfg_fixedmax.patch:90-93):
+//   s   = (q_i8 . k_i8) * q_scale * k_scale * sm_scale * log2(e)      (int32 dot product, exact)
+//   m   = running row max of s, updated once per 128-key tile
+//   P   = exp2(s - m + 8.807)  (<= 448), rounded to e4m3 for the P.V product
+//   d   = d * exp2(m_old - m) + sum(P)                                (fp32, before rounding)
+//   O   = O * exp2(m_old - m) + e4m3(P) . e4m3(V)                      (fp32 in tensor memory)
+//   out = O / d * v_scale  -> bf16
+// Differences from the sm89 kernel (covered by the tolerance tests): the running max is updated
+// per 128 keys instead of 64, P.V accumulates in fp32 rather than fp16 inside a tile, and exp2 is
+// the ex2.approx instruction on an fma of the dequantized score.
+//
+// CTA = one 128-row Q tile x one (batch, head) x one KV split. Warps: 0 = TMA producer,
+// 1 = tcgen05 issuer (one thread), 2..5 = softmax / correction / epilogue; softmax thread i owns
+// Q row i of the tile, which is TMEM lane i.
+// Tensor memory (512 columns): S0 [0,128), S1 [128,256) as int32 scores; the first 32 columns of
+// each S buffer are overwritten by that tile's e4m3 P (4 per column); O f32 [256,384).
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "lbq_kernels.h"
+#include "lbq_ptx.cuh"
+
+namespace lbq {
+
+constexpr int kStages = 4;
+constexpr int kTile = 128 * 128;         // bytes of one 128 x 128 8-bit tile
+constexpr int kAttnThreads = 192;
+constexpr float kFp8Offset = 8.807f;     // splitkv/README.md:58 (S_FP8_OFFSET)
+
+struct AttnBarriers {
+  uint64_t q_full;
+  uint64_t k_full[kStages];
+  uint64_t k_empty[kStages];
+  uint64_t v_full[kStages];
+  uint64_t v_empty[kStages];
+  uint64_t s_full[2];
+  uint64_t p_full;
+  uint64_t o_done;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr size_t kAttnSmemBytes = 1024 /*alignment slack*/ + kTile * (1 + 2 * kStages) + sizeof(AttnBarriers);
+
+__device__ int g_status;
+
+__device__ __forceinline__ int seg_valid(const AttnArgs& a, int seg) {
+  const int rest = a.kv_len - seg * a.seg_len;
+  return rest < a.seg_len ? rest : a.seg_len;
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + kTile;
+  uint8_t* sV = smem + kTile * (1 + kStages);
+  AttnBarriers* bar = reinterpret_cast<AttnBarriers*>(smem + kTile * (1 + 2 * kStages));
+  volatile int* abort_flag = &bar->abort;
+
+  const int qt = blockIdx.x, bh = blockIdx.y, split = blockIdx.z;
+  const int b = bh / a.heads, h = bh - b * a.heads;
+  const int t_begin = split * a.tiles_per_split;
+  const int t_end = min(t_begin + a.tiles_per_split, a.total_tiles);
+  const int n = t_end - t_begin;
+  const int tiles_per_seg = a.seg_pad / 128;
+  const int bhs = a.batch * a.heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bar->k_full[s], 1);
+      mbar_init(&bar->k_empty[s], 1);
+      mbar_init(&bar->v_full[s], 1);
+      mbar_init(&bar->v_empty[s], 1);
+    }
+    mbar_init(&bar->s_full[0], 1);
+    mbar_init(&bar->s_full[1], 1);
+    mbar_init(&bar->p_full, 128);
+    mbar_init(&bar->o_done, 1);
+    mbar_init(&bar->drain, 1);
+    bar->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bar->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  const uint32_t tS0 = tmem, tS1 = tmem + 128, tO = tmem + 256;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0 && n > 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      mbar_arrive_expect_tx(&bar->q_full, kTile);
+      tma_load_3d(sQ, &tm_q, &bar->q_full, 0, qt * 128, bh);
+      int issued = 0;
+      for (int i = 0; i < n; ++i) {
+        const int jt = t_begin + i;
+        const int seg = jt / tiles_per_seg, lt = jt - seg * tiles_per_seg;
+        const int s = i % kStages;
+        const uint32_t ph = (i / kStages) & 1;
+        if (!mbar_wait(&bar->k_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) break;
+        mbar_arrive_expect_tx(&bar->k_full[s], kTile);
+        tma_load_3d(sK + s * kTile, &tm_k, &bar->k_full[s], 0, lt * 128, seg * bhs + bh);
+        if (!mbar_wait(&bar->v_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) {
+          issued = i + 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&bar->v_full[s], kTile);
+        tma_load_3d(sV + s * kTile, &tm_v, &bar->v_full[s], lt * 128, 0, seg * bhs + bh);
+        issued = i + 1;
+      }
+      if (*abort_flag) {
+        // Let copies already in flight land before the CTA's shared memory goes away.
+        for (int i = (issued > kStages ? issued - kStages : 0); i < issued; ++i) {
+          const int s = i % kStages;
+          const uint32_t ph = (i / kStages) & 1;
+          mbar_drain_wait(&bar->k_full[s], ph);
+          mbar_drain_wait(&bar->v_full[s], ph);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ tcgen05 issuer
+    if (lane == 0 && n > 0) {
+      bool ok = mbar_wait(&bar->q_full, 0, abort_flag, a.status, kDevTimeoutQ);
+      tc_fence_after();
+      const uint64_t qdesc = smem_desc_sw128(smem_u32(sQ));
+      auto issue_pv = [&](int j) -> bool {
+        if (!mbar_wait(&bar->p_full, j & 1, abort_flag, a.status, kDevTimeoutP)) return false;
+        const int s = j % kStages;
+        if (!mbar_wait(&bar->v_full[s], (j / kStages) & 1, abort_flag, a.status, kDevTimeoutKV)) return false;
+        tc_fence_after();
+        const uint64_t vdesc = smem_desc_sw128(smem_u32(sV + s * kTile));
+        const uint32_t tp = (j & 1) ? tS1 : tS0;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f8_ts(tO, tp + 8 * kk, vdesc + 2 * kk, kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&bar->v_empty[s]);
+        tc_commit(&bar->o_done);
+        return true;
+      };
+      for (int i = 0; ok && i < n; ++i) {
+        const int s = i % kStages;
+        if (!mbar_wait(&bar->k_full[s], (i / kStages) & 1, abort_flag, a.status, kDevTimeoutKV)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t kdesc = smem_desc_sw128(smem_u32(sK + s * kTile));
+        const uint32_t ts = (i & 1) ? tS1 : tS0;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) mma_i8_ss(ts, qdesc + 2 * kk, kdesc + 2 * kk, kIdescQK, kk > 0 ? 1u : 0u);
+        tc_commit(&bar->s_full[i & 1]);
+        tc_commit(&bar->k_empty[s]);
+        if (i > 0) ok = issue_pv(i - 1);
+      }
+      if (ok) issue_pv(n - 1);
+      // Drain: every MMA issued above has completed once `drain` flips.
+      tc_commit(&bar->drain);
+      mbar_drain_wait(&bar->drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warpgroup
+    const int quarter = warp & 3;                       // TMEM lanes [32*quarter, 32*quarter+32)
+    const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+    const int row = qt * 128 + quarter * 32 + lane;
+    const float qs = a.q_scale[int64_t(bh) * (a.q_pad / 32) + qt * 4 + quarter];
+    const int kspb = a.seg_pad / 64;
+    float m = -INFINITY, dsum = 0.f;
+    bool ok = n > 0;
+    for (int i = 0; ok && i < n; ++i) {
+      const int jt = t_begin + i;
+      const int seg = jt / tiles_per_seg, lt = jt - seg * tiles_per_seg;
+      const int valid = min(128, seg_valid(a, seg) - lt * 128);
+      const float* ksp = a.k_scale + int64_t(seg * bhs + bh) * kspb + lt * 2;
+      const float c1a = __fmul_rn(__fmul_rn(qs, ksp[0]), a.sm_log2);
+      const float c1b = __fmul_rn(__fmul_rn(qs, ksp[1]), a.sm_log2);
+      if (!mbar_wait(&bar->s_full[i & 1], (i >> 1) & 1, abort_flag, a.status, kDevTimeoutS)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t ts = ((i & 1) ? tS1 : tS0) + lane_off;
+      uint32_t sv[4][32];
+      tmem_ld32(ts + 0, sv[0]);
+      tmem_ld32(ts + 32, sv[1]);
+      tmem_ld32(ts + 64, sv[2]);
+      tmem_ld32(ts + 96, sv[3]);
+      tmem_ld_wait();
+      int mxa = INT32_MIN, mxb = INT32_MIN;
+#pragma unroll
+      for (int c = 0; c < 64; ++c)
+        if (c < valid) mxa = max(mxa, int32_t(sv[c >> 5][c & 31]));
+#pragma unroll
+      for (int c = 64; c < 128; ++c)
+        if (c < valid) mxb = max(mxb, int32_t(sv[c >> 5][c & 31]));
+      float tmax = -INFINITY;
+      if (mxa != INT32_MIN) tmax = __fmul_rn(float(mxa), c1a);
+      if (mxb != INT32_MIN) tmax = fmaxf(tmax, __fmul_rn(float(mxb), c1b));
+      const float m_new = fmaxf(m, tmax);
+      const float alpha = (m_new == -INFINITY || m == m_new) ? 1.f : ex2_approx(m - m_new);
+      const float c0 = kFp8Offset - m_new;
+      float psum = 0.f;
+      uint32_t pw[32];
+#pragma unroll
+      for (int w = 0; w < 32; ++w) {
+        float p4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = 4 * w + e;
+          const float cc = c < 64 ? c1a : c1b;
+          float p = 0.f;
+          if (c < valid) p = ex2_approx(fmaf(float(int32_t(sv[c >> 5][c & 31])), cc, c0));
+          p4[e] = p;
+          psum += p;
+        }
+        pw[w] = pack_e4m3x2(p4[0], p4[1]) | (pack_e4m3x2(p4[2], p4[3]) << 16);
+      }
+      dsum = __fmaf_rn(dsum, alpha, psum);
+      tmem_st32(((i & 1) ? tS1 : tS0) + lane_off, pw);
+      tmem_st_wait();
+      if (i > 0) {
+        if (!mbar_wait(&bar->o_done, (i - 1) & 1, abort_flag, a.status, kDevTimeoutO)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t ov[32];
+            tmem_ld32(tO + lane_off + 32 * c, ov);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+            tmem_st32(tO + lane_off + 32 * c, ov);
+          }
+          tmem_st_wait();
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bar->p_full);
+      m = m_new;
+    }
+    if (ok && mbar_wait(&bar->o_done, (n - 1) & 1, abort_flag, a.status, kDevTimeoutO)) {
+      tc_fence_after();
+      if (a.num_splits == 1) {
+        const float rd = __frcp_rn(dsum);
+        const float* vs = a.v_scale + int64_t(bh) * 128;
+        __nv_bfloat16* dst = a.out + b * a.so_b + int64_t(row) * a.so_l + h * a.so_h;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t ov[32];
+          tmem_ld32(tO + lane_off + 32 * c, ov);
+          tmem_ld_wait();
+          uint32_t packed[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float o0 = __fmul_rn(__fmul_rn(__uint_as_float(ov[2 * e]), rd), vs[32 * c + 2 * e]);
+            const float o1 = __fmul_rn(__fmul_rn(__uint_as_float(ov[2 * e + 1]), rd), vs[32 * c + 2 * e + 1]);
+            const __nv_bfloat162 pr = __floats2bfloat162_rn(o0, o1);
+            packed[e] = *reinterpret_cast<const uint32_t*>(&pr);
+          }
+          if (row < a.q_len) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              reinterpret_cast<uint4*>(dst + 32 * c)[e] =
+                  make_uint4(packed[4 * e], packed[4 * e + 1], packed[4 * e + 2], packed[4 * e + 3]);
+          }
+        }
+      } else {
+        const int64_t prow = (int64_t(split) * bhs + bh) * a.q_pad + row;
+        float* dst = a.o_part + prow * 128;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t ov[32];
+          tmem_ld32(tO + lane_off + 32 * c, ov);
+          tmem_ld_wait();
+          if (row < a.q_len) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              reinterpret_cast<uint4*>(dst + 32 * c)[e] = make_uint4(ov[4 * e], ov[4 * e + 1], ov[4 * e + 2], ov[4 * e + 3]);
+          }
+        }
+        if (row < a.q_len) a.ml_part[prow] = make_float2(m, dsum);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// Flash-decoding merge of the per-split partials (splitkv/README.md:60-69): one warp per
+// (row, batch*head), 4 channels per lane.
+__global__ void __launch_bounds__(128) splitkv_combine_kernel(const CombineArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 4 + warp;
+  const int bh = blockIdx.y;
+  if (row >= a.q_len) return;
+  const int bhs = a.batch * a.heads;
+  float mx = -INFINITY;
+  for (int s = 0; s < a.num_splits; ++s) mx = fmaxf(mx, a.ml_part[(int64_t(s) * bhs + bh) * a.q_pad + row].x);
+  float L = 0.f;
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < a.num_splits; ++s) {
+    const int64_t prow = (int64_t(s) * bhs + bh) * a.q_pad + row;
+    const float2 ml = a.ml_part[prow];
+    const float w = ml.x == -INFINITY ? 0.f : ex2_approx(ml.x - mx);
+    L = fmaf(w, ml.y, L);
+    const float4 p = reinterpret_cast<const float4*>(a.o_part + prow * 128)[lane];
+    o.x = fmaf(w, p.x, o.x);
+    o.y = fmaf(w, p.y, o.y);
+    o.z = fmaf(w, p.z, o.z);
+    o.w = fmaf(w, p.w, o.w);
+  }
+  const float rl = __frcp_rn(L);
+  const float4 vs = reinterpret_cast<const float4*>(a.v_scale + int64_t(bh) * 128)[lane];
+  const int b = bh / a.heads, h = bh - b * a.heads;
+  const __nv_bfloat162 p0 = __floats2bfloat162_rn(o.x * rl * vs.x, o.y * rl * vs.y);
+  const __nv_bfloat162 p1 = __floats2bfloat162_rn(o.z * rl * vs.z, o.w * rl * vs.w);
+  uint2 st;
+  st.x = *reinterpret_cast<const uint32_t*>(&p0);
+  st.y = *reinterpret_cast<const uint32_t*>(&p1);
+  *reinterpret_cast<uint2*>(a.out + b * a.so_b + int64_t(row) * a.so_l + h * a.so_h + lane * 4) = st;
+}
+
+cudaError_t launch_attn(const AttnArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                        cudaStream_t st) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static bool configured[64] = {};
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kAttnSmemBytes));
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  dim3 grid(a.q_pad / 128, a.batch * a.heads, a.num_splits);
+  attn_fwd_kernel<<<grid, kAttnThreads, kAttnSmemBytes, st>>>(tm_q, tm_k, tm_v, a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st) {
+  dim3 grid((a.q_len + 3) / 4, a.batch * a.heads);
+  splitkv_combine_kernel<<<grid, 128, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+// Address of this device's status word (looked up once per device, with that device current).
+int* device_status_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  static int* ptrs[64] = {};
+  if (ptrs[dev] == nullptr) {
+    int* p = nullptr;
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_status) != cudaSuccess) return nullptr;
+    ptrs[dev] = p;
+  }
+  return ptrs[dev];
+}
+
+}  // namespace lbq

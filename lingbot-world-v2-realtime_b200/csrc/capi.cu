@@ -1,0 +1,306 @@
+// C ABI of liblbq.so (declared in include/lbq.h): argument validation, tensor-map encoding and
+// launches. Nothing here allocates device memory or synchronises, except lbq_device_status().
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+
+#include "../../include/lbq.h"
+#include "lbq_kernels.h"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(LBQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+// Checks a [B, L, H, 128] bf16 activation: non-null, 16-byte aligned base and strides.
+int check_act(const char* name, const void* p, int64_t sb, int64_t sl, int64_t sh) {
+  if (p == nullptr) return fail(LBQ_ERR_ARG, "%s is null", name);
+  if (!aligned16(p)) return fail(LBQ_ERR_ALIGN, "%s is not 16-byte aligned", name);
+  if (sb % 8 || sl % 8 || sh % 8 || sb < 0 || sl < 0 || sh < 0)
+    return fail(LBQ_ERR_ALIGN, "%s strides (%lld, %lld, %lld) must be non-negative multiples of 8 elements",
+                name, (long long)sb, (long long)sl, (long long)sh);
+  return LBQ_OK;
+}
+int check_ptr(const char* name, const void* p) {
+  if (p == nullptr) return fail(LBQ_ERR_ARG, "%s is null", name);
+  if (!aligned16(p)) return fail(LBQ_ERR_ALIGN, "%s is not 16-byte aligned", name);
+  return LBQ_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 3-D uint8 tensor map with a 128 x 128 box and 128-byte swizzle.
+int make_map(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
+             uint64_t stride2, const char* name) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(LBQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {stride1, stride2};
+  const cuuint32_t box[3] = {128, 128, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LBQ_ERR_CUDA, "tensor map for %s: CUresult %d", name, int(r));
+  return LBQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int lbq_abi_version(void) { return 100; }
+
+const char* lbq_last_error(void) { return g_err; }
+
+int lbq_device_status(int clear, int* status_out) {
+  int* p = lbq::device_status_ptr();
+  if (p == nullptr) return fail(LBQ_ERR_CUDA, "device status word unavailable");
+  int v = 0;
+  cudaError_t e = cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read status");
+  if (clear) {
+    const int zero = 0;
+    e = cudaMemcpy(p, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "clear status");
+  }
+  if (status_out) *status_out = v;
+  return LBQ_OK;
+}
+
+int lbq_kv_block_stats(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,
+                       int64_t sv_l, int64_t sv_h, int batch, int heads, int64_t kv_len, int blk_begin, int blk_end,
+                       int64_t max_blocks, double* ksum, float* vamax, void* stream) {
+  int r;
+  if ((r = check_act("k", k, sk_b, sk_l, sk_h)) || (r = check_act("v", v, sv_b, sv_l, sv_h))) return r;
+  if ((r = check_ptr("ksum", ksum)) || (r = check_ptr("vamax", vamax))) return r;
+  if (batch <= 0 || heads <= 0 || kv_len <= 0) return fail(LBQ_ERR_ARG, "batch, heads and kv_len must be positive");
+  if (blk_begin < 0 || blk_end > (kv_len + 63) / 64 || blk_end > max_blocks)
+    return fail(LBQ_ERR_ARG, "block range [%d, %d) outside the window (%lld tokens, %lld table rows)", blk_begin,
+                blk_end, (long long)kv_len, (long long)max_blocks);
+  if (blk_end <= blk_begin) return LBQ_OK;
+  lbq::KvBlockStatsArgs a{static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v),
+                          sk_b, sk_l, sk_h, sv_b, sv_l, sv_h, batch, heads, kv_len, blk_begin, blk_end,
+                          max_blocks, ksum, vamax};
+  cudaError_t e = lbq::launch_kv_block_stats(a, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "kv_block_stats launch");
+}
+
+int lbq_kv_window_sums(const double* ksum, const float* vamax, int batch, int heads, int blk_begin, int blk_end,
+                       int64_t max_blocks, double* ksum_total, float* vamax_total, void* stream) {
+  int r;
+  if ((r = check_ptr("ksum", ksum)) || (r = check_ptr("vamax", vamax)) || (r = check_ptr("ksum_total", ksum_total)) ||
+      (r = check_ptr("vamax_total", vamax_total)))
+    return r;
+  if (batch <= 0 || heads <= 0) return fail(LBQ_ERR_ARG, "batch and heads must be positive");
+  if (blk_begin < 0 || blk_end < blk_begin || blk_end > max_blocks)
+    return fail(LBQ_ERR_ARG, "block range [%d, %d) invalid for %lld table rows", blk_begin, blk_end,
+                (long long)max_blocks);
+  lbq::KvWindowSumsArgs a{ksum, vamax, batch, heads, blk_begin, blk_end, max_blocks, ksum_total, vamax_total};
+  cudaError_t e = lbq::launch_kv_window_sums(a, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "kv_window_sums launch");
+}
+
+int lbq_quant_q(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, int batch, int heads, int q_len,
+                int8_t* q_codes, float* q_scale, void* stream) {
+  int r;
+  if ((r = check_act("q", q, sq_b, sq_l, sq_h)) || (r = check_ptr("q_codes", q_codes)) ||
+      (r = check_ptr("q_scale", q_scale)))
+    return r;
+  if (batch <= 0 || heads <= 0 || q_len <= 0) return fail(LBQ_ERR_ARG, "batch, heads and q_len must be positive");
+  lbq::QuantQArgs a{static_cast<const __nv_bfloat16*>(q), sq_b, sq_l, sq_h, batch, heads, q_len,
+                    int(round_up(q_len, 128)), q_codes, q_scale};
+  cudaError_t e = lbq::launch_quant_q(a, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "quant_q launch");
+}
+
+int lbq_quant_kv(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b, int64_t sv_l,
+                 int64_t sv_h, int batch, int heads, int64_t tok0, int seg, int num_segments, int seg_valid,
+                 int seg_len, int64_t kv_len_total, const double* ksum_total, const float* vamax_total,
+                 int8_t* k_codes, float* k_scale, uint8_t* vt_codes, void* km_out, float* v_scale, int write_totals,
+                 void* stream) {
+  int r;
+  if ((r = check_act("k", k, sk_b, sk_l, sk_h)) || (r = check_act("v", v, sv_b, sv_l, sv_h))) return r;
+  if ((r = check_ptr("ksum_total", ksum_total)) || (r = check_ptr("vamax_total", vamax_total)) ||
+      (r = check_ptr("k_codes", k_codes)) || (r = check_ptr("k_scale", k_scale)) || (r = check_ptr("vt_codes", vt_codes)))
+    return r;
+  if (write_totals && (r = check_ptr("v_scale", v_scale))) return r;
+  if (batch <= 0 || heads <= 0 || seg_len <= 0 || kv_len_total <= 0 || num_segments <= 0)
+    return fail(LBQ_ERR_ARG, "batch, heads, seg_len, kv_len and num_segments must be positive");
+  if (seg < 0 || seg >= num_segments) return fail(LBQ_ERR_ARG, "segment %d of %d", seg, num_segments);
+  if (seg_len % 64 && num_segments > 1)
+    return fail(LBQ_ERR_ARG, "seg_len %d must be a multiple of 64 so K blocks match the whole window's", seg_len);
+  if (seg_valid <= 0 || seg_valid > seg_len) return fail(LBQ_ERR_ARG, "seg_valid %d not in (0, %d]", seg_valid, seg_len);
+  if (tok0 < 0) return fail(LBQ_ERR_ARG, "tok0 must be >= 0");
+  const int seg_pad = int(round_up(seg_len, 128));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  lbq::QuantKArgs ka{static_cast<const __nv_bfloat16*>(k), sk_b, sk_l, sk_h, batch, heads, tok0, seg, seg_valid,
+                     seg_pad, kv_len_total, ksum_total, k_codes, k_scale,
+                     static_cast<__nv_bfloat16*>(km_out), write_totals};
+  cudaError_t e = lbq::launch_quant_k(ka, st);
+  if (e != cudaSuccess) return cuda_fail(e, "quant_k launch");
+  lbq::QuantVArgs va{static_cast<const __nv_bfloat16*>(v), sv_b, sv_l, sv_h, batch, heads, tok0, seg, seg_valid,
+                     seg_pad, vamax_total, vt_codes, v_scale, write_totals};
+  e = lbq::launch_quant_vt(va, st);
+  return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "quant_vt launch");
+}
+
+size_t lbq_quant_qkv_workspace(int batch, int heads, int64_t kv_len) {
+  const int64_t nblk = (kv_len + 63) / 64;
+  const int64_t cols = int64_t(batch) * heads * 128;
+  return size_t(nblk * cols * (8 + 4) + cols * (8 + 4) + 64);
+}
+
+int lbq_quant_qkv(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, int q_len, const void* k, int64_t sk_b,
+                  int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b, int64_t sv_l, int64_t sv_h, int64_t kv_len,
+                  int batch, int heads, int8_t* q_codes, float* q_scale, int8_t* k_codes, float* k_scale,
+                  uint8_t* vt_codes, float* v_scale, void* km_out, void* workspace, size_t workspace_bytes,
+                  void* stream) {
+  if (kv_len <= 0 || kv_len > (int64_t(1) << 30)) return fail(LBQ_ERR_ARG, "kv_len %lld out of range", (long long)kv_len);
+  if (workspace == nullptr || workspace_bytes < lbq_quant_qkv_workspace(batch, heads, kv_len))
+    return fail(LBQ_ERR_ARG, "workspace of %zu bytes is smaller than the %zu needed", workspace_bytes,
+                lbq_quant_qkv_workspace(batch, heads, kv_len));
+  if (!aligned16(workspace)) return fail(LBQ_ERR_ALIGN, "workspace is not 16-byte aligned");
+  const int nblk = int((kv_len + 63) / 64);
+  const int64_t cols = int64_t(batch) * heads * 128;
+  double* ksum = static_cast<double*>(workspace);
+  double* ksum_total = ksum + int64_t(nblk) * cols;
+  float* vamax = reinterpret_cast<float*>(ksum_total + cols);
+  float* vamax_total = vamax + int64_t(nblk) * cols;
+  int r = lbq_kv_block_stats(k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h, batch, heads, kv_len, 0, nblk, nblk, ksum,
+                             vamax, stream);
+  if (r) return r;
+  if ((r = lbq_kv_window_sums(ksum, vamax, batch, heads, 0, nblk, nblk, ksum_total, vamax_total, stream))) return r;
+  if ((r = lbq_quant_q(q, sq_b, sq_l, sq_h, batch, heads, q_len, q_codes, q_scale, stream))) return r;
+  return lbq_quant_kv(k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h, batch, heads, 0, 0, 1, int(kv_len), int(kv_len),
+                      kv_len, ksum_total, vamax_total, k_codes, k_scale, vt_codes, km_out, v_scale, 1, stream);
+}
+
+int lbq_requant_cache(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,
+                      int64_t sv_l, int64_t sv_h, int batch, int heads, int64_t kv_len, int64_t max_blocks,
+                      const double* ksum, const float* vamax, void* sums_ws, int8_t* k_codes, float* k_scale,
+                      uint8_t* vt_codes, float* v_scale, void* km_out, void* stream) {
+  int r;
+  if ((r = check_ptr("sums_ws", sums_ws))) return r;
+  if (kv_len <= 0 || kv_len > (int64_t(1) << 30)) return fail(LBQ_ERR_ARG, "kv_len %lld out of range", (long long)kv_len);
+  const int nblk = int((kv_len + 63) / 64);
+  if (nblk > max_blocks) return fail(LBQ_ERR_ARG, "kv_len %lld needs %d stats rows, table has %lld", (long long)kv_len,
+                                     nblk, (long long)max_blocks);
+  const int64_t cols = int64_t(batch) * heads * 128;
+  double* ksum_total = static_cast<double*>(sums_ws);
+  float* vamax_total = reinterpret_cast<float*>(ksum_total + cols);
+  if ((r = lbq_kv_window_sums(ksum, vamax, batch, heads, 0, nblk, max_blocks, ksum_total, vamax_total, stream))) return r;
+  return lbq_quant_kv(k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h, batch, heads, 0, 0, 1, int(kv_len), int(kv_len),
+                      kv_len, ksum_total, vamax_total, k_codes, k_scale, vt_codes, km_out, v_scale, 1, stream);
+}
+
+int lbq_attn_fwd(const int8_t* q_codes, const float* q_scale, int q_len, const int8_t* k_codes, const float* k_scale,
+                 const uint8_t* vt_codes, const float* v_scale, int64_t kv_len, int num_segments, int seg_len,
+                 int batch, int heads, float sm_scale, void* out, int64_t so_b, int64_t so_l, int64_t so_h,
+                 int num_splits, float* o_part, float* ml_part, int* splits_used, void* stream) {
+  int r;
+  if ((r = check_ptr("q_codes", q_codes)) || (r = check_ptr("q_scale", q_scale)) || (r = check_ptr("k_codes", k_codes)) ||
+      (r = check_ptr("k_scale", k_scale)) || (r = check_ptr("vt_codes", vt_codes)) || (r = check_ptr("v_scale", v_scale)))
+    return r;
+  if ((r = check_act("out", out, so_b, so_l, so_h))) return r;
+  if (batch <= 0 || heads <= 0 || q_len <= 0 || kv_len <= 0 || num_segments <= 0 || seg_len <= 0)
+    return fail(LBQ_ERR_ARG, "batch, heads, q_len, kv_len, num_segments and seg_len must be positive");
+  if (int64_t(num_segments) * seg_len < kv_len || int64_t(num_segments - 1) * seg_len >= kv_len)
+    return fail(LBQ_ERR_ARG, "%d segments of %d tokens do not cover exactly %lld tokens", num_segments, seg_len,
+                (long long)kv_len);
+  if (num_segments > 1 && seg_len % 64)
+    return fail(LBQ_ERR_ARG, "seg_len %d must be a multiple of 64 with several segments", seg_len);
+  if (kv_len > (int64_t(1) << 30) || q_len > (1 << 30)) return fail(LBQ_ERR_ARG, "length too large");
+  if (int64_t(batch) * heads * num_segments > 65535 * 32) return fail(LBQ_ERR_ARG, "too many batch*heads*segments");
+  const int q_pad = int(round_up(q_len, 128));
+  const int seg_pad = int(round_up(seg_len, 128));
+  const int tiles_per_seg = seg_pad / 128;
+  const int last_valid = int(kv_len - int64_t(num_segments - 1) * seg_len);
+  const int total_tiles = (num_segments - 1) * tiles_per_seg + (last_valid + 127) / 128;
+  if (num_splits < 1) num_splits = 1;
+  if (num_splits > total_tiles) num_splits = total_tiles;
+  int tiles_per_split = (total_tiles + num_splits - 1) / num_splits;
+  num_splits = (total_tiles + tiles_per_split - 1) / tiles_per_split;
+  if (num_splits > 1) {
+    if ((r = check_ptr("o_part", o_part)) || (r = check_ptr("ml_part", ml_part))) return r;
+  }
+  if (num_splits > 65535) return fail(LBQ_ERR_ARG, "too many splits");
+  if (splits_used) *splits_used = num_splits;
+  const uint64_t bhs = uint64_t(batch) * heads;
+  CUtensorMap tq, tk, tv;
+  if ((r = make_map(&tq, q_codes, 128, q_pad, bhs, 128, uint64_t(q_pad) * 128, "q_codes"))) return r;
+  if ((r = make_map(&tk, k_codes, 128, seg_pad, bhs * num_segments, 128, uint64_t(seg_pad) * 128, "k_codes"))) return r;
+  if ((r = make_map(&tv, vt_codes, seg_pad, 128, bhs * num_segments, seg_pad, uint64_t(seg_pad) * 128, "vt_codes")))
+    return r;
+  if (sm_scale <= 0.f) sm_scale = 0.08838834764831845f;   // 128 ** -0.5
+  lbq::AttnArgs a{};
+  a.q_scale = q_scale;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.so_b = so_b;
+  a.so_l = so_l;
+  a.so_h = so_h;
+  a.o_part = o_part;
+  a.ml_part = reinterpret_cast<float2*>(ml_part);
+  a.batch = batch;
+  a.heads = heads;
+  a.q_len = q_len;
+  a.q_pad = q_pad;
+  a.kv_len = int(kv_len);
+  a.nseg = num_segments;
+  a.seg_len = seg_len;
+  a.seg_pad = seg_pad;
+  a.num_splits = num_splits;
+  a.tiles_per_split = tiles_per_split;
+  a.total_tiles = total_tiles;
+  a.sm_log2 = sm_scale * 1.4426950408889634f;
+  a.status = lbq::device_status_ptr();
+  cudaError_t e = lbq::launch_attn(a, tq, tk, tv, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "attn_fwd launch");
+}
+
+int lbq_splitkv_combine(const float* o_part, const float* ml_part, int num_splits, const float* v_scale, int batch,
+                        int heads, int q_len, void* out, int64_t so_b, int64_t so_l, int64_t so_h, void* stream) {
+  int r;
+  if ((r = check_ptr("o_part", o_part)) || (r = check_ptr("ml_part", ml_part)) || (r = check_ptr("v_scale", v_scale)))
+    return r;
+  if ((r = check_act("out", out, so_b, so_l, so_h))) return r;
+  if (num_splits < 1 || batch <= 0 || heads <= 0 || q_len <= 0)
+    return fail(LBQ_ERR_ARG, "num_splits, batch, heads and q_len must be positive");
+  lbq::CombineArgs a{o_part, reinterpret_cast<const float2*>(ml_part), v_scale, static_cast<__nv_bfloat16*>(out),
+                     so_b, so_l, so_h, batch, heads, q_len, int(round_up(q_len, 128)), num_splits};
+  cudaError_t e = lbq::launch_combine(a, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "splitkv_combine launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,167 @@
+"""Self-attention KV cache of the causal DiT — drop-in for lingbot/layers/kv_cache.py — plus the
+quantized attention over its window that replaces lingbot/layers/sage_preq.py:attend.
+
+The bookkeeping (`plan`, `evict`, `write`, `window`, `commit`) has the reference's semantics and
+host-int indices (kv_cache.py:11-88). What is new is a table of per-64-token-block statistics kept
+beside each layer's K/V (fp64 K sums and max |V| per channel, the generalisation of sage_preq's
+V min/max table, sage_preq.py:36-44,87-104): `write` refreshes the blocks it touched and `evict`
+the blocks after the sink, so `attend` re-quantizes the window with one read of the bf16 cache
+(window sums -> K/V codes) instead of two.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib, ops
+
+BLK = 64
+
+
+def _stats_tables(shape, device):
+    b, kv_size, h, d = shape
+    nb = (kv_size + BLK - 1) // BLK
+    return (torch.zeros(b, nb, h, d, dtype=torch.float64, device=device),
+            torch.zeros(b, nb, h, d, dtype=torch.float32, device=device))
+
+
+def allocate(num_layers, shape, dtype, device):
+    """One cache dict per layer; `shape` is [batch, window tokens, heads, head_dim] (kv_cache.py:11-20)."""
+    caches = []
+    for _ in range(num_layers):
+        ksum, vamax = _stats_tables(shape, device)
+        caches.append({
+            'k': torch.zeros(shape, dtype=dtype, device=device),
+            'v': torch.zeros(shape, dtype=dtype, device=device),
+            'global_end_index': torch.tensor([0], dtype=torch.long, device=device),
+            'local_end_index': torch.tensor([0], dtype=torch.long, device=device),
+            'global_end_int': 0,
+            'local_end_int': 0,
+            'lbq_ksum': ksum,
+            'lbq_vamax': vamax,
+        })
+    return caches
+
+
+def plan(kv_cache, num_new_tokens, current_start, sink_tokens, local_attn_size):
+    """Host-side bookkeeping of `write` (kv_cache.py:23-49):
+    (evicted, rolled, local_start_index, local_end_index, current_end)."""
+    current_end = current_start + num_new_tokens
+    kv_cache_size = kv_cache["k"].shape[1]
+    global_end = kv_cache.get("global_end_int")
+    if global_end is None:
+        global_end = kv_cache["global_end_index"].item()
+        local_end = kv_cache["local_end_index"].item()
+    else:
+        local_end = kv_cache["local_end_int"]
+    evicted = rolled = 0
+    if local_attn_size == -1:
+        local_end_index = current_end
+        local_start_index = current_start
+    elif (current_end > global_end) and (num_new_tokens + local_end > kv_cache_size):
+        evicted = num_new_tokens + local_end - kv_cache_size
+        rolled = local_end - evicted - sink_tokens
+        local_end_index = local_end + current_end - evicted - global_end
+        local_start_index = local_end_index - num_new_tokens
+    else:
+        local_end_index = local_end + current_end - global_end
+        local_start_index = local_end_index - num_new_tokens
+    return evicted, rolled, local_start_index, local_end_index, current_end
+
+
+def refresh_stats(kv_cache, tok_begin, tok_end):
+    """Recompute the block statistics of the blocks covering tokens [tok_begin, tok_end) of the
+    buffer (tokens past tok_end inside the last block count as absent until written)."""
+    k, v = kv_cache["k"], kv_cache["v"]
+    if "lbq_ksum" not in kv_cache:
+        kv_cache["lbq_ksum"], kv_cache["lbq_vamax"] = _stats_tables(tuple(k.shape), k.device)
+    if tok_end <= tok_begin or not k.is_cuda:
+        return
+    b, kv_size, h, _ = k.shape
+    ksum, vamax = kv_cache["lbq_ksum"], kv_cache["lbq_vamax"]
+    _lib.call("lbq_kv_block_stats", ops._ptr(k), *k.stride()[:3], ops._ptr(v), *v.stride()[:3], b, h, tok_end,
+              tok_begin // BLK, (tok_end + BLK - 1) // BLK, ksum.shape[1], ops._ptr(ksum), ops._ptr(vamax),
+              ops._stream())
+
+
+def evict(kv_cache, sink_tokens, evicted, rolled):
+    """Shift the window left past the sink to drop the oldest tokens (kv_cache.py:52-61), then
+    refresh the block statistics of everything after the sink."""
+    kv_cache["k"][:, sink_tokens:sink_tokens + rolled] = \
+        kv_cache["k"][:, sink_tokens + evicted:sink_tokens + evicted + rolled].clone()
+    kv_cache["v"][:, sink_tokens:sink_tokens + rolled] = \
+        kv_cache["v"][:, sink_tokens + evicted:sink_tokens + evicted + rolled].clone()
+    refresh_stats(kv_cache, sink_tokens, sink_tokens + rolled)
+
+
+def write(kv_cache, k, v, current_start, sink_tokens, local_attn_size):
+    """Store this forward's K/V, evicting the oldest non-sink tokens when the window is full
+    (kv_cache.py:64-75). Returns (local_end_index, current_end)."""
+    evicted, rolled, local_start_index, local_end_index, current_end = plan(
+        kv_cache, k.shape[1], current_start, sink_tokens, local_attn_size)
+    if evicted:
+        evict(kv_cache, sink_tokens, evicted, rolled)
+    kv_cache["k"][:, local_start_index:local_end_index] = k
+    kv_cache["v"][:, local_start_index:local_end_index] = v
+    refresh_stats(kv_cache, local_start_index, local_end_index)
+    return local_end_index, current_end
+
+
+def window(kv_cache, local_end_index, max_attention_size):
+    """The K/V slice this forward attends to (kv_cache.py:78-81)."""
+    start = max(0, local_end_index - max_attention_size)
+    return kv_cache["k"][:, start:local_end_index], kv_cache["v"][:, start:local_end_index]
+
+
+def commit(kv_cache, current_end, local_end_index):
+    kv_cache["global_end_int"] = current_end
+    kv_cache["local_end_int"] = local_end_index
+    kv_cache["global_end_index"].fill_(current_end)
+    kv_cache["local_end_index"].fill_(local_end_index)
+
+
+class WindowQuantizer:
+    """Reusable device buffers for re-quantizing one cache window per call (no allocation per call
+    once sized)."""
+
+    def __init__(self):
+        self.key = None
+
+    def buffers(self, batch, heads, q_len, kv_len, device):
+        key = (batch, heads, q_len, kv_len, str(device))
+        if key != self.key:
+            self.q_codes, self.q_scale = ops.alloc_q(batch, heads, q_len, device)
+            (self.k_codes, self.k_scale, self.vt_codes, self.v_scale,
+             self.km) = ops.alloc_kv(batch, heads, kv_len, 1, device)
+            self.sums = torch.empty(batch * heads * 128 * 3, dtype=torch.float32, device=device)
+            self.key = key
+        return self
+
+
+_default_quantizer = WindowQuantizer()
+
+
+def quantize_window(q, kv_cache, end, quantizer=None) -> ops.QuantWindow:
+    """Quantize q and the cache window [0, end) with the cached block statistics
+    (lbq_requant_cache + lbq_quant_q)."""
+    k, v = kv_cache["k"], kv_cache["v"]
+    ops._check_act("q", q)
+    b, lq, h, _ = q.shape
+    qz = (quantizer or _default_quantizer).buffers(b, h, lq, end, q.device)
+    st = ops._stream()
+    ksum, vamax = kv_cache["lbq_ksum"], kv_cache["lbq_vamax"]
+    _lib.call("lbq_requant_cache", ops._ptr(k), *k.stride()[:3], ops._ptr(v), *v.stride()[:3], b, h, end,
+              ksum.shape[1], ops._ptr(ksum), ops._ptr(vamax), ops._ptr(qz.sums), ops._ptr(qz.k_codes),
+              ops._ptr(qz.k_scale), ops._ptr(qz.vt_codes), ops._ptr(qz.v_scale), ops._ptr(qz.km), st)
+    _lib.call("lbq_quant_q", ops._ptr(q), *q.stride()[:3], b, h, lq, ops._ptr(qz.q_codes), ops._ptr(qz.q_scale), st)
+    return ops.QuantWindow(qz.q_codes, qz.q_scale, qz.k_codes, qz.k_scale, qz.vt_codes, qz.v_scale, qz.km, lq, end,
+                           end, 1)
+
+
+def attend(q, kv_cache, start, end, sm_scale=None, num_splits=None, out=None, quantizer=None):
+    """`sageattn(q, k_win, v_win, "NHD")` with the window [0, end) of `kv_cache`, whose tokens
+    [start, end) were written by this forward — the role of sage_preq.attend (sage_preq.py:107-128).
+    `start` is accepted for signature parity; the statistics were refreshed by `write`."""
+    w = quantize_window(q, kv_cache, end, quantizer)
+    return ops.attn_from_codes(w, sm_scale=sm_scale, out=out, num_splits=num_splits)

@@ -1,0 +1,98 @@
+"""Attention parity on the GPU against the CPU emulation of Sage's kernel (tolerance from the
+north star: cosine >= 0.9995 and max-abs <= 2e-2), reported beside an fp32 unquantized baseline."""
+import pytest
+import torch
+
+from oracle import sage_semantics as O
+from tests._gpu import k_codes_nhd, make_qkv, q_codes_nhd, v_codes_nhd
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN, MAX_ABS = 0.9995, 2e-2
+
+
+def oracle_from_window(w, rows=None, heads=None, sm_scale=None, kernel_granularity=False):
+    """Run the oracle kernel emulation on the GPU path's own codes (isolates the attention kernel).
+
+    Default: Sage's semantics (running max per 64 keys, fp16 P.V inside a tile). With
+    `kernel_granularity`, the emulation uses this kernel's own choices (running max per 128 keys,
+    fp32 P.V) and must then agree to bf16 rounding; the two emulations differ by up to ~2e-2 max-abs
+    on windows of a few dozen keys, where outputs are O(1) (the P rounding grid follows the running
+    max), and by far less on long windows."""
+    qs = w.q_scale.cpu()
+    nb = (w.kv_len + 63) // 64
+    ks = w.k_scale[0][:, :, :nb].cpu()
+    kw = dict(tile=128, pv_accum="fp32") if kernel_granularity else {}
+    return O.attn_from_codes(q_codes_nhd(w), qs, k_codes_nhd(w), ks, v_codes_nhd(w), w.v_scale.cpu(),
+                             sm_scale=sm_scale, rows=rows, heads=heads, **kw)
+
+
+SHAPES = [  # (b, h, lq, lk) — edge shapes from the reference's split-KV check (splitkv/check.py:58-63)
+    (1, 2, 300, 1000), (1, 2, 300, 65), (1, 2, 300, 64), (1, 2, 513, 4097), (2, 2, 128, 777),
+    (1, 1, 1, 1), (1, 3, 129, 129),
+]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=[f"b{b}h{h}q{q}k{k}" for b, h, q, k in SHAPES])
+@pytest.mark.parametrize("splits", [1, 3])
+def test_attention_matches_oracle(shape, splits):
+    from lingbot_b200 import _lib, ops
+    b, h, lq, lk = shape
+    q, k, v = make_qkv(11, b, h, lq, lk)
+    w = ops.quantize_qkv(q, k, v)
+    out = ops.attn_from_codes(w, num_splits=splits)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    got = out.float().cpu()
+    exact = O.compare(got, oracle_from_window(w, kernel_granularity=True))
+    assert exact["cos"] >= 0.99999 and exact["max_abs"] <= MAX_ABS, exact
+    sage = O.compare(got, oracle_from_window(w))
+    assert sage["cos"] >= COS_MIN, sage
+    fp32 = O.sdpa_fp32(q.cpu(), k.cpu(), v.cpu())
+    m32 = O.compare(out.float().cpu(), fp32)
+    assert m32["cos"] > 0.995, m32
+
+
+def test_attention_config1_rows_subset():
+    """BASELINE config 1 (q 6032 x kv 12064 x 12 heads); the oracle checks 3 heads x 384 rows."""
+    from lingbot_b200 import _lib, ops
+    q, k, v = make_qkv(0, 1, 12, 6032, 12064)
+    w = ops.quantize_qkv(q, k, v)
+    out = ops.attn_from_codes(w)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    rows = torch.cat([torch.arange(0, 128), torch.arange(2944, 3072), torch.arange(5904, 6032)])
+    heads = [0, 5, 11]
+    ref = oracle_from_window(w, rows=rows, heads=heads)
+    got = out.float().cpu()[:, rows][:, :, heads]
+    m = O.compare(got, ref[:, rows][:, :, heads])
+    assert m["cos"] >= COS_MIN and m["max_abs"] <= MAX_ABS, m
+    fp32 = O.sdpa_fp32(q.cpu(), k.cpu(), v.cpu(), rows=rows, heads=heads)[:, rows][:, :, heads]
+    assert O.compare(got, fp32)["cos"] > 0.995
+
+
+@pytest.mark.parametrize("splits", [2, 4, 7])
+def test_splits_agree(splits):
+    from lingbot_b200 import ops
+    q, k, v = make_qkv(5, 1, 4, 700, 5000)
+    w = ops.quantize_qkv(q, k, v)
+    o1 = ops.attn_from_codes(w, num_splits=1)
+    os_ = ops.attn_from_codes(w, num_splits=splits)
+    torch.cuda.synchronize()
+    m = O.compare(os_.float().cpu(), o1.float().cpu())
+    assert m["cos"] >= 0.9999 and m["max_abs"] <= 1e-2, m
+
+
+def test_drop_in_attention_signature():
+    """lingbot/layers/attention.py:27-40: same signature, NHD in/out, q dtype preserved, softmax_scale."""
+    from lingbot_b200.attention import attention
+    q, k, v = make_qkv(9, 1, 2, 256, 512)
+    o = attention(q, k, v)
+    assert o.shape == q.shape and o.dtype == q.dtype
+    o2 = attention(q, k, v, softmax_scale=0.05)
+    ref = O.sage_attention(q.cpu(), k.cpu(), v.cpu(), sm_scale=0.05)
+    m = O.compare(o2.float().cpu(), ref.float())
+    assert m["cos"] >= COS_MIN, m
+    # non-Sage branch (k_lens) goes to the paper's attention, as in the reference
+    o3 = attention(q, k, v, k_lens=torch.tensor([300]))
+    assert o3.shape == q.shape

@@ -1,0 +1,45 @@
+"""The C ABI library loads without a GPU and exports every entry point include/lbq.h declares."""
+import ctypes
+import os
+import re
+
+from lingbot_b200 import _lib
+from lingbot_b200.build import build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared():
+    src = open(os.path.join(ROOT, "include", "lbq.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(lbq_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_the_expected_entry_points():
+    names = declared()
+    for n in ("lbq_quant_qkv", "lbq_requant_cache", "lbq_attn_fwd", "lbq_splitkv_combine", "lbq_last_error"):
+        assert n in names
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    build()
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    missing = [n for n in declared() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_ctypes_signatures_cover_the_header():
+    assert sorted(_lib.SIGNATURES) == declared()
+
+
+def test_argument_validation_without_a_gpu():
+    """Host-side checks fire before any CUDA call: errors come back as codes + messages."""
+    _lib.load()
+    lib = _lib._lib
+    rc = lib.lbq_quant_q(None, 0, 0, 0, 1, 1, 1, None, None, None)
+    assert rc == 1 and b"null" in lib.lbq_last_error()
+    buf = ctypes.create_string_buffer(64)
+    mis = ctypes.c_void_p(ctypes.addressof(buf) + 1)
+    rc = lib.lbq_quant_q(mis, 0, 0, 0, 1, 1, 1, mis, mis, None)
+    assert rc == 2 and b"aligned" in lib.lbq_last_error()
+    assert lib.lbq_abi_version() == 100
