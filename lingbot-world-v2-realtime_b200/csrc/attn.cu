@@ -56,6 +56,89 @@ __device__ __forceinline__ int seg_valid(const AttnArgs& a, int seg) {
   return rest < a.seg_len ? rest : a.seg_len;
 }
 
+// Of every 16 key pairs, this many take the FMA-pipe polynomial exp2 and the rest MUFU ex2:
+// MUFU issues one exp per 8 clocks per SM sub-partition, so the split balances the two pipes.
+constexpr int kPolyPairs = 4;
+
+// Softmax of one 128-key tile for the calling thread's row. `sv` holds the int32 scores loaded from
+// tensor memory; on return `pw` holds the e4m3 P (4 keys per word, key 4w in the low byte), `m` and
+// `dsum` are updated and `alpha` = 2^(m_old - m_new) is the factor O must be rescaled by.
+// Scores are turned into floats by the magic-number add (S + 0x4B400000 is the float 1.5*2^23 + S
+// for |S| < 2^22; |S| <= 128*127*127 here), which keeps the conversion off the MUFU pipe.
+template <bool kMasked>
+__device__ __forceinline__ void softmax_tile(uint32_t (&sv)[4][32], int valid, float c1a, float c1b, float& m,
+                                             float& dsum, float& alpha, uint32_t (&pw)[32]) {
+  constexpr float kMagic = 12582912.0f;
+  if (kMasked) {
+#pragma unroll
+    for (int c = 0; c < 128; ++c)
+      if (c >= valid) sv[c >> 5][c & 31] = 0xFFC00000u;     // -2^22: never the row max
+  }
+#pragma unroll
+  for (int c = 0; c < 128; ++c) sv[c >> 5][c & 31] += 0x4B400000u;
+  auto F = [&](int c) { return __uint_as_float(sv[c >> 5][c & 31]); };
+  // row max of each 64-key half (both halves have their own K scale): 4 chains of 3-input max
+  float mh[2];
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int b0 = half * 64;
+    float r0 = F(b0 + 0), r1 = F(b0 + 1), r2 = F(b0 + 2), r3 = F(b0 + 3);
+#pragma unroll
+    for (int c = b0 + 4; c < b0 + 64; c += 8) {
+      r0 = fmax3(r0, F(c + 0), F(c + 1));
+      r1 = fmax3(r1, F(c + 2), F(c + 3));
+      r2 = fmax3(r2, F(c + 4), F(c + 5));
+      r3 = fmax3(r3, F(c + 6), F(c + 7));
+    }
+    mh[half] = fmax3(r0, r1, fmaxf(r2, r3));
+  }
+  // tile max in log2 units; (mh - magic) is the exact integer max
+  float tmax = __fmul_rn(mh[0] - kMagic, c1a);
+  // a half with no valid key must not contribute (its block scale is the 1e-7 floor, so the
+  // stand-in score would not be far enough below the real ones)
+  if (!kMasked || valid > 64) tmax = fmaxf(tmax, __fmul_rn(mh[1] - kMagic, c1b));
+  const float m_new = fmaxf(m, tmax);
+  alpha = (m == m_new) ? 1.f : ex2_approx(m - m_new);
+  m = m_new;
+  const float c0 = kFp8Offset - m_new;
+  const uint64_t nmagic = f2_pack(-kMagic, -kMagic);
+  const uint64_t c0x2 = f2_pack(c0, c0);
+  uint64_t acc0 = f2_pack(0.f, 0.f), acc1 = acc0;
+#pragma unroll
+  for (int w = 0; w < 32; ++w) {
+    uint32_t half16[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int c = 4 * w + 2 * e;
+      const float c1 = c < 64 ? c1a : c1b;
+      const uint64_t t = f2_add(f2_pack(F(c), F(c + 1)), nmagic);          // exact: the integer score
+      const uint64_t x = f2_fma(t, f2_pack(c1, c1), c0x2);                   // s - m + 8.807 (log2)
+      float x0, x1;
+      f2_unpack(x, x0, x1);
+      uint64_t p;
+      if (((c >> 1) & 15) >= 16 - kPolyPairs) {
+        p = exp2_poly_x2(x0, x1);
+      } else {
+        p = f2_pack(ex2_approx(x0), ex2_approx(x1));
+      }
+      float p0, p1;
+      f2_unpack(p, p0, p1);
+      if (kMasked) {
+        if (c >= valid) p0 = 0.f;
+        if (c + 1 >= valid) p1 = 0.f;
+        p = f2_pack(p0, p1);
+      }
+      if (e == 0) acc0 = f2_add(acc0, p); else acc1 = f2_add(acc1, p);
+      half16[e] = pack_e4m3x2(p0, p1);
+    }
+    pw[w] = half16[0] | (half16[1] << 16);
+  }
+  float s0, s1, s2, s3;
+  f2_unpack(acc0, s0, s1);
+  f2_unpack(acc1, s2, s3);
+  dsum = __fmaf_rn(dsum, alpha, (s0 + s1) + (s2 + s3));
+}
+
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const AttnArgs a) {
@@ -205,36 +288,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tmem_ld32(ts + 64, sv[2]);
       tmem_ld32(ts + 96, sv[3]);
       tmem_ld_wait();
-      int mxa = INT32_MIN, mxb = INT32_MIN;
-#pragma unroll
-      for (int c = 0; c < 64; ++c)
-        if (c < valid) mxa = max(mxa, int32_t(sv[c >> 5][c & 31]));
-#pragma unroll
-      for (int c = 64; c < 128; ++c)
-        if (c < valid) mxb = max(mxb, int32_t(sv[c >> 5][c & 31]));
-      float tmax = -INFINITY;
-      if (mxa != INT32_MIN) tmax = __fmul_rn(float(mxa), c1a);
-      if (mxb != INT32_MIN) tmax = fmaxf(tmax, __fmul_rn(float(mxb), c1b));
-      const float m_new = fmaxf(m, tmax);
-      const float alpha = (m_new == -INFINITY || m == m_new) ? 1.f : ex2_approx(m - m_new);
-      const float c0 = kFp8Offset - m_new;
-      float psum = 0.f;
       uint32_t pw[32];
-#pragma unroll
-      for (int w = 0; w < 32; ++w) {
-        float p4[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int c = 4 * w + e;
-          const float cc = c < 64 ? c1a : c1b;
-          float p = 0.f;
-          if (c < valid) p = ex2_approx(fmaf(float(int32_t(sv[c >> 5][c & 31])), cc, c0));
-          p4[e] = p;
-          psum += p;
-        }
-        pw[w] = pack_e4m3x2(p4[0], p4[1]) | (pack_e4m3x2(p4[2], p4[3]) << 16);
-      }
-      dsum = __fmaf_rn(dsum, alpha, psum);
+      float alpha;
+      if (valid == 128)
+        softmax_tile<false>(sv, 128, c1a, c1b, m, dsum, alpha, pw);
+      else
+        softmax_tile<true>(sv, valid, c1a, c1b, m, dsum, alpha, pw);
       tmem_st32(((i & 1) ? tS1 : tS0) + lane_off, pw);
       tmem_st_wait();
       if (i > 0) {
@@ -258,7 +317,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&bar->p_full);
-      m = m_new;
     }
     if (ok && mbar_wait(&bar->o_done, (n - 1) & 1, abort_flag, a.status, kDevTimeoutO)) {
       tc_fence_after();

@@ -209,6 +209,55 @@ __device__ __forceinline__ uint32_t pack_e4m3x2(float lo, float hi) {
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
   return r;
 }
+// ---- packed fp32 pairs (sm_100 f32x2 instructions: one issue slot for two lanes of work)
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair on the FMA pipe (no MUFU): x is clamped to >= -125, split as x = j + f with
+// j = round(x) (magic-number rounding) and f in [-0.5, 0.5]; 2^f is a degree-3 polynomial fitted
+// here to minimise the maximum relative error on [-0.5, 0.5] (7.5e-5, iteratively reweighted
+// least squares), and j is added to the exponent field with an integer multiply-add.
+__device__ __forceinline__ uint64_t exp2_poly_x2(float x0, float x1) {
+  constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
+  x0 = fmaxf(x0, -125.f);
+  x1 = fmaxf(x1, -125.f);
+  const uint64_t x = f2_pack(x0, x1);
+  const uint64_t t = f2_add(x, f2_pack(kMagic, kMagic));
+  const uint64_t j = f2_add(t, f2_pack(-kMagic, -kMagic));
+  const uint64_t f = f2_fma(j, f2_pack(-1.f, -1.f), x);
+  uint64_t p = f2_fma(f2_pack(5.517166853e-02f, 5.517166853e-02f), f, f2_pack(2.426111400e-01f, 2.426111400e-01f));
+  p = f2_fma(p, f, f2_pack(6.932609677e-01f, 6.932609677e-01f));
+  p = f2_fma(p, f, f2_pack(9.999280572e-01f, 9.999280572e-01f));
+  float p0, p1, t0, t1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(t, t0, t1);
+  // bits(t) << 23 == round(x) << 23 (mod 2^32): the magic's own bits shift out of the word.
+  const uint32_t r0 = __float_as_uint(t0) * 8388608u + __float_as_uint(p0);
+  const uint32_t r1 = __float_as_uint(t1) * 8388608u + __float_as_uint(p1);
+  return f2_pack(__uint_as_float(r0), __uint_as_float(r1));
+}
+
 // fp32 -> int8 code, round-half-even, saturating (cvt.rni.sat.s8.f32).
 __device__ __forceinline__ int32_t cvt_rni_sat_s8(float x) {
   int32_t r;

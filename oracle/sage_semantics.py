@@ -124,7 +124,7 @@ def quantize_qkv(q, k, v):
 
 
 def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_scale=None,
-                    tile=BLK_K, pv_accum="fp16", rows=None, heads=None):
+                    tile=BLK_K, pv_accum="fp16", rows=None, heads=None, splits=1):
     """Torch emulation of Sage's `qk_int8_sv_f8_accum_f16_fuse_v_scale_attn_inst_buf` (the call at
     sage_preq.py:126-127 / sage_kvq.py:107-110), non-causal, per-warp Q granularity.
 
@@ -138,6 +138,9 @@ def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_sca
       out    = O / d * v_scale
     Returns fp32 [B, Lq, H, D]. `rows` / `heads` restrict the computation to a subset (query rows
     are independent, so the subset equals the same rows of the full result).
+    `splits` > 1 emulates split-KV (splitkv/README.md:36-69): the key tiles are cut into `splits`
+    contiguous ranges (ceil division, empty ranges dropped), each runs the loop above from a fresh
+    running max, and the partials merge as out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) d_s.
     """
     b, lq, h, d = q_codes.shape
     lk = k_codes.shape[1]
@@ -149,38 +152,55 @@ def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_sca
     out = torch.zeros(b, lq, h, d, dtype=torch.float32)
     vq_all = e4m3_to_float(v_codes)                                    # [B, Lk, H, D]
     off = torch.tensor(S_FP8_OFFSET, dtype=torch.float32)
+    ntiles = (lk + tile - 1) // tile
+    per = (ntiles + splits - 1) // splits
+    ranges = [(s0 * tile, min(lk, (s0 + per) * tile)) for s0 in range(0, ntiles, per)]
     for bi in range(b):
         for hi in heads:
             qf = q_codes[bi, rows, hi].float()                          # [R, D]
             qs = q_scale[bi, hi][rows // WARP_Q]                         # [R]
             kf = k_codes[bi, :, hi].float()                             # [Lk, D]
             vf = vq_all[bi, :, hi]                                       # [Lk, D]
-            r = qf.shape[0]
-            m = torch.full((r,), -math.inf)
-            dsum = torch.zeros(r)
-            acc = torch.zeros(r, d)
-            for t0 in range(0, lk, tile):
-                t1 = min(t0 + tile, lk)
-                s_int = qf @ kf[t0:t1].T                                 # exact integers
-                ks = k_scale[bi, hi][torch.arange(t0, t1) // BLK_K]      # [T]
-                s = s_int * (qs[:, None] * ks[None, :])                  # dequantized, fp32
-                m_new = torch.maximum(m, s.max(dim=1).values)
-                alpha = torch.exp2((m - m_new) * sm_log2)
-                p = torch.exp2((s - m_new[:, None]) * sm_log2 + off)
-                dsum = dsum * alpha + p.sum(dim=1)
-                pq = e4m3_to_float(e4m3_rn_satfinite(p))
-                if pv_accum == "fp16":
-                    tile_acc = torch.zeros(r, d)
-                    for c0 in range(0, t1 - t0, 32):                     # m16n8k32 steps
-                        c1 = min(c0 + 32, t1 - t0)
-                        tile_acc = (tile_acc + pq[:, c0:c1] @ vf[t0 + c0:t0 + c1]).half().float()
-                else:
-                    tile_acc = pq @ vf[t0:t1]
-                acc = acc * alpha[:, None] + tile_acc
-                m = m_new
+            parts = [_attn_range(qf, qs, kf, vf, k_scale[bi, hi], lo, hi_, tile, pv_accum, sm_log2, off)
+                     for lo, hi_ in ranges]
+            mx = torch.stack([p[0] for p in parts]).max(dim=0).values
+            acc = torch.zeros(qf.shape[0], d)
+            dsum = torch.zeros(qf.shape[0])
+            for m_s, d_s, o_s in parts:
+                w = torch.exp2((m_s - mx) * sm_log2)
+                acc += w[:, None] * o_s
+                dsum += w * d_s
             o = acc * (1.0 / dsum)[:, None] * v_scale[bi, hi][None, :]
             out[bi, rows, hi] = o
     return out
+
+
+def _attn_range(qf, qs, kf, vf, ks_all, lo, hi, tile, pv_accum, sm_log2, off):
+    """The kernel loop over keys [lo, hi): returns (running max m, row sum d, unnormalized O)."""
+    r, d = qf.shape[0], vf.shape[1]
+    m = torch.full((r,), -math.inf)
+    dsum = torch.zeros(r)
+    acc = torch.zeros(r, d)
+    for t0 in range(lo, hi, tile):
+        t1 = min(t0 + tile, hi)
+        s_int = qf @ kf[t0:t1].T                                 # exact integers
+        ks = ks_all[torch.arange(t0, t1) // BLK_K]               # [T]
+        s = s_int * (qs[:, None] * ks[None, :])                  # dequantized, fp32
+        m_new = torch.maximum(m, s.max(dim=1).values)
+        alpha = torch.exp2((m - m_new) * sm_log2)
+        p = torch.exp2((s - m_new[:, None]) * sm_log2 + off)
+        dsum = dsum * alpha + p.sum(dim=1)
+        pq = e4m3_to_float(e4m3_rn_satfinite(p))
+        if pv_accum == "fp16":
+            tile_acc = torch.zeros(r, d)
+            for c0 in range(0, t1 - t0, 32):                     # m16n8k32 steps
+                c1 = min(c0 + 32, t1 - t0)
+                tile_acc = (tile_acc + pq[:, c0:c1] @ vf[t0 + c0:t0 + c1]).half().float()
+        else:
+            tile_acc = pq @ vf[t0:t1]
+        acc = acc * alpha[:, None] + tile_acc
+        m = m_new
+    return m, dsum, acc
 
 
 def sage_attention(q, k, v, sm_scale=None, **kw):
@@ -209,7 +229,7 @@ def sdpa_fp32(q, k, v, sm_scale=None, rows=None, heads=None):
 
 def compare(a: torch.Tensor, b: torch.Tensor) -> dict:
     """Error metrics used throughout (splitkv/check.py:48-56)."""
-    a, b = a.float().flatten(), b.float().flatten()
+    a, b = a.double().flatten(), b.double().flatten()
     dlt = (a - b).abs()
     return dict(cos=F.cosine_similarity(a, b, dim=0).item(), max_abs=dlt.max().item(),
                 rel_l2=((a - b).norm() / b.norm()).item())
