@@ -13,13 +13,16 @@
 //   out = O / d * v_scale  -> bf16
 // Differences from the sm89 kernel (covered by the tolerance tests): the running max is updated
 // per 128 keys instead of 64, P.V accumulates in fp32 rather than fp16 inside a tile, and exp2 is
-// the ex2.approx instruction on an fma of the dequantized score.
+// the ex2.approx instruction for 3/4 of the keys and an FMA-pipe polynomial (relative error
+// < 7.5e-5) for the rest.
 //
 // CTA = one 128-row Q tile x one (batch, head) x one KV split. Warps: 0 = TMA producer,
-// 1 = tcgen05 issuer (one thread), 2..5 = softmax / correction / epilogue; softmax thread i owns
-// Q row i of the tile, which is TMEM lane i.
-// Tensor memory (512 columns): S0 [0,128), S1 [128,256) as int32 scores; the first 32 columns of
-// each S buffer are overwritten by that tile's e4m3 P (4 per column); O f32 [256,384).
+// 1 = tcgen05 issuer (one thread), 2..9 = two softmax warpgroups. Q row r of the tile is TMEM lane
+// r; warpgroup g handles keys [64g, 64g+64) of every 128-key tile (one K scale block) and columns
+// [64g, 64g+64) of O. The two threads of a row exchange their partial row max through shared
+// memory each tile.
+// Tensor memory (512 columns): S0 [0,128), S1 [128,256) as int32 scores; columns [0,32) of each S
+// buffer are overwritten by that tile's e4m3 P (4 keys per column); O f32 [256,384).
 #include <cuda_bf16.h>
 #include <cstdint>
 
@@ -30,10 +33,12 @@ namespace lbq {
 
 constexpr int kStages = 4;
 constexpr int kTile = 128 * 128;         // bytes of one 128 x 128 8-bit tile
-constexpr int kAttnThreads = 192;
+constexpr int kSoftmaxWGs = 2;
+constexpr int kAttnThreads = 64 + 128 * kSoftmaxWGs;
 constexpr float kFp8Offset = 8.807f;     // splitkv/README.md:58 (S_FP8_OFFSET)
+constexpr float kMagic = 12582912.0f;    // 1.5 * 2^23
 
-struct AttnBarriers {
+struct AttnShared {
   uint64_t q_full;
   uint64_t k_full[kStages];
   uint64_t k_empty[kStages];
@@ -43,11 +48,13 @@ struct AttnBarriers {
   uint64_t p_full;
   uint64_t o_done;
   uint64_t drain;
+  uint64_t xchg_bar[4][2];               // per TMEM lane quarter, per tile parity: 64 arrivals
   uint32_t tmem_base;
   int abort;
+  float xchg[2][kSoftmaxWGs][128];       // partial row max (tile parity, warpgroup, row); then d
 };
 
-constexpr size_t kAttnSmemBytes = 1024 /*alignment slack*/ + kTile * (1 + 2 * kStages) + sizeof(AttnBarriers);
+constexpr size_t kAttnSmemBytes = 1024 /*alignment slack*/ + kTile * (1 + 2 * kStages) + sizeof(AttnShared);
 
 __device__ int g_status;
 
@@ -60,59 +67,52 @@ __device__ __forceinline__ int seg_valid(const AttnArgs& a, int seg) {
 // MUFU issues one exp per 8 clocks per SM sub-partition, so the split balances the two pipes.
 constexpr int kPolyPairs = 4;
 
-// Softmax of one 128-key tile for the calling thread's row. `sv` holds the int32 scores loaded from
-// tensor memory; on return `pw` holds the e4m3 P (4 keys per word, key 4w in the low byte), `m` and
-// `dsum` are updated and `alpha` = 2^(m_old - m_new) is the factor O must be rescaled by.
-// Scores are turned into floats by the magic-number add (S + 0x4B400000 is the float 1.5*2^23 + S
-// for |S| < 2^22; |S| <= 128*127*127 here), which keeps the conversion off the MUFU pipe.
+// Scores -> floats by the magic-number add (S + 0x4B400000 is the float 1.5*2^23 + S for
+// |S| < 2^22, and |S| <= 128*127*127 here), which keeps the conversion off the MUFU pipe; masked
+// keys become -2^22. Returns the partial row max over this thread's 64 keys in log2 units, or
+// -inf when none of them is valid.
 template <bool kMasked>
-__device__ __forceinline__ void softmax_tile(uint32_t (&sv)[4][32], int valid, float c1a, float c1b, float& m,
-                                             float& dsum, float& alpha, uint32_t (&pw)[32]) {
-  constexpr float kMagic = 12582912.0f;
+__device__ __forceinline__ float softmax_convert_max(uint32_t (&sv)[2][32], int valid, float c1) {
   if (kMasked) {
 #pragma unroll
-    for (int c = 0; c < 128; ++c)
-      if (c >= valid) sv[c >> 5][c & 31] = 0xFFC00000u;     // -2^22: never the row max
+    for (int c = 0; c < 64; ++c)
+      if (c >= valid) sv[c >> 5][c & 31] = 0xFFC00000u;
   }
 #pragma unroll
-  for (int c = 0; c < 128; ++c) sv[c >> 5][c & 31] += 0x4B400000u;
+  for (int c = 0; c < 64; ++c) sv[c >> 5][c & 31] += 0x4B400000u;
   auto F = [&](int c) { return __uint_as_float(sv[c >> 5][c & 31]); };
-  // row max of each 64-key half (both halves have their own K scale): 4 chains of 3-input max
-  float mh[2];
+  float r0 = fmaxf(F(0), F(1)), r1 = fmaxf(F(2), F(3)), r2 = fmaxf(F(4), F(5)), r3 = fmaxf(F(6), F(7));
 #pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    const int b0 = half * 64;
-    float r0 = F(b0 + 0), r1 = F(b0 + 1), r2 = F(b0 + 2), r3 = F(b0 + 3);
-#pragma unroll
-    for (int c = b0 + 4; c < b0 + 64; c += 8) {
-      r0 = fmax3(r0, F(c + 0), F(c + 1));
-      r1 = fmax3(r1, F(c + 2), F(c + 3));
-      r2 = fmax3(r2, F(c + 4), F(c + 5));
-      r3 = fmax3(r3, F(c + 6), F(c + 7));
-    }
-    mh[half] = fmax3(r0, r1, fmaxf(r2, r3));
+  for (int c = 8; c < 64; c += 8) {
+    r0 = fmax3(r0, F(c + 0), F(c + 1));
+    r1 = fmax3(r1, F(c + 2), F(c + 3));
+    r2 = fmax3(r2, F(c + 4), F(c + 5));
+    r3 = fmax3(r3, F(c + 6), F(c + 7));
   }
-  // tile max in log2 units; (mh - magic) is the exact integer max
-  float tmax = __fmul_rn(mh[0] - kMagic, c1a);
-  // a half with no valid key must not contribute (its block scale is the 1e-7 floor, so the
-  // stand-in score would not be far enough below the real ones)
-  if (!kMasked || valid > 64) tmax = fmaxf(tmax, __fmul_rn(mh[1] - kMagic, c1b));
-  const float m_new = fmaxf(m, tmax);
-  alpha = (m == m_new) ? 1.f : ex2_approx(m - m_new);
-  m = m_new;
-  const float c0 = kFp8Offset - m_new;
+  const float mh = fmax3(r0, r1, fmaxf(r2, r3));
+  if (kMasked && valid <= 0) return -INFINITY;
+  return __fmul_rn(mh - kMagic, c1);          // (mh - magic) is the exact integer max
+}
+
+// P = 2^(s*c1 + 8.807 - m) for this thread's 64 keys -> e4m3 words in `pw` (key 4w in the low
+// byte); returns the fp32 sum of P (masked keys contribute 0).
+template <bool kMasked>
+__device__ __forceinline__ float softmax_exp_pack(const uint32_t (&sv)[2][32], int valid, float c1, float m,
+                                                  uint32_t (&pw)[16]) {
+  auto F = [&](int c) { return __uint_as_float(sv[c >> 5][c & 31]); };
+  const float c0 = kFp8Offset - m;
   const uint64_t nmagic = f2_pack(-kMagic, -kMagic);
   const uint64_t c0x2 = f2_pack(c0, c0);
+  const uint64_t c1x2 = f2_pack(c1, c1);
   uint64_t acc0 = f2_pack(0.f, 0.f), acc1 = acc0;
 #pragma unroll
-  for (int w = 0; w < 32; ++w) {
+  for (int w = 0; w < 16; ++w) {
     uint32_t half16[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int c = 4 * w + 2 * e;
-      const float c1 = c < 64 ? c1a : c1b;
-      const uint64_t t = f2_add(f2_pack(F(c), F(c + 1)), nmagic);          // exact: the integer score
-      const uint64_t x = f2_fma(t, f2_pack(c1, c1), c0x2);                   // s - m + 8.807 (log2)
+      const uint64_t t = f2_add(f2_pack(F(c), F(c + 1)), nmagic);   // exact: the integer score
+      const uint64_t x = f2_fma(t, c1x2, c0x2);                      // s - m + 8.807 (log2)
       float x0, x1;
       f2_unpack(x, x0, x1);
       uint64_t p;
@@ -136,7 +136,7 @@ __device__ __forceinline__ void softmax_tile(uint32_t (&sv)[4][32], int valid, f
   float s0, s1, s2, s3;
   f2_unpack(acc0, s0, s1);
   f2_unpack(acc1, s2, s3);
-  dsum = __fmaf_rn(dsum, alpha, (s0 + s1) + (s2 + s3));
+  return (s0 + s1) + (s2 + s3);
 }
 
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -147,8 +147,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sQ = smem;
   uint8_t* sK = smem + kTile;
   uint8_t* sV = smem + kTile * (1 + kStages);
-  AttnBarriers* bar = reinterpret_cast<AttnBarriers*>(smem + kTile * (1 + 2 * kStages));
-  volatile int* abort_flag = &bar->abort;
+  AttnShared* sh = reinterpret_cast<AttnShared*>(smem + kTile * (1 + 2 * kStages));
+  volatile int* abort_flag = &sh->abort;
 
   const int qt = blockIdx.x, bh = blockIdx.y, split = blockIdx.z;
   const int b = bh / a.heads, h = bh - b * a.heads;
@@ -160,29 +160,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bar->q_full, 1);
+    mbar_init(&sh->q_full, 1);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bar->k_full[s], 1);
-      mbar_init(&bar->k_empty[s], 1);
-      mbar_init(&bar->v_full[s], 1);
-      mbar_init(&bar->v_empty[s], 1);
+      mbar_init(&sh->k_full[s], 1);
+      mbar_init(&sh->k_empty[s], 1);
+      mbar_init(&sh->v_full[s], 1);
+      mbar_init(&sh->v_empty[s], 1);
     }
-    mbar_init(&bar->s_full[0], 1);
-    mbar_init(&bar->s_full[1], 1);
-    mbar_init(&bar->p_full, 128);
-    mbar_init(&bar->o_done, 1);
-    mbar_init(&bar->drain, 1);
-    bar->abort = 0;
+    mbar_init(&sh->s_full[0], 1);
+    mbar_init(&sh->s_full[1], 1);
+    mbar_init(&sh->p_full, 128 * kSoftmaxWGs);
+    mbar_init(&sh->o_done, 1);
+    mbar_init(&sh->drain, 1);
+    for (int q = 0; q < 4; ++q) {
+      mbar_init(&sh->xchg_bar[q][0], 32 * kSoftmaxWGs);
+      mbar_init(&sh->xchg_bar[q][1], 32 * kSoftmaxWGs);
+    }
+    sh->abort = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(&bar->tmem_base, 512);
+    tmem_alloc(&sh->tmem_base, 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = bar->tmem_base;
+  const uint32_t tmem = sh->tmem_base;
   const uint32_t tS0 = tmem, tS1 = tmem + 128, tO = tmem + 256;
 
   if (warp == 0) {
@@ -191,23 +195,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(&bar->q_full, kTile);
-      tma_load_3d(sQ, &tm_q, &bar->q_full, 0, qt * 128, bh);
+      mbar_arrive_expect_tx(&sh->q_full, kTile);
+      tma_load_3d(sQ, &tm_q, &sh->q_full, 0, qt * 128, bh);
       int issued = 0;
       for (int i = 0; i < n; ++i) {
         const int jt = t_begin + i;
         const int seg = jt / tiles_per_seg, lt = jt - seg * tiles_per_seg;
         const int s = i % kStages;
         const uint32_t ph = (i / kStages) & 1;
-        if (!mbar_wait(&bar->k_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) break;
-        mbar_arrive_expect_tx(&bar->k_full[s], kTile);
-        tma_load_3d(sK + s * kTile, &tm_k, &bar->k_full[s], 0, lt * 128, seg * bhs + bh);
-        if (!mbar_wait(&bar->v_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) {
+        if (!mbar_wait(&sh->k_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) break;
+        mbar_arrive_expect_tx(&sh->k_full[s], kTile);
+        tma_load_3d(sK + s * kTile, &tm_k, &sh->k_full[s], 0, lt * 128, seg * bhs + bh);
+        if (!mbar_wait(&sh->v_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) {
           issued = i + 1;
           break;
         }
-        mbar_arrive_expect_tx(&bar->v_full[s], kTile);
-        tma_load_3d(sV + s * kTile, &tm_v, &bar->v_full[s], lt * 128, 0, seg * bhs + bh);
+        mbar_arrive_expect_tx(&sh->v_full[s], kTile);
+        tma_load_3d(sV + s * kTile, &tm_v, &sh->v_full[s], lt * 128, 0, seg * bhs + bh);
         issued = i + 1;
       }
       if (*abort_flag) {
@@ -215,34 +219,34 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int i = (issued > kStages ? issued - kStages : 0); i < issued; ++i) {
           const int s = i % kStages;
           const uint32_t ph = (i / kStages) & 1;
-          mbar_drain_wait(&bar->k_full[s], ph);
-          mbar_drain_wait(&bar->v_full[s], ph);
+          mbar_drain_wait(&sh->k_full[s], ph);
+          mbar_drain_wait(&sh->v_full[s], ph);
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ tcgen05 issuer
     if (lane == 0 && n > 0) {
-      bool ok = mbar_wait(&bar->q_full, 0, abort_flag, a.status, kDevTimeoutQ);
+      bool ok = mbar_wait(&sh->q_full, 0, abort_flag, a.status, kDevTimeoutQ);
       tc_fence_after();
       const uint64_t qdesc = smem_desc_sw128(smem_u32(sQ));
       auto issue_pv = [&](int j) -> bool {
-        if (!mbar_wait(&bar->p_full, j & 1, abort_flag, a.status, kDevTimeoutP)) return false;
+        if (!mbar_wait(&sh->p_full, j & 1, abort_flag, a.status, kDevTimeoutP)) return false;
         const int s = j % kStages;
-        if (!mbar_wait(&bar->v_full[s], (j / kStages) & 1, abort_flag, a.status, kDevTimeoutKV)) return false;
+        if (!mbar_wait(&sh->v_full[s], (j / kStages) & 1, abort_flag, a.status, kDevTimeoutKV)) return false;
         tc_fence_after();
         const uint64_t vdesc = smem_desc_sw128(smem_u32(sV + s * kTile));
         const uint32_t tp = (j & 1) ? tS1 : tS0;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           mma_f8_ts(tO, tp + 8 * kk, vdesc + 2 * kk, kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&bar->v_empty[s]);
-        tc_commit(&bar->o_done);
+        tc_commit(&sh->v_empty[s]);
+        tc_commit(&sh->o_done);
         return true;
       };
       for (int i = 0; ok && i < n; ++i) {
         const int s = i % kStages;
-        if (!mbar_wait(&bar->k_full[s], (i / kStages) & 1, abort_flag, a.status, kDevTimeoutKV)) {
+        if (!mbar_wait(&sh->k_full[s], (i / kStages) & 1, abort_flag, a.status, kDevTimeoutKV)) {
           ok = false;
           break;
         }
@@ -251,20 +255,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t ts = (i & 1) ? tS1 : tS0;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) mma_i8_ss(ts, qdesc + 2 * kk, kdesc + 2 * kk, kIdescQK, kk > 0 ? 1u : 0u);
-        tc_commit(&bar->s_full[i & 1]);
-        tc_commit(&bar->k_empty[s]);
+        tc_commit(&sh->s_full[i & 1]);
+        tc_commit(&sh->k_empty[s]);
         if (i > 0) ok = issue_pv(i - 1);
       }
       if (ok) issue_pv(n - 1);
       // Drain: every MMA issued above has completed once `drain` flips.
-      tc_commit(&bar->drain);
-      mbar_drain_wait(&bar->drain, 0);
+      tc_commit(&sh->drain);
+      mbar_drain_wait(&sh->drain, 0);
     }
   } else {
-    // ------------------------------------------------------------ softmax warpgroup
+    // ------------------------------------------------------------ softmax warpgroups
+    const int wg = (warp - 2) >> 2;                     // key half / O column half
     const int quarter = warp & 3;                       // TMEM lanes [32*quarter, 32*quarter+32)
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
-    const int row = qt * 128 + quarter * 32 + lane;
+    const int trow = quarter * 32 + lane;               // row inside the Q tile
+    const int row = qt * 128 + trow;
+    const int col0 = wg * 64;
     const float qs = a.q_scale[int64_t(bh) * (a.q_pad / 32) + qt * 4 + quarter];
     const int kspb = a.seg_pad / 64;
     float m = -INFINITY, dsum = 0.f;
@@ -272,93 +279,108 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int i = 0; ok && i < n; ++i) {
       const int jt = t_begin + i;
       const int seg = jt / tiles_per_seg, lt = jt - seg * tiles_per_seg;
-      const int valid = min(128, seg_valid(a, seg) - lt * 128);
-      const float* ksp = a.k_scale + int64_t(seg * bhs + bh) * kspb + lt * 2;
-      const float c1a = __fmul_rn(__fmul_rn(qs, ksp[0]), a.sm_log2);
-      const float c1b = __fmul_rn(__fmul_rn(qs, ksp[1]), a.sm_log2);
-      if (!mbar_wait(&bar->s_full[i & 1], (i >> 1) & 1, abort_flag, a.status, kDevTimeoutS)) {
+      const int valid = min(128, seg_valid(a, seg) - lt * 128) - col0;   // keys of my half
+      const float c1 = __fmul_rn(__fmul_rn(qs, a.k_scale[int64_t(seg * bhs + bh) * kspb + lt * 2 + wg]), a.sm_log2);
+      if (!mbar_wait(&sh->s_full[i & 1], (i >> 1) & 1, abort_flag, a.status, kDevTimeoutS)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const uint32_t ts = ((i & 1) ? tS1 : tS0) + lane_off;
-      uint32_t sv[4][32];
-      tmem_ld32(ts + 0, sv[0]);
-      tmem_ld32(ts + 32, sv[1]);
-      tmem_ld32(ts + 64, sv[2]);
-      tmem_ld32(ts + 96, sv[3]);
+      uint32_t sv[2][32];
+      tmem_ld32(ts + col0, sv[0]);
+      tmem_ld32(ts + col0 + 32, sv[1]);
       tmem_ld_wait();
-      uint32_t pw[32];
-      float alpha;
-      if (valid == 128)
-        softmax_tile<false>(sv, 128, c1a, c1b, m, dsum, alpha, pw);
-      else
-        softmax_tile<true>(sv, valid, c1a, c1b, m, dsum, alpha, pw);
-      tmem_st32(((i & 1) ? tS1 : tS0) + lane_off, pw);
+      const bool masked = valid < 64;
+      const float tmax = masked ? softmax_convert_max<true>(sv, valid, c1) : softmax_convert_max<false>(sv, 64, c1);
+      // exchange the partial row max with the other warpgroup's thread of this row
+      sh->xchg[i & 1][wg][trow] = tmax;
+      mbar_arrive(&sh->xchg_bar[quarter][i & 1]);
+      if (!mbar_wait(&sh->xchg_bar[quarter][i & 1], (i >> 1) & 1, abort_flag, a.status, kDevTimeoutS)) {
+        ok = false;
+        break;
+      }
+      const float other = sh->xchg[i & 1][wg ^ 1][trow];
+      const float m_new = fmax3(m, tmax, other);
+      const float alpha = (m == m_new) ? 1.f : ex2_approx(m - m_new);
+      m = m_new;
+      uint32_t pw[16];
+      const float psum = masked ? softmax_exp_pack<true>(sv, valid, c1, m, pw) : softmax_exp_pack<false>(sv, 64, c1, m, pw);
+      dsum = __fmaf_rn(dsum, alpha, psum);
+      tmem_st16(((i & 1) ? tS1 : tS0) + lane_off + wg * 16, pw);
       tmem_st_wait();
       if (i > 0) {
-        if (!mbar_wait(&bar->o_done, (i - 1) & 1, abort_flag, a.status, kDevTimeoutO)) {
+        if (!mbar_wait(&sh->o_done, (i - 1) & 1, abort_flag, a.status, kDevTimeoutO)) {
           ok = false;
           break;
         }
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 2; ++c) {
             uint32_t ov[32];
-            tmem_ld32(tO + lane_off + 32 * c, ov);
+            const uint32_t ta = tO + lane_off + col0 + 32 * c;
+            tmem_ld32(ta, ov);
             tmem_ld_wait();
 #pragma unroll
             for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-            tmem_st32(tO + lane_off + 32 * c, ov);
+            tmem_st32(ta, ov);
           }
           tmem_st_wait();
         }
       }
       tc_fence_before();
-      mbar_arrive(&bar->p_full);
+      mbar_arrive(&sh->p_full);
     }
-    if (ok && mbar_wait(&bar->o_done, (n - 1) & 1, abort_flag, a.status, kDevTimeoutO)) {
+    if (ok && mbar_wait(&sh->o_done, (n - 1) & 1, abort_flag, a.status, kDevTimeoutO)) {
       tc_fence_after();
-      if (a.num_splits == 1) {
-        const float rd = __frcp_rn(dsum);
-        const float* vs = a.v_scale + int64_t(bh) * 128;
-        __nv_bfloat16* dst = a.out + b * a.so_b + int64_t(row) * a.so_l + h * a.so_h;
+      // row sum = the two warpgroups' partial sums (same order in both threads)
+      const int par = n & 1;
+      sh->xchg[par][wg][trow] = dsum;
+      mbar_arrive(&sh->xchg_bar[quarter][par]);
+      if (mbar_wait(&sh->xchg_bar[quarter][par], (n >> 1) & 1, abort_flag, a.status, kDevTimeoutS)) {
+        const float dtot = sh->xchg[par][0][trow] + sh->xchg[par][1][trow];
+        if (a.num_splits == 1) {
+          const float rd = __frcp_rn(dtot);
+          const float* vs = a.v_scale + int64_t(bh) * 128 + col0;
+          __nv_bfloat16* dst = a.out + b * a.so_b + int64_t(row) * a.so_l + h * a.so_h + col0;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t ov[32];
-          tmem_ld32(tO + lane_off + 32 * c, ov);
-          tmem_ld_wait();
-          uint32_t packed[16];
+          for (int c = 0; c < 2; ++c) {
+            uint32_t ov[32];
+            tmem_ld32(tO + lane_off + col0 + 32 * c, ov);
+            tmem_ld_wait();
+            uint32_t packed[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float o0 = __fmul_rn(__fmul_rn(__uint_as_float(ov[2 * e]), rd), vs[32 * c + 2 * e]);
-            const float o1 = __fmul_rn(__fmul_rn(__uint_as_float(ov[2 * e + 1]), rd), vs[32 * c + 2 * e + 1]);
-            const __nv_bfloat162 pr = __floats2bfloat162_rn(o0, o1);
-            packed[e] = *reinterpret_cast<const uint32_t*>(&pr);
-          }
-          if (row < a.q_len) {
+            for (int e = 0; e < 16; ++e) {
+              const float o0 = __fmul_rn(__fmul_rn(__uint_as_float(ov[2 * e]), rd), vs[32 * c + 2 * e]);
+              const float o1 = __fmul_rn(__fmul_rn(__uint_as_float(ov[2 * e + 1]), rd), vs[32 * c + 2 * e + 1]);
+              const __nv_bfloat162 pr = __floats2bfloat162_rn(o0, o1);
+              packed[e] = *reinterpret_cast<const uint32_t*>(&pr);
+            }
+            if (row < a.q_len) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              reinterpret_cast<uint4*>(dst + 32 * c)[e] =
-                  make_uint4(packed[4 * e], packed[4 * e + 1], packed[4 * e + 2], packed[4 * e + 3]);
+              for (int e = 0; e < 4; ++e)
+                reinterpret_cast<uint4*>(dst + 32 * c)[e] =
+                    make_uint4(packed[4 * e], packed[4 * e + 1], packed[4 * e + 2], packed[4 * e + 3]);
+            }
           }
-        }
-      } else {
-        const int64_t prow = (int64_t(split) * bhs + bh) * a.q_pad + row;
-        float* dst = a.o_part + prow * 128;
+        } else {
+          const int64_t prow = (int64_t(split) * bhs + bh) * a.q_pad + row;
+          float* dst = a.o_part + prow * 128 + col0;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t ov[32];
-          tmem_ld32(tO + lane_off + 32 * c, ov);
-          tmem_ld_wait();
-          if (row < a.q_len) {
+          for (int c = 0; c < 2; ++c) {
+            uint32_t ov[32];
+            tmem_ld32(tO + lane_off + col0 + 32 * c, ov);
+            tmem_ld_wait();
+            if (row < a.q_len) {
 #pragma unroll
-            for (int e = 0; e < 8; ++e)
-              reinterpret_cast<uint4*>(dst + 32 * c)[e] = make_uint4(ov[4 * e], ov[4 * e + 1], ov[4 * e + 2], ov[4 * e + 3]);
+              for (int e = 0; e < 8; ++e)
+                reinterpret_cast<uint4*>(dst + 32 * c)[e] =
+                    make_uint4(ov[4 * e], ov[4 * e + 1], ov[4 * e + 2], ov[4 * e + 3]);
+            }
           }
+          if (wg == 0 && row < a.q_len) a.ml_part[prow] = make_float2(m, dtot);
         }
-        if (row < a.q_len) a.ml_part[prow] = make_float2(m, dsum);
       }
     }
   }
