@@ -17,10 +17,10 @@
 // < 7.5e-5) for the rest.
 //
 // CTA = one 128-row Q tile x one (batch, head) x one KV split. Warps: 0 = TMA producer,
-// 1 = tcgen05 issuer (one thread), 2..9 = two softmax warpgroups. Q row r of the tile is TMEM lane
-// r; warpgroup g handles keys [64g, 64g+64) of every 128-key tile (one K scale block) and columns
-// [64g, 64g+64) of O. The two threads of a row exchange their partial row max through shared
-// memory each tile.
+// 1 = tcgen05 issuer (one thread), 2.. = kSoftmaxWGs softmax warpgroups. Q row r of the tile is
+// TMEM lane r; warpgroup g handles keys [g*kKeys, (g+1)*kKeys) of every 128-key tile (inside one
+// K scale block) and the same columns of O. The threads of a row exchange their partial row maxima
+// through shared memory each tile.
 // Tensor memory (512 columns): S0 [0,128), S1 [128,256) as int32 scores; columns [0,32) of each S
 // buffer are overwritten by that tile's e4m3 P (4 keys per column); O f32 [256,384).
 #include <cuda_bf16.h>
@@ -33,7 +33,12 @@ namespace lbq {
 
 constexpr int kStages = 4;
 constexpr int kTile = 128 * 128;         // bytes of one 128 x 128 8-bit tile
-constexpr int kSoftmaxWGs = 2;
+#ifndef LBQ_SOFTMAX_WGS
+#define LBQ_SOFTMAX_WGS 2
+#endif
+constexpr int kSoftmaxWGs = LBQ_SOFTMAX_WGS;   // 2 or 4 warpgroups share each 128-key tile
+constexpr int kKeys = 128 / kSoftmaxWGs;       // keys (and O columns) per softmax thread
+constexpr int kChunks = kKeys / 32;
 constexpr int kAttnThreads = 64 + 128 * kSoftmaxWGs;
 constexpr float kFp8Offset = 8.807f;     // splitkv/README.md:58 (S_FP8_OFFSET)
 constexpr float kMagic = 12582912.0f;    // 1.5 * 2^23
@@ -65,25 +70,28 @@ __device__ __forceinline__ int seg_valid(const AttnArgs& a, int seg) {
 
 // Of every 16 key pairs, this many take the FMA-pipe polynomial exp2 and the rest MUFU ex2:
 // MUFU issues one exp per 8 clocks per SM sub-partition, so the split balances the two pipes.
-constexpr int kPolyPairs = 4;
+#ifndef LBQ_POLY_PAIRS
+#define LBQ_POLY_PAIRS 4
+#endif
+constexpr int kPolyPairs = LBQ_POLY_PAIRS;
 
 // Scores -> floats by the magic-number add (S + 0x4B400000 is the float 1.5*2^23 + S for
 // |S| < 2^22, and |S| <= 128*127*127 here), which keeps the conversion off the MUFU pipe; masked
-// keys become -2^22. Returns the partial row max over this thread's 64 keys in log2 units, or
-// -inf when none of them is valid.
+// keys become -2^22. Returns the partial row max over this thread's keys in log2 units, or -inf
+// when none of them is valid.
 template <bool kMasked>
-__device__ __forceinline__ float softmax_convert_max(uint32_t (&sv)[2][32], int valid, float c1) {
+__device__ __forceinline__ float softmax_convert_max(uint32_t (&sv)[kChunks][32], int valid, float c1) {
   if (kMasked) {
 #pragma unroll
-    for (int c = 0; c < 64; ++c)
+    for (int c = 0; c < kKeys; ++c)
       if (c >= valid) sv[c >> 5][c & 31] = 0xFFC00000u;
   }
 #pragma unroll
-  for (int c = 0; c < 64; ++c) sv[c >> 5][c & 31] += 0x4B400000u;
+  for (int c = 0; c < kKeys; ++c) sv[c >> 5][c & 31] += 0x4B400000u;
   auto F = [&](int c) { return __uint_as_float(sv[c >> 5][c & 31]); };
   float r0 = fmaxf(F(0), F(1)), r1 = fmaxf(F(2), F(3)), r2 = fmaxf(F(4), F(5)), r3 = fmaxf(F(6), F(7));
 #pragma unroll
-  for (int c = 8; c < 64; c += 8) {
+  for (int c = 8; c < kKeys; c += 8) {
     r0 = fmax3(r0, F(c + 0), F(c + 1));
     r1 = fmax3(r1, F(c + 2), F(c + 3));
     r2 = fmax3(r2, F(c + 4), F(c + 5));
@@ -94,11 +102,11 @@ __device__ __forceinline__ float softmax_convert_max(uint32_t (&sv)[2][32], int 
   return __fmul_rn(mh - kMagic, c1);          // (mh - magic) is the exact integer max
 }
 
-// P = 2^(s*c1 + 8.807 - m) for this thread's 64 keys -> e4m3 words in `pw` (key 4w in the low
+// P = 2^(s*c1 + 8.807 - m) for this thread's keys -> e4m3 words in `pw` (key 4w in the low
 // byte); returns the fp32 sum of P (masked keys contribute 0).
 template <bool kMasked>
-__device__ __forceinline__ float softmax_exp_pack(const uint32_t (&sv)[2][32], int valid, float c1, float m,
-                                                  uint32_t (&pw)[16]) {
+__device__ __forceinline__ float softmax_exp_pack(const uint32_t (&sv)[kChunks][32], int valid, float c1, float m,
+                                                  uint32_t (&pw)[kKeys / 4]) {
   auto F = [&](int c) { return __uint_as_float(sv[c >> 5][c & 31]); };
   const float c0 = kFp8Offset - m;
   const uint64_t nmagic = f2_pack(-kMagic, -kMagic);
@@ -106,7 +114,7 @@ __device__ __forceinline__ float softmax_exp_pack(const uint32_t (&sv)[2][32], i
   const uint64_t c1x2 = f2_pack(c1, c1);
   uint64_t acc0 = f2_pack(0.f, 0.f), acc1 = acc0;
 #pragma unroll
-  for (int w = 0; w < 16; ++w) {
+  for (int w = 0; w < kKeys / 4; ++w) {
     uint32_t half16[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
@@ -266,12 +274,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax warpgroups
-    const int wg = (warp - 2) >> 2;                     // key half / O column half
+    const int wg = (warp - 2) >> 2;                     // key slice / O column slice
     const int quarter = warp & 3;                       // TMEM lanes [32*quarter, 32*quarter+32)
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
     const int trow = quarter * 32 + lane;               // row inside the Q tile
     const int row = qt * 128 + trow;
-    const int col0 = wg * 64;
+    const int col0 = wg * kKeys;
     const float qs = a.q_scale[int64_t(bh) * (a.q_pad / 32) + qt * 4 + quarter];
     const int kspb = a.seg_pad / 64;
     float m = -INFINITY, dsum = 0.f;
@@ -279,20 +287,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int i = 0; ok && i < n; ++i) {
       const int jt = t_begin + i;
       const int seg = jt / tiles_per_seg, lt = jt - seg * tiles_per_seg;
-      const int valid = min(128, seg_valid(a, seg) - lt * 128) - col0;   // keys of my half
-      const float c1 = __fmul_rn(__fmul_rn(qs, a.k_scale[int64_t(seg * bhs + bh) * kspb + lt * 2 + wg]), a.sm_log2);
+      const int valid = min(128, seg_valid(a, seg) - lt * 128) - col0;   // keys of my slice
+      const float c1 =
+          __fmul_rn(__fmul_rn(qs, a.k_scale[int64_t(seg * bhs + bh) * kspb + lt * 2 + col0 / 64]), a.sm_log2);
       if (!mbar_wait(&sh->s_full[i & 1], (i >> 1) & 1, abort_flag, a.status, kDevTimeoutS)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const uint32_t ts = ((i & 1) ? tS1 : tS0) + lane_off;
-      uint32_t sv[2][32];
-      tmem_ld32(ts + col0, sv[0]);
-      tmem_ld32(ts + col0 + 32, sv[1]);
+      uint32_t sv[kChunks][32];
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) tmem_ld32(ts + col0 + 32 * c, sv[c]);
       tmem_ld_wait();
-      const bool masked = valid < 64;
-      const float tmax = masked ? softmax_convert_max<true>(sv, valid, c1) : softmax_convert_max<false>(sv, 64, c1);
+      const bool masked = valid < kKeys;
+      const float tmax = masked ? softmax_convert_max<true>(sv, valid, c1) : softmax_convert_max<false>(sv, kKeys, c1);
       // exchange the partial row max with the other warpgroup's thread of this row
       sh->xchg[i & 1][wg][trow] = tmax;
       mbar_arrive(&sh->xchg_bar[quarter][i & 1]);
@@ -300,14 +309,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         ok = false;
         break;
       }
-      const float other = sh->xchg[i & 1][wg ^ 1][trow];
-      const float m_new = fmax3(m, tmax, other);
+      float m_new = fmaxf(m, tmax);
+#pragma unroll
+      for (int g = 0; g < kSoftmaxWGs; ++g) m_new = fmaxf(m_new, sh->xchg[i & 1][g][trow]);
       const float alpha = (m == m_new) ? 1.f : ex2_approx(m - m_new);
       m = m_new;
-      uint32_t pw[16];
-      const float psum = masked ? softmax_exp_pack<true>(sv, valid, c1, m, pw) : softmax_exp_pack<false>(sv, 64, c1, m, pw);
+      uint32_t pw[kKeys / 4];
+      const float psum =
+          masked ? softmax_exp_pack<true>(sv, valid, c1, m, pw) : softmax_exp_pack<false>(sv, kKeys, c1, m, pw);
       dsum = __fmaf_rn(dsum, alpha, psum);
-      tmem_st16(((i & 1) ? tS1 : tS0) + lane_off + wg * 16, pw);
+      tmem_st(((i & 1) ? tS1 : tS0) + lane_off + col0 / 4, pw);
       tmem_st_wait();
       if (i > 0) {
         if (!mbar_wait(&sh->o_done, (i - 1) & 1, abort_flag, a.status, kDevTimeoutO)) {
@@ -317,13 +328,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
+          for (int c = 0; c < kChunks; ++c) {
             uint32_t ov[32];
             const uint32_t ta = tO + lane_off + col0 + 32 * c;
             tmem_ld32(ta, ov);
             tmem_ld_wait();
+            const uint64_t a2 = f2_pack(alpha, alpha);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+            for (int e = 0; e < 32; e += 2) {
+              float lo, hi;
+              f2_unpack(f2_mul(f2_pack(__uint_as_float(ov[e]), __uint_as_float(ov[e + 1])), a2), lo, hi);
+              ov[e] = __float_as_uint(lo);
+              ov[e + 1] = __float_as_uint(hi);
+            }
             tmem_st32(ta, ov);
           }
           tmem_st_wait();
@@ -334,18 +351,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     if (ok && mbar_wait(&sh->o_done, (n - 1) & 1, abort_flag, a.status, kDevTimeoutO)) {
       tc_fence_after();
-      // row sum = the two warpgroups' partial sums (same order in both threads)
+      // row sum = the warpgroups' partial sums (same order in every thread of the row)
       const int par = n & 1;
       sh->xchg[par][wg][trow] = dsum;
       mbar_arrive(&sh->xchg_bar[quarter][par]);
       if (mbar_wait(&sh->xchg_bar[quarter][par], (n >> 1) & 1, abort_flag, a.status, kDevTimeoutS)) {
-        const float dtot = sh->xchg[par][0][trow] + sh->xchg[par][1][trow];
+        float dtot = 0.f;
+#pragma unroll
+        for (int g = 0; g < kSoftmaxWGs; ++g) dtot += sh->xchg[par][g][trow];
         if (a.num_splits == 1) {
           const float rd = __frcp_rn(dtot);
           const float* vs = a.v_scale + int64_t(bh) * 128 + col0;
           __nv_bfloat16* dst = a.out + b * a.so_b + int64_t(row) * a.so_l + h * a.so_h + col0;
 #pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
+          for (int c = 0; c < kChunks; ++c) {
             uint32_t ov[32];
             tmem_ld32(tO + lane_off + col0 + 32 * c, ov);
             tmem_ld_wait();
@@ -368,7 +387,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const int64_t prow = (int64_t(split) * bhs + bh) * a.q_pad + row;
           float* dst = a.o_part + prow * 128 + col0;
 #pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
+          for (int c = 0; c < kChunks; ++c) {
             uint32_t ov[32];
             tmem_ld32(tO + lane_off + col0 + 32 * c, ov);
             tmem_ld_wait();
