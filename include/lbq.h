@@ -106,6 +106,22 @@ LBQ_API int lbq_quant_qkv(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_
                   float* k_scale, uint8_t* vt_codes, float* v_scale, void* km_out,
                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* lbq_quant_qkv for callers that cannot give this library device memory: an embedding runtime
+ * whose device memory pool is fixed and owned elsewhere (no allocation once serving starts), or an
+ * FFI binding that can pass inputs and outputs but not a workspace. Same arguments and results as
+ * lbq_quant_qkv without the workspace; the scratch is a 16 MiB array inside the library (one per
+ * GPU that loads it, kept until exit), so a call needs batch * heads * (ceil(kv_len/64) + 1) * 1536
+ * bytes <= 16 MiB (58176 keys at 12 heads, batch 1) and is rejected with LBQ_ERR_ARG beyond that.
+ * The call allocates nothing. All calls on a device share the array: calls whose kernels overlap
+ * on the GPU race. The first call on a device looks up the array's address; make it before any
+ * stream capture. No counterpart in the reference (its quantizers allocate through torch). */
+LBQ_API int lbq_quant_qkv_static(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, int q_len,
+                                 const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h,
+                                 const void* v, int64_t sv_b, int64_t sv_l, int64_t sv_h, int64_t kv_len,
+                                 int batch, int heads, int8_t* q_codes, float* q_scale, int8_t* k_codes,
+                                 float* k_scale, uint8_t* vt_codes, float* v_scale, void* km_out,
+                                 void* stream);
+
 /* Re-quantize a bf16 KV cache window [0, kv_len) whose block statistics are current (kept by
  * lbq_kv_block_stats on every write): window sums + K/V codes, one segment, in 3 launches.
  * `sums_ws` holds B*H*128 doubles followed by B*H*128 floats.

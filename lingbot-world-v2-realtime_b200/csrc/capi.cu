@@ -76,6 +76,16 @@ int make_map(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_
 
 }  // namespace
 
+namespace lbq {
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+}  // namespace lbq
+
 extern "C" {
 
 int lbq_abi_version(void) { return 100; }

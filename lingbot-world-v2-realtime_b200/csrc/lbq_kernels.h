@@ -99,5 +99,7 @@ cudaError_t launch_attn(const AttnArgs& a, const CUtensorMap& tm_q, const CUtens
                         const CUtensorMap& tm_v, cudaStream_t st);
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st);
 int* device_status_ptr();
+// Records `code` and a printf-style message as this thread's lbq_last_error(); returns `code`.
+int set_error(int code, const char* fmt, ...);
 
 }  // namespace lbq

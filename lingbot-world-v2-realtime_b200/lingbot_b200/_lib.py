@@ -26,6 +26,8 @@ SIGNATURES = {
     "lbq_quant_qkv_workspace": (_sz, [_i32, _i32, _i64]),
     "lbq_quant_qkv": (_i32, [_vp, _i64, _i64, _i64, _i32, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
                              _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "lbq_quant_qkv_static": (_i32, [_vp, _i64, _i64, _i64, _i32, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
+                                    _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "lbq_requant_cache": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _i32, _i64, _i64, _vp, _vp,
                                  _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "lbq_attn_fwd": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _f32, _vp, _i64,
