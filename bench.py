@@ -182,12 +182,9 @@ def max_over_ranks(x, world):
 
 
 def shard_rows(world, rank):
-    """128-aligned query slices: rank r owns rows [r0, r1) of the chunk."""
-    tiles = (LQ + 127) // 128
-    per = -(-tiles // world)
-    r0 = min(LQ, rank * per * 128)
-    r1 = min(LQ, (rank + 1) * per * 128)
-    return r0, r1
+    """128-aligned query slices: rank r owns rows [r0, r1) of the chunk (lingbot_b200.split)."""
+    from lingbot_b200 import split
+    return split.shard_rows(LQ, world, rank)
 
 
 # ----------------------------------------------------------------------------- our chunk
@@ -212,20 +209,15 @@ class Chunk:
         kv_full = torch.randn(2, LAYERS, 1, LQ, H, D, generator=g, device=device)
         kv_full[0] += koff
         kv_full = kv_full.bfloat16()
-        self.kv_parts = self._my_kv_part(kv_full)                 # [2, L, 1, part, H, D]
+        from lingbot_b200 import split
+        self.part = split.token_part(LQ, world)
+        self.kv_parts = torch.stack([torch.stack([split.pad_share(kv_full[t, li], world, rank)
+                                                  for li in range(LAYERS)]) for t in range(2)])   # [2, L, 1, part, H, D]
         del kv_full
         self.out = torch.empty(1, n_loc, H, D, dtype=torch.bfloat16, device=device)
         self.quantizer = kv_cache.WindowQuantizer()
         self.kv_gather = torch.empty(2, world, 1, self.part, H, D, dtype=torch.bfloat16, device=device) \
             if world > 1 else None
-
-    def _my_kv_part(self, kv_full):
-        self.part = -(-LQ // self.world)
-        lo = min(LQ, self.rank * self.part)
-        hi = min(LQ, lo + self.part)
-        buf = torch.zeros(2, LAYERS, 1, self.part, H, D, dtype=torch.bfloat16, device=self.dev)
-        buf[:, :, :, :hi - lo] = kv_full[:, :, :, lo:hi]
-        return buf
 
     def call(self, layer, q=None, kv_part=None, attn_events=None, out=None):
         """One (pass, layer): gather the current chunk's K/V (N > 1), write it into the cache,
@@ -235,12 +227,9 @@ class Chunk:
         q = self.q[layer] if q is None else q
         kv_part = self.kv_parts[:, layer] if kv_part is None else kv_part
         if self.world > 1:
-            import torch.distributed as dist
-            dist.all_gather_into_tensor(self.kv_gather[0], kv_part[0].contiguous())
-            dist.all_gather_into_tensor(self.kv_gather[1], kv_part[1].contiguous())
-            # rank r holds chunk tokens [r*part, (r+1)*part): rank-major order is token order
-            kcur = self.kv_gather[0].reshape(1, self.world * self.part, H, D)[:, :LQ]
-            vcur = self.kv_gather[1].reshape(1, self.world * self.part, H, D)[:, :LQ]
+            from lingbot_b200 import split
+            kcur = split.gather_tokens(kv_part[0], LQ, out=self.kv_gather[0])
+            vcur = split.gather_tokens(kv_part[1], LQ, out=self.kv_gather[1])
         else:
             kcur, vcur = kv_part[0], kv_part[1]
         c["k"][:, MEM:LK] = kcur

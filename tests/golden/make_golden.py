@@ -13,7 +13,7 @@ What it records:
     `lingbot/layers/sage_preq.py:115-124` drives Sage's quantizers per call.
   * kv_schedule.json — the host bookkeeping of `lingbot/layers/kv_cache.py` (plan/evict/write/
     window/commit) over the write / rewrite / eviction schedule of
-    `experiments/bench_attn/sage_preq_check.py:11-36`, with checksums of the cache buffers after
+    `experiments/bench_attn/sage_preq_check.py:11-36`, with float64 (order-independent) checksums of the cache buffers after
     every write.
 """
 import argparse
@@ -106,8 +106,8 @@ def kv_schedule(kvc):
             steps.append(dict(chunk=chunk, rewrite=rewrite, n=n, current_start=start,
                               plan=list(plan), end=end, current_end=cur_end,
                               window=[int(kw.shape[1])],
-                              k_checksum=float(kc["k"].float().sum()),
-                              v_checksum=float(kc["v"].float().sum())))
+                              k_checksum=float(kc["k"].double().sum()),
+                              v_checksum=float(kc["v"].double().sum())))
             kvc.commit(kc, cur_end, end)
         start += n
     return dict(T=T, n_tok=n_tok, sink=sink, local=local, H=H, D=D, steps=steps)
