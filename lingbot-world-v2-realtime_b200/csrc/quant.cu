@@ -70,20 +70,21 @@ __global__ void __launch_bounds__(128) kv_block_stats_kernel(KvBlockStatsArgs a)
       vm[i] = fmaxf(vm[i], fabsf(vf[i]));
     }
   }
-  __shared__ double sh_s[8][128];
-  __shared__ float sh_v[8][128];
+  // [row group][channel within chunk][chunk]: a warp's 16 chunks of one slot are consecutive words
+  __shared__ double sh_s[8][8][16];
+  __shared__ float sh_v[8][8][16];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    sh_s[rg][c16 * 8 + i] = s[i];
-    sh_v[rg][c16 * 8 + i] = vm[i];
+    sh_s[rg][i][c16] = s[i];
+    sh_v[rg][i][c16] = vm[i];
   }
   __syncthreads();
   double tot = 0.0;
   float vmax = 0.f;
 #pragma unroll
   for (int g = 0; g < 8; ++g) {
-    tot += sh_s[g][t];
-    vmax = fmaxf(vmax, sh_v[g][t]);
+    tot += sh_s[g][t & 7][t >> 3];
+    vmax = fmaxf(vmax, sh_v[g][t & 7][t >> 3]);
   }
   const int64_t o = ((int64_t(b) * a.max_blocks + blk) * a.heads + h) * 128 + t;
   a.ksum[o] = tot;
@@ -91,11 +92,12 @@ __global__ void __launch_bounds__(128) kv_block_stats_kernel(KvBlockStatsArgs a)
 }
 
 // ------------------------------------------------------------------ window sums
-// One CTA per (head, batch): per channel, sum of the block sums (fixed order -> deterministic) and
-// max of the block maxima over blocks [blk_begin, blk_end).
-__global__ void __launch_bounds__(1024) kv_window_sums_kernel(KvWindowSumsArgs a) {
-  const int h = blockIdx.x, b = blockIdx.y;
-  const int c = threadIdx.x & 127, g = threadIdx.x >> 7;   // 8 block groups
+// One CTA per (32-channel group, head, batch), 256 threads = 32 channels x 8 block groups: per
+// channel, the sum of the block sums (fixed order -> deterministic) and the max of the block maxima
+// over blocks [blk_begin, blk_end).
+__global__ void __launch_bounds__(256) kv_window_sums_kernel(KvWindowSumsArgs a) {
+  const int cg = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int c = cg * 32 + (threadIdx.x & 31), g = threadIdx.x >> 5;
   double s = 0.0;
   float vm = 0.f;
   for (int blk = a.blk_begin + g; blk < a.blk_end; blk += 8) {
@@ -103,18 +105,18 @@ __global__ void __launch_bounds__(1024) kv_window_sums_kernel(KvWindowSumsArgs a
     s += a.ksum[o];
     vm = fmaxf(vm, a.vamax[o]);
   }
-  __shared__ double sh_s[8][128];
-  __shared__ float sh_v[8][128];
-  sh_s[g][c] = s;
-  sh_v[g][c] = vm;
+  __shared__ double sh_s[8][32];
+  __shared__ float sh_v[8][32];
+  sh_s[g][threadIdx.x & 31] = s;
+  sh_v[g][threadIdx.x & 31] = vm;
   __syncthreads();
   if (g == 0) {
     double tot = 0.0;
     float vmax = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      tot += sh_s[i][c];
-      vmax = fmaxf(vmax, sh_v[i][c]);
+      tot += sh_s[i][threadIdx.x];
+      vmax = fmaxf(vmax, sh_v[i][threadIdx.x]);
     }
     const int64_t o = (int64_t(b) * a.heads + h) * 128 + c;
     a.ksum_total[o] = tot;
@@ -123,42 +125,50 @@ __global__ void __launch_bounds__(1024) kv_window_sums_kernel(KvWindowSumsArgs a
 }
 
 // ------------------------------------------------------------------ Q quantizer
-// One CTA (4 warps) per (128-row tile, head, batch); warp w owns the 32-row scale group.
-// Lane l handles rows 2*i + (l >> 4), 16-byte chunk (l & 15), i = 0..15.
-__global__ void __launch_bounds__(128) quant_q_kernel(QuantQArgs a) {
+// One CTA (8 warps) per (128-row tile, head, batch); warps 2g and 2g+1 share the 32-row scale group
+// g, 16 rows each. Lane l handles rows 2*i + (l >> 4) of its warp's 16, 16-byte chunk (l & 15). The
+// raw bf16 stays in registers for the second (quantizing) pass.
+__global__ void __launch_bounds__(256) quant_q_kernel(QuantQArgs a) {
   const int tile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  const int row0 = tile * 128 + w * 32;
+  const int g = w >> 1;
+  const int row0 = tile * 128 + g * 32 + (w & 1) * 16;
   const int c16 = l & 15;
-  float x[16][8];
+  __shared__ float sh_max[8];
+  uint4 raw[8];
   float amax = 0.f;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
+  for (int i = 0; i < 8; ++i) {
     const int row = row0 + 2 * i + (l >> 4);
-    if (row < a.q_len) {
-      const uint4 r = *reinterpret_cast<const uint4*>(a.q + b * a.sq_b + int64_t(row) * a.sq_l + h * a.sq_h + c16 * 8);
-      bf16x8_to_f32(r, x[i]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) x[i][j] = 0.f;
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(x[i][j]));
+    raw[i] = row < a.q_len
+                 ? *reinterpret_cast<const uint4*>(a.q + b * a.sq_b + int64_t(row) * a.sq_l + h * a.sq_h + c16 * 8)
+                 : make_uint4(0u, 0u, 0u, 0u);
   }
-  amax = fmaxf(warp_max(amax), 1e-7f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float x[8];
+    bf16x8_to_f32(raw[i], x);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(x[j]));
+  }
+  amax = warp_max(amax);
+  if (l == 0) sh_max[w] = amax;
+  __syncthreads();
+  amax = fmaxf(fmaxf(sh_max[2 * g], sh_max[2 * g + 1]), 1e-7f);
   const float inv = __fmul_rn(__frcp_rn(amax), 127.f);
   const int64_t bh = int64_t(b) * a.heads + h;
-  if (l == 0) a.q_scale[bh * (a.q_pad / 32) + tile * 4 + w] = __fdiv_rn(amax, 127.f);
+  if (threadIdx.x == 64 * g) a.q_scale[bh * (a.q_pad / 32) + tile * 4 + g] = __fdiv_rn(amax, 127.f);
   int8_t* dst = a.q_codes + (bh * a.q_pad + row0) * 128;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int row = 2 * i + (l >> 4);
+  for (int i = 0; i < 8; ++i) {
+    float x[8];
+    bf16x8_to_f32(raw[i], x);
     uint2 packed;
-    packed.x = pack_s8x4(cvt_rni_sat_s8(__fmul_rn(x[i][0], inv)), cvt_rni_sat_s8(__fmul_rn(x[i][1], inv)),
-                         cvt_rni_sat_s8(__fmul_rn(x[i][2], inv)), cvt_rni_sat_s8(__fmul_rn(x[i][3], inv)));
-    packed.y = pack_s8x4(cvt_rni_sat_s8(__fmul_rn(x[i][4], inv)), cvt_rni_sat_s8(__fmul_rn(x[i][5], inv)),
-                         cvt_rni_sat_s8(__fmul_rn(x[i][6], inv)), cvt_rni_sat_s8(__fmul_rn(x[i][7], inv)));
-    *reinterpret_cast<uint2*>(dst + row * 128 + c16 * 8) = packed;
+    packed.x = pack_s8x4(cvt_rni_sat_s8(__fmul_rn(x[0], inv)), cvt_rni_sat_s8(__fmul_rn(x[1], inv)),
+                         cvt_rni_sat_s8(__fmul_rn(x[2], inv)), cvt_rni_sat_s8(__fmul_rn(x[3], inv)));
+    packed.y = pack_s8x4(cvt_rni_sat_s8(__fmul_rn(x[4], inv)), cvt_rni_sat_s8(__fmul_rn(x[5], inv)),
+                         cvt_rni_sat_s8(__fmul_rn(x[6], inv)), cvt_rni_sat_s8(__fmul_rn(x[7], inv)));
+    *reinterpret_cast<uint2*>(dst + (2 * i + (l >> 4)) * 128 + c16 * 8) = packed;
   }
 }
 
@@ -187,23 +197,24 @@ __global__ void __launch_bounds__(128) quant_k_kernel(QuantKArgs a) {
   float km[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) km[j] = sh_km[c16 * 8 + j];
-  float x[8][8];
+  uint4 raw[8];
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int r = rg + 8 * i;
     const int64_t tok = int64_t(blk) * 64 + r;      // token index inside this segment
+    raw[i] = tok < a.seg_valid
+                 ? *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + (a.tok0 + tok) * a.sk_l + h * a.sk_h + c16 * 8)
+                 : make_uint4(0u, 0u, 0u, 0u);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t tok = int64_t(blk) * 64 + rg + 8 * i;
     if (tok < a.seg_valid) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + (a.tok0 + tok) * a.sk_l + h * a.sk_h + c16 * 8);
-      bf16x8_to_f32(raw, x[i]);
+      float x[8];
+      bf16x8_to_f32(raw[i], x);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        x[i][j] = __fsub_rn(x[i][j], km[j]);
-        amax = fmaxf(amax, fabsf(x[i][j]));
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) x[i][j] = 0.f;
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(__fsub_rn(x[j], km[j])));
     }
   }
   amax = warp_max(amax);
@@ -217,65 +228,73 @@ __global__ void __launch_bounds__(128) quant_k_kernel(QuantKArgs a) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int r = rg + 8 * i;
+    const bool valid = int64_t(blk) * 64 + r < a.seg_valid;   // pad tokens encode 0
+    float x[8];
+    bf16x8_to_f32(raw[i], x);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = valid ? __fmul_rn(__fsub_rn(x[j], km[j]), inv) : 0.f;
     uint2 packed;
-    packed.x = pack_s8x4(cvt_rni_sat_s8(__fmul_rn(x[i][0], inv)), cvt_rni_sat_s8(__fmul_rn(x[i][1], inv)),
-                         cvt_rni_sat_s8(__fmul_rn(x[i][2], inv)), cvt_rni_sat_s8(__fmul_rn(x[i][3], inv)));
-    packed.y = pack_s8x4(cvt_rni_sat_s8(__fmul_rn(x[i][4], inv)), cvt_rni_sat_s8(__fmul_rn(x[i][5], inv)),
-                         cvt_rni_sat_s8(__fmul_rn(x[i][6], inv)), cvt_rni_sat_s8(__fmul_rn(x[i][7], inv)));
+    packed.x = pack_s8x4(cvt_rni_sat_s8(x[0]), cvt_rni_sat_s8(x[1]), cvt_rni_sat_s8(x[2]), cvt_rni_sat_s8(x[3]));
+    packed.y = pack_s8x4(cvt_rni_sat_s8(x[4]), cvt_rni_sat_s8(x[5]), cvt_rni_sat_s8(x[6]), cvt_rni_sat_s8(x[7]));
     *reinterpret_cast<uint2*>(dst + r * 128 + c16 * 8) = packed;
   }
 }
 
 // ------------------------------------------------------------------ V quantizer (transposing)
-// One CTA per (128-token tile of this segment, head, batch), 256 threads. Reads [128 tok][128 ch]
-// bf16, writes e4m3 codes transposed to [128 ch][128 tok] through shared memory.
+// One CTA per (128-token tile of this segment, head, batch), 256 threads. The bf16 tile
+// [128 tokens][128 channels] is staged in shared memory with coalesced 16-byte loads (row pitch
+// 272 bytes, so the column reads below are conflict-free); then thread t takes the channel pair
+// (2*(t & 63), +1) over 32 tokens (32*(t >> 6) ...), converts to e4m3 and writes, per channel,
+// 32 consecutive key bytes of the transposed codes [channel][key].
+constexpr int kVtPitch = 272;   // bytes per staged token row
+
 __global__ void __launch_bounds__(256) quant_vt_kernel(QuantVArgs a) {
   const int tile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int t = threadIdx.x;
   const int64_t bh = int64_t(b) * a.heads + h;
+  __shared__ __align__(16) uint8_t sh_v[128 * kVtPitch];
   __shared__ float sh_recp[128];
-  __shared__ __align__(16) uint8_t sh_t[128][128 + 16];   // [channel][token], padded rows
   if (t < 128) {
     const float amax = a.vamax_total[bh * 128 + t];
     sh_recp[t] = __fmul_rn(__frcp_rn(amax), 2.25f);
     if (tile == 0 && a.write_scale) a.v_scale[bh * 128 + t] = __fdiv_rn(amax, 2.25f);
   }
-  __syncthreads();
-  const int c16 = t & 15;
-  float rc[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) rc[j] = sh_recp[c16 * 8 + j];
-#pragma unroll 4
   for (int i = 0; i < 8; ++i) {
-    const int r = (t >> 4) + 16 * i;                 // token row inside the tile
+    const int piece = t + 256 * i;                   // 2048 pieces of 16 bytes
+    const int r = piece >> 4, c16 = piece & 15;
     const int64_t tok = int64_t(tile) * 128 + r;
-    float x[8];
-    if (tok < a.seg_valid) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + (a.tok0 + tok) * a.sv_l + h * a.sv_h + c16 * 8);
-      bf16x8_to_f32(raw, x);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) x[j] = fminf(fmaxf(__fmul_rn(x[j], rc[j]), -2.25f), 2.25f);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) x[j] = 0.f;
-    }
-#pragma unroll
-    for (int j = 0; j < 8; j += 2) {
-      const uint32_t p = pack_e4m3x2(x[j], x[j + 1]);
-      sh_t[c16 * 8 + j][r] = uint8_t(p & 0xff);
-      sh_t[c16 * 8 + j + 1][r] = uint8_t(p >> 8);
-    }
+    const uint4 raw = tok < a.seg_valid
+                          ? *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + (a.tok0 + tok) * a.sv_l + h * a.sv_h + c16 * 8)
+                          : make_uint4(0u, 0u, 0u, 0u);
+    *reinterpret_cast<uint4*>(&sh_v[r * kVtPitch + c16 * 16]) = raw;
   }
   __syncthreads();
-  // 128 channel rows x 128 bytes: each thread stores 16-byte pieces.
-  const int64_t seg_bh = (int64_t(a.seg) * a.batch + b) * a.heads + h;
-  uint8_t* dst = a.vt_codes + seg_bh * 128 * a.seg_pad + int64_t(tile) * 128;
+  const int cp = t & 63, tq = t >> 6;
+  const float r0 = sh_recp[2 * cp], r1 = sh_recp[2 * cp + 1];
+  uint32_t w0[8], w1[8];                             // channel 2cp / 2cp+1: 32 key bytes each
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int piece = t + 256 * i;                   // 1024 pieces of 16 bytes
-    const int ch = piece >> 3, off = (piece & 7) * 16;
-    *reinterpret_cast<uint4*>(dst + int64_t(ch) * a.seg_pad + off) = *reinterpret_cast<const uint4*>(&sh_t[ch][off]);
+  for (int k4 = 0; k4 < 8; ++k4) {
+    float lo[4], hi[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int r = tq * 32 + 4 * k4 + e;
+      const uint32_t pair = *reinterpret_cast<const uint32_t*>(&sh_v[r * kVtPitch + cp * 4]);
+      lo[e] = fminf(fmaxf(__fmul_rn(__uint_as_float(pair << 16), r0), -2.25f), 2.25f);
+      hi[e] = fminf(fmaxf(__fmul_rn(__uint_as_float(pair & 0xffff0000u), r1), -2.25f), 2.25f);
+    }
+    // padded tokens were staged as 0 and encode as 0
+    w0[k4] = pack_e4m3x2(lo[0], lo[1]) | (pack_e4m3x2(lo[2], lo[3]) << 16);
+    w1[k4] = pack_e4m3x2(hi[0], hi[1]) | (pack_e4m3x2(hi[2], hi[3]) << 16);
   }
+  const int64_t seg_bh = (int64_t(a.seg) * a.batch + b) * a.heads + h;
+  uint8_t* dst = a.vt_codes + seg_bh * 128 * a.seg_pad + int64_t(tile) * 128 + tq * 32;
+  uint4* d0 = reinterpret_cast<uint4*>(dst + int64_t(2 * cp) * a.seg_pad);
+  uint4* d1 = reinterpret_cast<uint4*>(dst + int64_t(2 * cp + 1) * a.seg_pad);
+  d0[0] = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+  d0[1] = make_uint4(w0[4], w0[5], w0[6], w0[7]);
+  d1[0] = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+  d1[1] = make_uint4(w1[4], w1[5], w1[6], w1[7]);
 }
 
 // ------------------------------------------------------------------ launchers
@@ -285,13 +304,13 @@ cudaError_t launch_kv_block_stats(const KvBlockStatsArgs& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 cudaError_t launch_kv_window_sums(const KvWindowSumsArgs& a, cudaStream_t st) {
-  dim3 grid(a.heads, a.batch);
-  kv_window_sums_kernel<<<grid, 1024, 0, st>>>(a);
+  dim3 grid(4, a.heads, a.batch);
+  kv_window_sums_kernel<<<grid, 256, 0, st>>>(a);
   return cudaGetLastError();
 }
 cudaError_t launch_quant_q(const QuantQArgs& a, cudaStream_t st) {
   dim3 grid(a.q_pad / 128, a.heads, a.batch);
-  quant_q_kernel<<<grid, 128, 0, st>>>(a);
+  quant_q_kernel<<<grid, 256, 0, st>>>(a);
   return cudaGetLastError();
 }
 cudaError_t launch_quant_k(const QuantKArgs& a, cudaStream_t st) {
