@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["chunk", "call", "requant"], default="chunk")
+    ap.add_argument("--call-kv", type=int, default=12064,
+                    help="keys of the single-call workload (12064 = BASELINE config 1; 30160 = one chunk call)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -391,7 +393,7 @@ def run_call(args, world, rank, local):
     through 8 sets (> L2)."""
     from lingbot_b200 import ops
     dev = torch.device("cuda", local)
-    lq, lk = 6032, 12064
+    lq, lk = 6032, args.call_kv
     g = torch.Generator(device=dev).manual_seed(0)
     sets = []
     for _ in range(8):
@@ -525,7 +527,7 @@ def main():
                     "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                     "dtype": "int8 QK^T / fp8 e4m3 PV (bf16 in/out)", "data": "synthetic",
                     "config": {"workload": {"chunk": "BASELINE config 4: full chunk, 4 denoise + 1 memory-write pass x 30 layers",
-                                            "call": "BASELINE config 1: q 6032 x kv 12064",
+                                            "call": f"BASELINE config 1: q 6032 x kv {args.call_kv}",
                                             "requant": "BASELINE config 2: bf16 cache [30, 24128, 12, 128]"}[args.workload],
                                "q_len": LQ, "kv_len": LK, "memory_tokens": MEM, "heads": H, "head_dim": D,
                                "parallelism": f"query shards x{world}" if world > 1 else "single GPU",
