@@ -18,12 +18,14 @@
 //
 // CTA = two 128-row Q tiles (A, B) x one (batch, head) x one KV split. Warps: 0 = TMA producer,
 // 1 = tcgen05 issuer (one thread), 2..5 = softmax warpgroup A, 6..9 = softmax warpgroup B. Q row r
-// of a tile is TMEM lane r; one thread owns one row and all 128 keys of each key tile. The issuer
-// interleaves the tiles (PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1)), so while one warpgroup computes
-// its softmax the tensor core works for the other.
-// Tensor memory (512 columns): S_A [0,128), S_B [128,256) as int32 scores, O_A [256,384),
-// O_B [384,512) in fp32; columns [0,32) of each S buffer are overwritten by that tile's e4m3 P
-// (4 keys per column), which the P.V product reads as its A operand.
+// of a tile is TMEM lane r; one thread owns one row and all 128 keys of each key tile. While one
+// warpgroup computes its softmax the tensor core works for the other.
+// Tensor memory (512 columns): S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512) (fp32).
+// As soon as a warpgroup has read its scores it refills its S buffer with 0x4B400000, the bits of
+// the float 1.5*2^23, and the next Q.K^T accumulates onto it: the int32 accumulator then holds the
+// bits of the float 1.5*2^23 + S (|S| <= 128*127*127 < 2^22), so scores need no conversion. P is
+// written (e4m3, 128-byte-swizzled K-major rows) to a double-buffered shared-memory tile that the
+// P.V product reads as its A operand; the next Q.K^T therefore does not wait for P.V.
 #include <cuda_bf16.h>
 #include <cstdint>
 
@@ -32,7 +34,7 @@
 
 namespace lbq {
 
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr int kTile = 128 * 128;         // bytes of one 128 x 128 8-bit tile
 constexpr int kAttnThreads = 64 + 256;   // producer, issuer, 2 softmax warpgroups
 constexpr float kFp8Offset = 8.807f;     // splitkv/README.md:58 (S_FP8_OFFSET)
@@ -52,6 +54,7 @@ struct AttnShared {
   uint64_t v_full[kStages];
   uint64_t v_empty[kStages];
   uint64_t s_full[2];                    // per Q tile
+  uint64_t s_free[2];
   uint64_t p_full[2];
   uint64_t o_done[2];
   uint64_t drain;
@@ -59,7 +62,8 @@ struct AttnShared {
   int abort;
 };
 
-constexpr size_t kAttnSmemBytes = 1024 /*alignment slack*/ + kTile * (2 + 2 * kStages) + sizeof(AttnShared);
+// smem: Q_A, Q_B | P_A[2], P_B[2] | K stages | V stages | barriers
+constexpr size_t kAttnSmemBytes = 1024 /*alignment slack*/ + kTile * (6 + 2 * kStages) + sizeof(AttnShared);
 
 __device__ int g_status;
 
@@ -68,23 +72,19 @@ __device__ __forceinline__ int seg_valid(const AttnArgs& a, int seg) {
   return rest < a.seg_len ? rest : a.seg_len;
 }
 
-// Softmax of one 128-key tile for the calling thread's row. `sv` holds the int32 scores loaded from
-// tensor memory; the e4m3 P is stored to tensor memory at `tP` (4 keys per 32-bit column, key 4w
-// in the low byte of column w) in 32-key chunks as it is produced, `m` and `dsum` are updated and
-// the factor O must be rescaled by, 2^(m_old - m_new), is returned.
-// Scores become floats by the magic-number add (S + 0x4B400000 is the float 1.5*2^23 + S for
-// |S| < 2^22, and |S| <= 128*127*127 here), which keeps the conversion off the MUFU pipe. Keys
-// 0..63 use K scale c1a, keys 64..127 use c1b (one 64-token block each).
+// Softmax of one 128-key tile for the calling thread's row. `sv` holds the scores as the bits of
+// 1.5*2^23 + S (see the tensor-memory note above). The e4m3 P is written to this row of the shared
+// P tile `prow` (128 bytes, 16-byte chunk c stored at chunk c ^ (row & 7): the 128-byte swizzle the
+// MMA descriptor expects) as it is produced; `m` and `dsum` are updated and the factor O must be
+// rescaled by, 2^(m_old - m_new), is returned. Keys 0..63 use K scale c1a, keys 64..127 use c1b.
 template <bool kMasked>
 __device__ __forceinline__ float softmax_tile(uint32_t (&sv)[4][32], int valid, float c1a, float c1b, float& m,
-                                              float& dsum, uint32_t tP) {
+                                              float& dsum, uint8_t* prow, int rsw) {
   if (kMasked) {
 #pragma unroll
     for (int c = 0; c < 128; ++c)
-      if (c >= valid) sv[c >> 5][c & 31] = 0xFFC00000u;     // -2^22: below every real score
+      if (c >= valid) sv[c >> 5][c & 31] = 0x4B000000u;     // 1.5*2^23 - 2^22: below every real score
   }
-#pragma unroll
-  for (int c = 0; c < 128; ++c) sv[c >> 5][c & 31] += 0x4B400000u;
   auto F = [&](int c) { return __uint_as_float(sv[c >> 5][c & 31]); };
   float mh[2];
 #pragma unroll
@@ -108,20 +108,21 @@ __device__ __forceinline__ float softmax_tile(uint32_t (&sv)[4][32], int valid, 
   const float m_new = fmaxf(m, tmax);
   const float alpha = (m == m_new) ? 1.f : ex2_approx(m - m_new);
   m = m_new;
-  const float c0 = kFp8Offset - m_new;
-  const uint64_t nmagic = f2_pack(-kMagic, -kMagic);
-  const uint64_t c0x2 = f2_pack(c0, c0);
+  // x = (f - magic) * c1 + (8.807 - m) = f * c1 + c0, c0 = 8.807 - m - magic * c1 (one rounding; the
+  // argument is off by at most half an ulp of |c0|, about 6e-5 for typical scales)
+  const float c0a = fmaf(-kMagic, c1a, kFp8Offset - m_new);
+  const float c0b = fmaf(-kMagic, c1b, kFp8Offset - m_new);
+  const uint64_t c0ax2 = f2_pack(c0a, c0a), c0bx2 = f2_pack(c0b, c0b);
   const uint64_t c1ax2 = f2_pack(c1a, c1a), c1bx2 = f2_pack(c1b, c1b);
   uint64_t acc0 = f2_pack(0.f, 0.f), acc1 = acc0;
-  uint32_t pw[8];
+  uint32_t pw[4];
 #pragma unroll
   for (int w = 0; w < 32; ++w) {
     uint32_t half16[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int c = 4 * w + 2 * e;
-      const uint64_t t = f2_add(f2_pack(F(c), F(c + 1)), nmagic);          // exact: the integer score
-      const uint64_t x = f2_fma(t, c < 64 ? c1ax2 : c1bx2, c0x2);           // s - m + 8.807 (log2)
+      const uint64_t x = f2_fma(f2_pack(F(c), F(c + 1)), c < 64 ? c1ax2 : c1bx2, c < 64 ? c0ax2 : c0bx2);
       float x0, x1;
       f2_unpack(x, x0, x1);
       uint64_t p;
@@ -140,8 +141,9 @@ __device__ __forceinline__ float softmax_tile(uint32_t (&sv)[4][32], int valid, 
       if (e == 0) acc0 = f2_add(acc0, p); else acc1 = f2_add(acc1, p);
       half16[e] = pack_e4m3x2(p0, p1);
     }
-    pw[w & 7] = half16[0] | (half16[1] << 16);
-    if ((w & 7) == 7) tmem_st8(tP + (w & ~7), pw);     // keys of S chunk w/8 are no longer needed
+    pw[w & 3] = half16[0] | (half16[1] << 16);
+    if ((w & 3) == 3)   // 16 keys done: one swizzled 16-byte chunk of the row
+      *reinterpret_cast<uint4*>(prow + (((w >> 2) ^ rsw) << 4)) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
   }
   float s0, s1, s2, s3;
   f2_unpack(acc0, s0, s1);
@@ -157,9 +159,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                              // [2][kTile]
-  uint8_t* sK = smem + 2 * kTile;
-  uint8_t* sV = smem + kTile * (2 + kStages);
-  AttnShared* sh = reinterpret_cast<AttnShared*>(smem + kTile * (2 + 2 * kStages));
+  uint8_t* sP = smem + 2 * kTile;                  // [tile][buffer][kTile]
+  uint8_t* sK = smem + 6 * kTile;
+  uint8_t* sV = smem + kTile * (6 + kStages);
+  AttnShared* sh = reinterpret_cast<AttnShared*>(smem + kTile * (6 + 2 * kStages));
   volatile int* abort_flag = &sh->abort;
 
   const int qp = blockIdx.x, bh = blockIdx.y, split = blockIdx.z;   // qp: pair of 128-row Q tiles
@@ -181,6 +184,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sh->s_full[t], 1);
+      mbar_init(&sh->s_free[t], 128);
       mbar_init(&sh->p_full[t], 128);
       mbar_init(&sh->o_done[t], 1);
     }
@@ -241,42 +245,45 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       bool ok = mbar_wait(&sh->q_full, 0, abort_flag, a.status, kDevTimeoutQ);
       tc_fence_after();
       const uint64_t qdesc[2] = {smem_desc_sw128(smem_u32(sQ)), smem_desc_sw128(smem_u32(sQ + kTile))};
+      // S_t += Q_t . K(i)^T, onto the magic constant the softmax left in S_t
       auto issue_qk = [&](int t, int i) {
         const uint64_t kdesc = smem_desc_sw128(smem_u32(sK + (i % kStages) * kTile));
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_i8_ss(tmem + 128 * t, qdesc[t] + 2 * kk, kdesc + 2 * kk, kIdescQK, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk) mma_i8_ss(tmem + 128 * t, qdesc[t] + 2 * kk, kdesc + 2 * kk, kIdescQK, 1u);
         tc_commit(&sh->s_full[t]);
       };
       auto issue_pv = [&](int t, int j) {
+        const uint64_t pdesc = smem_desc_sw128(smem_u32(sP + (2 * t + (j & 1)) * kTile));
         const uint64_t vdesc = smem_desc_sw128(smem_u32(sV + (j % kStages) * kTile));
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          mma_f8_ts(tmem + 256 + 128 * t, tmem + 128 * t + 8 * kk, vdesc + 2 * kk, kIdescPV,
-                    (j > 0 || kk > 0) ? 1u : 0u);
+          mma_f8_ss(tmem + 256 + 128 * t, pdesc + 2 * kk, vdesc + 2 * kk, kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&sh->o_done[t]);
       };
       if (ok && (ok = mbar_wait(&sh->k_full[0], 0, abort_flag, a.status, kDevTimeoutKV))) {
-        tc_fence_after();
-        issue_qk(0, 0);
-        issue_qk(1, 0);
-        tc_commit(&sh->k_empty[0]);
+        for (int t = 0; ok && t < 2; ++t) {
+          ok = mbar_wait(&sh->s_free[t], 0, abort_flag, a.status, kDevTimeoutS);   // S_t initialised
+          tc_fence_after();
+          if (ok) issue_qk(t, 0);
+        }
+        if (ok) tc_commit(&sh->k_empty[0]);
       }
       for (int j = 0; ok && j < n; ++j) {
         const int s = j % kStages;
         const bool more = j + 1 < n;
-        if (!mbar_wait(&sh->v_full[s], (j / kStages) & 1, abort_flag, a.status, kDevTimeoutKV)) break;
         if (more && !mbar_wait(&sh->k_full[(j + 1) % kStages], ((j + 1) / kStages) & 1, abort_flag, a.status,
                                kDevTimeoutKV))
           break;
-        for (int t = 0; t < 2; ++t) {
-          if (!mbar_wait(&sh->p_full[t], j & 1, abort_flag, a.status, kDevTimeoutP)) {
-            ok = false;
-            break;
+        if (!mbar_wait(&sh->v_full[s], (j / kStages) & 1, abort_flag, a.status, kDevTimeoutKV)) break;
+        for (int t = 0; ok && t < 2; ++t) {
+          if (more) {            // S_t(j) read and refilled -> next scores
+            if (!(ok = mbar_wait(&sh->s_free[t], (j + 1) & 1, abort_flag, a.status, kDevTimeoutS))) break;
+            tc_fence_after();
+            issue_qk(t, j + 1);
           }
+          if (!(ok = mbar_wait(&sh->p_full[t], j & 1, abort_flag, a.status, kDevTimeoutP))) break;
           tc_fence_after();
-          issue_pv(t, j);                               // reads P_t(j) from S_t ...
-          if (more) issue_qk(t, j + 1);                 // ... before S_t is overwritten
+          issue_pv(t, j);
         }
         if (!ok) break;
         tc_commit(&sh->v_empty[s]);
@@ -303,6 +310,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     };
     float m = -INFINITY, dsum = 0.f;
     bool ok = n > 0;
+    const int prow_off = (quarter * 32 + lane) * 128;
+    const int rsw = lane & 7;                               // row & 7 (rows of a warp start at 32k)
+    // S_t starts as the magic constant (the first Q.K^T accumulates onto it)
+#pragma unroll
+    for (int c = 0; c < 16; ++c) tmem_fill8(tS + 8 * c, 0x4B400000u);
+    tmem_st_wait();
+    tc_fence_before();
+    mbar_arrive(&sh->s_free[t]);
     float2 ks_next = ok ? *reinterpret_cast<const float2*>(kscale_ptr(0)) : make_float2(0.f, 0.f);
     for (int i = 0; ok && i < n; ++i) {
       const int jt = t_begin + i;
@@ -323,9 +338,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tmem_ld32(tS + 64, sv[2]);
       tmem_ld32(tS + 96, sv[3]);
       tmem_ld_wait();
-      const float alpha = valid == 128 ? softmax_tile<false>(sv, 128, c1a, c1b, m, dsum, tS)
-                                       : softmax_tile<true>(sv, valid, c1a, c1b, m, dsum, tS);
+      // refill S_t with the magic constant and let the next Q.K^T go
+#pragma unroll
+      for (int c = 0; c < 16; ++c) tmem_fill8(tS + 8 * c, 0x4B400000u);
       tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&sh->s_free[t]);
+      // P_t[i & 1] was last read by P.V of tile i - 2, complete since the o_done wait of tile i - 1
+      uint8_t* prow = sP + (2 * t + (i & 1)) * kTile + prow_off;
+      const float alpha = valid == 128 ? softmax_tile<false>(sv, 128, c1a, c1b, m, dsum, prow, rsw)
+                                       : softmax_tile<true>(sv, valid, c1a, c1b, m, dsum, prow, rsw);
+      fence_proxy_async_smem();
       if (i > 0) {
         if (!mbar_wait(&sh->o_done[t], (i - 1) & 1, abort_flag, a.status, kDevTimeoutO)) {
           ok = false;
