@@ -358,18 +358,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
           const uint64_t a2 = f2_pack(alpha, alpha);
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t ov[32];
-            tmem_ld32(tO + 32 * c, ov);
+          for (int c = 0; c < 4; c += 2) {     // two 32-column chunks per load/store round trip
+            uint32_t ov[2][32];
+            tmem_ld32(tO + 32 * c, ov[0]);
+            tmem_ld32(tO + 32 * c + 32, ov[1]);
             tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              float lo, hi;
-              f2_unpack(f2_mul(f2_pack(__uint_as_float(ov[e]), __uint_as_float(ov[e + 1])), a2), lo, hi);
-              ov[e] = __float_as_uint(lo);
-              ov[e + 1] = __float_as_uint(hi);
+            for (int h2 = 0; h2 < 2; ++h2) {
+#pragma unroll
+              for (int e = 0; e < 32; e += 2) {
+                float lo, hi;
+                f2_unpack(f2_mul(f2_pack(__uint_as_float(ov[h2][e]), __uint_as_float(ov[h2][e + 1])), a2), lo, hi);
+                ov[h2][e] = __float_as_uint(lo);
+                ov[h2][e + 1] = __float_as_uint(hi);
+              }
             }
-            tmem_st32(tO + 32 * c, ov);
+            tmem_st32(tO + 32 * c, ov[0]);
+            tmem_st32(tO + 32 * c + 32, ov[1]);
           }
           tmem_st_wait();
         }
