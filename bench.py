@@ -218,8 +218,12 @@ class Chunk:
         del kv_full
         self.out = torch.empty(1, n_loc, H, D, dtype=torch.bfloat16, device=device)
         self.quantizer = kv_cache.WindowQuantizer()
-        self.kv_gather = torch.empty(2, world, 1, self.part, H, D, dtype=torch.bfloat16, device=device) \
-            if world > 1 else None
+        self.splitter = None
+        if world > 1:
+            # N > 1: the chunk's K/V all-gather overlaps the re-quant of the replicated memory part
+            self.splitter = split.SplitAttention(1, H, n_loc, MEM, LQ, device)
+            for c in self.caches:
+                self.splitter.memory_changed(c)
 
     def call(self, layer, q=None, kv_part=None, attn_events=None, out=None):
         """One (pass, layer): gather the current chunk's K/V (N > 1), write it into the cache,
@@ -228,12 +232,11 @@ class Chunk:
         c = self.caches[layer]
         q = self.q[layer] if q is None else q
         kv_part = self.kv_parts[:, layer] if kv_part is None else kv_part
-        if self.world > 1:
-            from lingbot_b200 import split
-            kcur = split.gather_tokens(kv_part[0], LQ, out=self.kv_gather[0])
-            vcur = split.gather_tokens(kv_part[1], LQ, out=self.kv_gather[1])
-        else:
-            kcur, vcur = kv_part[0], kv_part[1]
+        splits = ops.pick_splits(1, H, self.r1 - self.r0, LK)
+        if self.splitter is not None:
+            self.splitter(q, c, kv_part[0], kv_part[1], self.out if out is None else out, attn_events=attn_events)
+            return 9 + (1 if splits > 1 else 0)
+        kcur, vcur = kv_part[0], kv_part[1]
         c["k"][:, MEM:LK] = kcur
         c["v"][:, MEM:LK] = vcur
         kv_cache.refresh_stats(c, MEM, LK)
@@ -243,7 +246,6 @@ class Chunk:
         ops.attn_from_codes(w, out=self.out if out is None else out)
         if attn_events is not None:
             attn_events[1].record()
-        splits = ops.pick_splits(1, H, self.r1 - self.r0, LK)
         return 6 + (1 if splits > 1 else 0)
 
     def step(self, attn_times=None):

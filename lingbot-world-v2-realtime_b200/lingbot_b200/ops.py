@@ -92,14 +92,14 @@ def quantize_qkv(q, k, v) -> QuantWindow:
 
 
 def pick_splits(batch, heads, q_len, kv_len, num_sms=NUM_SMS_B200):
-    """Split the key range when the (q-tile, head) grid cannot fill the SMs: aim at ~2 CTAs per SM
-    without making a split shorter than 8 key tiles."""
-    ctas = (round_up(q_len, 128) // 128) * batch * heads
+    """Split the key range when the grid cannot fill the SMs. A CTA of the attention kernel holds a
+    pair of 128-row Q tiles and occupies a whole SM, so the split count is the largest one that keeps
+    the grid within one wave (no tail), and never makes a split shorter than 8 key tiles."""
+    ctas = ((round_up(q_len, 128) // 128 + 1) // 2) * batch * heads
     tiles = (kv_len + 127) // 128
     if ctas >= num_sms:
         return 1
-    want = -(-2 * num_sms // ctas)
-    return max(1, min(want, tiles // 8))
+    return max(1, min(num_sms // ctas, tiles // 8))
 
 
 def attn_from_codes(w: QuantWindow, sm_scale=None, out=None, num_splits=None):
