@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--call-kv", type=int, default=12064,
                     help="keys of the single-call workload (12064 = BASELINE config 1; 30160 = one chunk call)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="launch every kernel from Python instead of replaying "
+                    "one CUDA graph per layer")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -71,8 +73,10 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms from before the warm-up to after the
+    timed region; `summary()` keeps the samples taken between `mark_start()` and `mark_end()` (with
+    0.25 s of slack on both sides, as the sampling period may exceed a short timed region)."""
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -84,15 +88,23 @@ class ClockSampler:
         except Exception:
             self.dev = "0"
         self.proc = None
+        self.t_start = self.t_end = None
+        self.lines = []
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
         return self
+
+    def mark_start(self):
+        self.t_start = time.time()
+
+    def mark_end(self):
+        self.t_end = time.time()
 
     def __exit__(self, *exc):
         self.lines = []
@@ -105,19 +117,34 @@ class ClockSampler:
                 out, _ = self.proc.communicate()
             self.lines = [ln for ln in out.splitlines() if ln.strip()]
 
+    @staticmethod
+    def _stamp(txt):
+        import datetime
+        try:
+            return datetime.datetime.strptime(txt.strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            return None
+
     def summary(self):
+        rows = []
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 10:
+                continue
+            rows.append((self._stamp(parts[0]), parts))
+        if self.t_start is not None and self.t_end is not None:
+            inside = [r for r in rows if r[0] is not None and self.t_start - 0.25 <= r[0] <= self.t_end + 0.25]
+            if inside:
+                rows = inside
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
+        for _t, parts in rows:
             try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
+                sm.append(float(parts[2]))
+                mx = float(parts[3])
             except ValueError:
                 continue
-            for n, val in zip(names, parts[5:9]):
+            for n, val in zip(names, parts[6:10]):
                 if val.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
@@ -192,14 +219,22 @@ def shard_rows(world, rank):
 # ----------------------------------------------------------------------------- our chunk
 class Chunk:
     """Device state of the chunk benchmark: 30 layer caches (memory part resident), per-layer
-    current-chunk q/k/v, the quantizer buffers and the output."""
+    current-chunk q/k/v, the quantizer buffers and the output. With N > 1 the caches are carved from
+    a peer heap mapped by every rank, and the sequence split exchanges over NVLink peer memory."""
 
     def __init__(self, world, rank, device):
-        from lingbot_b200 import kv_cache
+        from lingbot_b200 import kv_cache, split
         self.world, self.rank, self.dev = world, rank, device
         self.r0, self.r1 = shard_rows(world, rank)
+        self.heap = None
+        if world > 1:
+            from lingbot_b200 import peer
+            self.part = split.share_part(LQ, world)
+            self.heap = peer.PeerHeap(kv_cache.heap_bytes(LAYERS, [1, LK, H, D], torch.bfloat16) + (16 << 20), device)
+        else:
+            self.part = LQ
         g = torch.Generator(device=device).manual_seed(1234)
-        self.caches = kv_cache.allocate(LAYERS, [1, LK, H, D], torch.bfloat16, device)
+        self.caches = kv_cache.allocate(LAYERS, [1, LK, H, D], torch.bfloat16, device, heap=self.heap)
         koff = torch.randn(LAYERS, 1, 1, H, D, generator=g, device=device) * 3.0
         for li, c in enumerate(self.caches):
             c["k"][:, :MEM].normal_(generator=g).add_(koff[li])
@@ -211,31 +246,37 @@ class Chunk:
         kv_full = torch.randn(2, LAYERS, 1, LQ, H, D, generator=g, device=device)
         kv_full[0] += koff
         kv_full = kv_full.bfloat16()
-        from lingbot_b200 import split
-        self.part = split.token_part(LQ, world)
-        self.kv_parts = torch.stack([torch.stack([split.pad_share(kv_full[t, li], world, rank)
+        self.kv_parts = torch.stack([torch.stack([split.pad_share(kv_full[t, li], world, rank, self.part)
                                                   for li in range(LAYERS)]) for t in range(2)])   # [2, L, 1, part, H, D]
         del kv_full
         self.out = torch.empty(1, n_loc, H, D, dtype=torch.bfloat16, device=device)
         self.quantizer = kv_cache.WindowQuantizer()
         self.splitter = None
         if world > 1:
-            # N > 1: the chunk's K/V all-gather overlaps the re-quant of the replicated memory part
-            self.splitter = split.SplitAttention(1, H, n_loc, MEM, LQ, device)
+            self.splitter = split.SplitAttention(1, H, n_loc, MEM, LQ, device, self.heap)
             for c in self.caches:
                 self.splitter.memory_changed(c)
+            torch.cuda.synchronize()
+            barrier(world)               # every exchange area zeroed before any rank signals into it
+        self.graphs = None
+
+    def launches_per_call(self):
+        from lingbot_b200 import ops
+        splits = ops.pick_splits(1, H, self.r1 - self.r0, LK)
+        if self.splitter is not None:
+            return self.splitter.launches(splits)
+        return 5 + (1 if splits > 1 else 0)    # block stats, window sums, K/V codes, Q codes, attention
 
     def call(self, layer, q=None, kv_part=None, attn_events=None, out=None):
-        """One (pass, layer): gather the current chunk's K/V (N > 1), write it into the cache,
+        """One (pass, layer): exchange the current chunk's K/V (N > 1), write it into the cache,
         re-quantize the window, quantize Q, attend. Returns the number of our kernel launches."""
         from lingbot_b200 import kv_cache, ops
         c = self.caches[layer]
         q = self.q[layer] if q is None else q
         kv_part = self.kv_parts[:, layer] if kv_part is None else kv_part
-        splits = ops.pick_splits(1, H, self.r1 - self.r0, LK)
         if self.splitter is not None:
             self.splitter(q, c, kv_part[0], kv_part[1], self.out if out is None else out, attn_events=attn_events)
-            return 9 + (1 if splits > 1 else 0)
+            return self.launches_per_call()
         kcur, vcur = kv_part[0], kv_part[1]
         c["k"][:, MEM:LK] = kcur
         c["v"][:, MEM:LK] = vcur
@@ -246,12 +287,38 @@ class Chunk:
         ops.attn_from_codes(w, out=self.out if out is None else out)
         if attn_events is not None:
             attn_events[1].record()
-        return 6 + (1 if splits > 1 else 0)
+        return self.launches_per_call()
+
+    def capture(self, bufs=None):
+        """One CUDA graph per layer (and per input slot of `bufs` = [(q, kv_part, out), ...]): the whole
+        call, with timing events around the attention launch. Returns [(graph, (ev0, ev1)), ...]."""
+        torch.cuda.synchronize()
+        barrier(self.world)
+        graphs = []
+        slots = bufs if bufs is not None else [None]
+        for li in range(LAYERS):
+            for sl in slots:
+                g = torch.cuda.CUDAGraph()
+                ev = (torch.cuda.Event(enable_timing=True, external=True),
+                      torch.cuda.Event(enable_timing=True, external=True))
+                with torch.cuda.graph(g):
+                    if sl is None:
+                        self.call(li, attn_events=ev)
+                    else:
+                        self.call(li, q=sl[0], kv_part=sl[1], out=sl[2], attn_events=ev)
+                graphs.append((g, ev))
+        torch.cuda.synchronize()
+        barrier(self.world)
+        return graphs
 
     def step(self, attn_times=None):
         launches = 0
         for _p in range(PASSES):
             for li in range(LAYERS):
+                if self.graphs is not None:
+                    self.graphs[li][0].replay()
+                    launches += self.launches_per_call()
+                    continue
                 ev = None
                 if attn_times is not None:
                     ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -266,23 +333,28 @@ def run_ours(args, world, rank, local):
     peaks, peak_src = measured_peaks()
     chunk = Chunk(world, rank, dev)
     torch.cuda.synchronize()
-    for _ in range(args.warmup):
-        chunk.step()
-    torch.cuda.synchronize()
-    barrier(world)
+    chunk.step()                         # eager warm-up (allocations, tensor maps, lazy loading)
+    if not args.eager:
+        chunk.graphs = chunk.capture()
     attn_ev = []
     with ClockSampler(dev) as clk:
+        for _ in range(args.warmup):
+            chunk.step()
         torch.cuda.synchronize()
         barrier(world)
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clk.mark_start()
         t0.record()
         launches = 0
         for _ in range(args.steps):
             launches += chunk.step(attn_times=attn_ev)
         t1.record()
         torch.cuda.synchronize()
+        clk.mark_end()
         barrier(world)
     ms = max_over_ranks(t0.elapsed_time(t1), world) / args.steps
+    if chunk.graphs is not None:         # each layer graph's last replay (inside the timed region)
+        attn_ev = [ev for _g, ev in chunk.graphs]
     attn_ms = sum(a.elapsed_time(b) for a, b in attn_ev) / len(attn_ev)
     status = _lib.device_status()
     if status:
@@ -323,6 +395,14 @@ def run_e2e(chunk, args, world):
     h2d += h_kv[0].numel() * 2
     d2h = h_out[0].numel() * 2
 
+    graphs = None
+    if chunk.graphs is not None:
+        for s in range(2):
+            d_q[s].zero_()
+            d_kv[s].zero_()
+            chunk.call(0, q=d_q[s], kv_part=d_kv[s], out=d_out[s])      # eager warm-up of these buffers
+        graphs = chunk.capture([(d_q[s], d_kv[s], d_out[s]) for s in range(2)])
+
     def stage(i):
         s = i % 2
         with torch.cuda.stream(copy):
@@ -339,7 +419,10 @@ def run_e2e(chunk, args, world):
             if i + 1 < n:
                 stage(i + 1)
             main.wait_event(ready[s])
-            chunk.call(i % LAYERS, q=d_q[s], kv_part=d_kv[s], out=d_out[s])
+            if graphs is not None:
+                graphs[(i % LAYERS) * 2 + s][0].replay()
+            else:
+                chunk.call(i % LAYERS, q=d_q[s], kv_part=d_kv[s], out=d_out[s])
             freed[s].record(main)
             h_out[s].copy_(d_out[s], non_blocking=True)
 
@@ -376,17 +459,19 @@ def read_traffic(kernel):
 
 # ----------------------------------------------------------------------------- other workloads
 def _timed(fn, steps, warmup, dev, world):
-    for _ in range(warmup):
-        fn()
-    torch.cuda.synchronize()
-    barrier(world)
     with ClockSampler(dev) as clk:
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clk.mark_start()
         t0.record()
         for _ in range(steps):
             fn()
         t1.record()
         torch.cuda.synchronize()
+        clk.mark_end()
     return max_over_ranks(t0.elapsed_time(t1), world) / steps, clk.summary()
 
 
@@ -424,7 +509,7 @@ def run_call(args, world, rank, local):
     peaks, src = measured_peaks()
     peak = 2.0 * peaks.get("bf16_tflops", 1590.0)
     ach = flops / (attn_ms * 1e-3) / 1e12
-    return dict(tops=flops / (ms * 1e-3) / 1e12, ms=ms, clocks=clocks, launches=7 * args.steps, e2e=None,
+    return dict(tops=flops / (ms * 1e-3) / 1e12, ms=ms, clocks=clocks, launches=5 * args.steps, e2e=None,
                 roofline={"bound": "tensor", "achieved": round(ach, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
                           "frac": round(ach / peak, 4), "traffic": None, "kernel": "attn_fwd_kernel",
                           "peak_source": f"2 x bf16_tflops burst ({src})", "attn_ms_per_call": round(attn_ms, 4)})
@@ -463,10 +548,10 @@ def run_requant(args, world, rank, local):
     alg_bytes = 2 * k.numel() * 2 + 2 * k.numel() + ks.numel() * 4 + nl * H * D * (2 + 4)
     peaks, src = measured_peaks()
     gbs = alg_bytes / (ms * 1e-3) / 1e9
-    return dict(tops=gbs, ms=ms, clocks=clocks, launches=3 * args.steps, e2e=None, unit="GB/s",
+    return dict(tops=gbs, ms=ms, clocks=clocks, launches=2 * args.steps, e2e=None, unit="GB/s",
                 roofline={"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                           "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": None,
-                          "kernel": "quant_k_kernel + quant_vt_kernel", "peak_source": src,
+                          "kernel": "quant_kv_kernel", "peak_source": src,
                           "algorithmic_bytes": alg_bytes})
 
 

@@ -156,6 +156,72 @@ LBQ_API int lbq_splitkv_combine(const float* o_part, const float* ml_part, int n
                         const float* v_scale, int batch, int heads, int q_len, void* out,
                         int64_t so_b, int64_t so_l, int64_t so_h, void* stream);
 
+/* ---------------------------------------------------------------- sequence split over peer memory
+ * The ranks of one node share a "peer heap": a device buffer per rank, mapped into every other
+ * rank's address space through CUDA IPC and carved identically on every rank, so a buffer is named
+ * by its byte offset and rank p's copy lives at peers[p] + offset. `peers` is a device array of
+ * nranks (<= 8) u64 heap bases as mapped in the calling process (its own heap at [rank]). The
+ * exchange area (lbq_exchange_bytes, 256-byte aligned offset `xchg_off`) is zeroed by the caller on
+ * every rank, followed by a barrier, before first use. Waits are bounded by `timeout_ns`; a wait
+ * that gives up records LBQ status 0x201 / 0x202 (lbq_device_status) instead of hanging.
+ * Together these replace the head/token exchange of lingbot/parallel/split_dit.py:366-445 (`_layer`:
+ * the q/k/v head exchange `self.xch(...)`, the cache write in `_attend`, the output send-back),
+ * which needs the head count divisible by the degree (lingbot/parallel/config.py:13-17). */
+
+/* Interprocess handle of the device allocation holding `ptr` (64 bytes to `handle_out`) and the
+ * offset of `ptr` inside it. Synchronous; no stream work. Replaces the CUDA-IPC buffer sharing
+ * behind `self.xch` in lingbot/parallel/split_dit.py (ZEROCOPY path). */
+LBQ_API int lbq_peer_export(const void* ptr, void* handle_out, uint64_t* offset_out);
+
+/* Maps another process's allocation (handle from lbq_peer_export) into this process; *base_out is
+ * the mapped allocation base (add the exported offset to reach the peer's pointer). */
+LBQ_API int lbq_peer_open(const void* handle, void** base_out);
+
+/* Unmaps an allocation base returned by lbq_peer_open. */
+LBQ_API int lbq_peer_close(void* base);
+
+/* Bytes of the exchange area for nranks ranks and batch x heads. */
+LBQ_API int64_t lbq_exchange_bytes(int nranks, int batch, int heads);
+
+/* Per-channel totals (fp64 K sum, max |V|) of this rank's share of the chunk, reduced from its block
+ * statistics in this rank's cache tables (ksum/vamax [B][max_blocks][H][128], rows [row0, row0 +
+ * nb_valid), written by lbq_kv_block_stats), stored into every rank's exchange area, one signal per
+ * CTA. Replaces this rank's part of the window reductions of lingbot/layers/sage_preq.py:47-63,115
+ * (`_v_scale`, `k.mean`) under a sequence split. */
+LBQ_API int lbq_share_totals_push(const double* ksum, const float* vamax, int64_t max_blocks, int row0,
+                          int nb_valid, int batch, int heads, const uint64_t* peers, int nranks, int rank,
+                          int64_t xchg_off, void* stream);
+
+/* Waits for every rank's lbq_share_totals_push of this call, then writes the window totals
+ * tot_ksum = mem_ksum + the shares' sums in rank order and tot_vamax likewise with max ([B*H*128]),
+ * identical on every rank. One per call, after lbq_share_totals_push on the same stream. */
+LBQ_API int lbq_chunk_totals(const uint64_t* peers, int nranks, int rank, int64_t xchg_off, int batch,
+                     int heads, const double* mem_ksum, const float* mem_vamax, double* tot_ksum,
+                     float* tot_vamax, uint64_t timeout_ns, void* stream);
+
+/* Copies this rank's bf16 K/V share (k/v [B, part, H, 128], share_valid valid tokens, nb_part =
+ * part / 64 on every rank) into every rank's cache replica (heap offsets cache_k_off / cache_v_off of
+ * [B][cache_tokens][H][128] bf16 caches, starting at token dst_tok0, a multiple of 64) and the
+ * share's block-statistics rows of this rank's tables into the other ranks' tables (heap offsets
+ * tbl_ksum_off / tbl_vamax_off, [B][tbl_max_blocks][H][128]), then signals the other ranks. Must be
+ * ordered after this call's lbq_chunk_totals (which proves that every rank has finished reading its
+ * cache in the previous call). `ctas` (0 = 148) CTAs stride over the share, bounding how many SMs the
+ * push takes from concurrent kernels; every rank passes the same value, here and to lbq_peer_wait. Replaces the ZEROCOPY K/V write into the peer's buffer and the
+ * kv_cache.write of lingbot/parallel/split_dit.py:371-376,425-431. */
+LBQ_API int lbq_share_push(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h,
+                   const void* v, int64_t sv_b, int64_t sv_l, int64_t sv_h,
+                   int batch, int heads, int share_valid, int nb_part,
+                   const uint64_t* peers, int nranks, int rank, int64_t xchg_off,
+                   int64_t cache_k_off, int64_t cache_v_off, int64_t cache_tokens, int64_t dst_tok0,
+                   int64_t tbl_ksum_off, int64_t tbl_vamax_off, int64_t tbl_max_blocks, int ctas,
+                   void* stream);
+
+/* Waits until every other rank's lbq_share_push of this call has landed in this rank's cache
+ * (this rank's own push is ordered by the caller's streams). Replaces the
+ * `comp[c].wait_event(ev)` on the peer's inbox at lingbot/parallel/split_dit.py:384-386. */
+LBQ_API int lbq_peer_wait(const uint64_t* peers, int nranks, int rank, int64_t xchg_off, int nb_part,
+                  int batch, int heads, int push_ctas, uint64_t timeout_ns, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

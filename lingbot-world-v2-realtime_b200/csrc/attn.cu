@@ -481,12 +481,14 @@ cudaError_t launch_attn(const AttnArgs& a, const CUtensorMap& tm_q, const CUtens
     configured[dev] = true;
   }
   dim3 grid((a.q_pad / 128 + 1) / 2, a.batch * a.heads, a.num_splits);
+  if (cudaError_t e0 = prefer_max_shared<attn_fwd_kernel>(); e0 != cudaSuccess) return e0;
   attn_fwd_kernel<<<grid, kAttnThreads, kAttnSmemBytes, st>>>(tm_q, tm_k, tm_v, a);
   return cudaGetLastError();
 }
 
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st) {
   dim3 grid((a.q_len + 3) / 4, a.batch * a.heads);
+  if (cudaError_t e0 = prefer_max_shared<splitkv_combine_kernel>(); e0 != cudaSuccess) return e0;
   splitkv_combine_kernel<<<grid, 128, 0, st>>>(a);
   return cudaGetLastError();
 }

@@ -176,12 +176,10 @@ int lbq_quant_kv(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const 
   lbq::QuantKArgs ka{static_cast<const __nv_bfloat16*>(k), sk_b, sk_l, sk_h, batch, heads, tok0, seg, seg_valid,
                      seg_pad, kv_len_total, ksum_total, k_codes, k_scale,
                      static_cast<__nv_bfloat16*>(km_out), write_totals};
-  cudaError_t e = lbq::launch_quant_k(ka, st);
-  if (e != cudaSuccess) return cuda_fail(e, "quant_k launch");
   lbq::QuantVArgs va{static_cast<const __nv_bfloat16*>(v), sv_b, sv_l, sv_h, batch, heads, tok0, seg, seg_valid,
                      seg_pad, vamax_total, vt_codes, v_scale, write_totals};
-  e = lbq::launch_quant_vt(va, st);
-  return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "quant_vt launch");
+  cudaError_t e = lbq::launch_quant_kv(ka, va, st);
+  return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "quant_kv launch");
 }
 
 size_t lbq_quant_qkv_workspace(int batch, int heads, int64_t kv_len) {

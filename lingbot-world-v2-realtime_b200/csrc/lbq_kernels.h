@@ -90,15 +90,106 @@ struct CombineArgs {
   int batch, heads, q_len, q_pad, num_splits;
 };
 
+// Exchange area of a sequence split (byte offsets from its start, inside the peer heap).
+namespace xchg {
+constexpr int kMaxRanks = 8;
+constexpr int64_t kFlagsData = 32;    // u32[8]  share_push signals, raised by the producers
+constexpr int64_t kSeenData = 96;     // u32[8]  share signals consumed (local)
+constexpr int64_t kCall = 128;        // u32     calls completed: totals tag - 1 and slot parity (local)
+constexpr int64_t kDone = 132;        // u32     chunk_totals CTAs finished this call (local)
+constexpr int64_t kSlots = 256;       // u64 tagged words [2 parity][ranks][3][B*H*128]
+constexpr int kPushCtas = 148;        // default share_push grid (persistent)
+__host__ __device__ inline int64_t slot_word(uint32_t par, int nranks, int r, int w, int64_t cols) {
+  return ((int64_t(par) * nranks + r) * 3 + w) * cols;
+}
+__host__ __device__ inline int64_t bytes(int nranks, int64_t cols) { return kSlots + 2 * int64_t(nranks) * 3 * cols * 8; }
+__host__ __device__ inline int push_ctas(int units, int ctas) {
+  const int c = ctas > 0 ? ctas : kPushCtas;
+  return units < c ? units : c;
+}
+}  // namespace xchg
+
+struct ShareTotalsArgs {
+  const double* ksum;         // this rank's cache tables [B][max_blocks][H][128]
+  const float* vamax;
+  int64_t max_blocks;
+  int row0, nb_valid;         // the share's rows in the tables
+  int batch, heads;
+  const uint64_t* peers;      // [nranks] heap base of every rank, as mapped in this process
+  int nranks, rank;
+  int64_t xchg_off;
+};
+
+struct ChunkTotalsArgs {
+  const uint64_t* peers;
+  int nranks, rank;
+  int64_t xchg_off;
+  int batch, heads;
+  const double* mem_ksum;     // [B*H*128] totals of the memory part
+  const float* mem_vamax;
+  double* tot_ksum;           // [B*H*128] totals of the window
+  float* tot_vamax;
+  uint64_t timeout_ns;
+  int* status;
+};
+
+struct SharePushArgs {
+  const __nv_bfloat16* k;     // this rank's share [B, part, H, 128]
+  const __nv_bfloat16* v;
+  int64_t sk_b, sk_l, sk_h, sv_b, sv_l, sv_h;
+  int batch, heads;
+  int share_valid, nb_part;   // valid tokens; 64-token blocks of a share (the same on every rank)
+  const uint64_t* peers;
+  int nranks, rank;
+  int64_t xchg_off;
+  int64_t cache_k_off, cache_v_off;     // heap offsets of this layer's cache K / V [B][cache_tokens][H][128]
+  int64_t cache_tokens;
+  int64_t dst_tok0;                     // cache token of the share's first token (multiple of 64)
+  int64_t tbl_ksum_off, tbl_vamax_off;  // heap offsets of this layer's block tables [B][max_blocks][H][128]
+  int64_t tbl_max_blocks;
+  int ctas;                             // grid size (the same on every rank)
+};
+
+struct PeerWaitArgs {
+  const uint64_t* peers;
+  int nranks, rank;
+  int64_t xchg_off;
+  uint32_t per_call;          // share_push CTAs per rank and call
+  uint64_t timeout_ns;
+  int* status;
+};
+
 cudaError_t launch_kv_block_stats(const KvBlockStatsArgs& a, cudaStream_t st);
 cudaError_t launch_kv_window_sums(const KvWindowSumsArgs& a, cudaStream_t st);
 cudaError_t launch_quant_q(const QuantQArgs& a, cudaStream_t st);
-cudaError_t launch_quant_k(const QuantKArgs& a, cudaStream_t st);
-cudaError_t launch_quant_vt(const QuantVArgs& a, cudaStream_t st);
+cudaError_t launch_quant_kv(const QuantKArgs& ka, const QuantVArgs& va, cudaStream_t st);
 cudaError_t launch_attn(const AttnArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                         const CUtensorMap& tm_v, cudaStream_t st);
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st);
+cudaError_t launch_share_totals_push(const ShareTotalsArgs& a, cudaStream_t st);
+cudaError_t launch_chunk_totals(const ChunkTotalsArgs& a, cudaStream_t st);
+cudaError_t launch_share_push(const SharePushArgs& a, cudaStream_t st);
+cudaError_t launch_peer_wait(const PeerWaitArgs& a, cudaStream_t st);
 int* device_status_ptr();
+
+// Sets the largest shared-memory carveout for `Kernel` on the current device (once per device). All
+// kernels of this library prefer it, so an SM never has to drain to change its L1/shared split when
+// kernels of different shared-memory needs run concurrently (the share push beside the quantizers).
+template <auto Kernel>
+inline cudaError_t prefer_max_shared() {
+  static bool done[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!done[dev]) {
+    e = cudaFuncSetAttribute(Kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             int(cudaSharedmemCarveoutMaxShared));
+    if (e != cudaSuccess) return e;
+    done[dev] = true;
+  }
+  return cudaSuccess;
+}
 // Records `code` and a printf-style message as this thread's lbq_last_error(); returns `code`.
 int set_error(int code, const char* fmt, ...);
 

@@ -26,6 +26,8 @@ enum DeviceStatus : int {
   kDevTimeoutS = 0x103,      // softmax: S tile never completed
   kDevTimeoutP = 0x104,      // MMA: P tile never written
   kDevTimeoutO = 0x105,      // O accumulator never completed
+  kDevTimeoutPeerStats = 0x201,  // sequence split: a rank's share statistics never arrived
+  kDevTimeoutPeerData = 0x202,   // sequence split: a rank's K/V share never arrived
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -1,0 +1,276 @@
+// Sequence-split exchange over NVLink peer memory, sm_100a.
+//
+// Every rank of a sequence split holds a replica of the layer KV caches and an exchange area, all
+// inside one "peer heap" (a device buffer that every other rank of the node has mapped through CUDA
+// IPC). All ranks carve the heap identically, so a buffer is named by its byte offset and rank p's
+// copy lives at peers[p] + offset. The kernels below replace the all-reduce of the chunk statistics
+// and the all-gather of the chunk's K/V (lingbot/parallel/split_dit.py:366-445 exchanges heads and
+// tokens through host-staged copies instead):
+//
+//   share_totals_push  per-channel totals (fp64 K sum, max |V|) of this rank's share, from the block
+//                      statistics lbq_kv_block_stats wrote into this rank's cache tables, stored
+//                      into every rank's slot for this rank as tagged 8-byte words.
+//   chunk_totals       waits for every rank's tagged totals and adds the memory totals and the
+//                      shares' in rank order (bit-identical on every rank).
+//   share_push         copies this rank's bf16 K/V share and its block statistics into every rank's
+//                      cache replica and tables, then a signal per CTA.
+//   peer_wait          waits for every other rank's share_push signals.
+//
+// The totals travel as tagged words: each 8-byte store carries 32 data bits and the call's tag (call
+// counter + 1, kept on the device by every rank in lockstep), so the receiver polls the data itself.
+// The share push signals with monotonic u32 counters in the receiver's exchange area, raised with a
+// system-scope release add by one thread per producer CTA after a CTA barrier and a system fence; the
+// receiver keeps how many it has consumed ("seen") in its own area. No host-side epoch is needed, so
+// the launches can be replayed from a CUDA graph. Every wait is bounded (time limit in the arguments)
+// and records a status code instead of hanging. Totals slots are double-buffered by call parity: rank
+// r writes its call-c+1 totals only after it read every rank's call-c totals, which each rank sends
+// after finishing its call c-1 reads, so a slot is never overwritten while it is read.
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "lbq_ptx.cuh"
+#include "lbq_kernels.h"
+
+namespace lbq {
+
+namespace {
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ char* heap(const uint64_t* peers, int p) {
+  return reinterpret_cast<char*>(static_cast<uintptr_t>(peers[p]));
+}
+// Waits until counter `flag` reaches `target` (modular u32 order); false after `timeout_ns`.
+__device__ __forceinline__ bool wait_counter(const uint32_t* flag, uint32_t target, uint64_t timeout_ns) {
+  if (int32_t(ld_acquire_sys(flag) - target) >= 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0; i < LBQ_SPIN_LIMIT; ++i) {
+    __nanosleep(64);
+    if (int32_t(ld_acquire_sys(flag) - target) >= 0) return true;
+    if ((i & 63) == 0 && globaltimer_ns() - t0 > timeout_ns) break;
+  }
+  return false;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ share totals -> every rank
+// One CTA per (32-channel group, head, batch), 256 threads = 32 channels x 8 block groups: per
+// channel, the fp64 sum of the share's block sums and the max of its block maxima (this rank's cache
+// tables, rows [row0, row0 + nb_valid), written by lbq_kv_block_stats). Each rank's slot receives three
+// tagged words per channel (the two halves of the sum and the max), each an 8-byte store of 32 data bits
+// and the call's tag, so the receiver needs no fence or separate signal: a word is complete when its
+// tag is this call's.
+__global__ void __launch_bounds__(256) share_totals_push_kernel(ShareTotalsArgs a) {
+  const int cg = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int c = cg * 32 + (threadIdx.x & 31), g = threadIdx.x >> 5;
+  double s = 0.0;
+  float vm = 0.f;
+#pragma unroll 4
+  for (int blk = g; blk < a.nb_valid; blk += 8) {
+    const int64_t o = ((int64_t(b) * a.max_blocks + a.row0 + blk) * a.heads + h) * 128 + c;
+    s += a.ksum[o];
+    vm = fmaxf(vm, a.vamax[o]);
+  }
+  __shared__ double sh_s[8][32];
+  __shared__ float sh_v[8][32];
+  sh_s[g][threadIdx.x & 31] = s;
+  sh_v[g][threadIdx.x & 31] = vm;
+  __syncthreads();
+  if (g != 0) return;
+  double tot = 0.0;
+  float vmax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    tot += sh_s[i][threadIdx.x];
+    vmax = fmaxf(vmax, sh_v[i][threadIdx.x]);
+  }
+  const char* mine = heap(a.peers, a.rank) + a.xchg_off;
+  const uint32_t call = *reinterpret_cast<const volatile uint32_t*>(mine + xchg::kCall);
+  const uint64_t tag = uint64_t(call + 1u) << 32;
+  const int64_t cols = int64_t(a.batch) * a.heads * 128;
+  const int64_t col = (int64_t(b) * a.heads + h) * 128 + c;
+  const uint64_t w0 = tag | uint32_t(__double2loint(tot));
+  const uint64_t w1 = tag | uint32_t(__double2hiint(tot));
+  const uint64_t w2 = tag | __float_as_uint(vmax);
+  for (int q = 0; q < a.nranks; ++q) {
+    uint64_t* slot = reinterpret_cast<uint64_t*>(heap(a.peers, (a.rank + 1 + q) % a.nranks) + a.xchg_off +
+                                                 xchg::kSlots) +
+                     xchg::slot_word(call & 1u, a.nranks, a.rank, 0, cols) + col;
+    st_relaxed_sys_u64(slot, w0);
+    st_relaxed_sys_u64(slot + cols, w1);
+    st_relaxed_sys_u64(slot + 2 * cols, w2);
+  }
+}
+
+// ------------------------------------------------------------------ window totals of the split window
+// One CTA per (head, batch), one channel per thread: waits for every rank's three tagged words of its
+// channel, then tot = memory totals + the ranks' share totals in rank order (the same sum on every
+// rank). The last CTA to finish advances the call counter (the tag and the slot parity).
+__global__ void __launch_bounds__(128) chunk_totals_kernel(ChunkTotalsArgs a) {
+  const int h = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
+  char* mine = heap(a.peers, a.rank) + a.xchg_off;
+  const uint32_t call = *reinterpret_cast<const volatile uint32_t*>(mine + xchg::kCall);
+  const uint32_t tag = call + 1u;
+  const int64_t cols = int64_t(a.batch) * a.heads * 128;
+  const int64_t col = (int64_t(b) * a.heads + h) * 128 + t;
+  const uint64_t* slots = reinterpret_cast<const uint64_t*>(mine + xchg::kSlots);
+  __shared__ int sh_fail;
+  if (t == 0) sh_fail = 0;
+  __syncthreads();
+  double s = a.mem_ksum[col];
+  float vm = a.mem_vamax[col];
+  bool ok = true;
+  const uint64_t t0 = globaltimer_ns();
+  for (int r = 0; r < a.nranks && ok; ++r) {
+    const uint64_t* w = slots + xchg::slot_word(call & 1u, a.nranks, r, 0, cols) + col;
+    uint64_t v0, v1, v2;
+    for (uint32_t i = 0;; ++i) {
+      v0 = ld_relaxed_sys_u64(w);
+      v1 = ld_relaxed_sys_u64(w + cols);
+      v2 = ld_relaxed_sys_u64(w + 2 * cols);
+      if (uint32_t(v0 >> 32) == tag && uint32_t(v1 >> 32) == tag && uint32_t(v2 >> 32) == tag) break;
+      if (i >= LBQ_SPIN_LIMIT || ((i & 63) == 63 && globaltimer_ns() - t0 > a.timeout_ns)) {
+        ok = false;
+        break;
+      }
+      __nanosleep(32);
+    }
+    if (ok) {
+      s += __hiloint2double(int(uint32_t(v1)), int(uint32_t(v0)));
+      vm = fmaxf(vm, __uint_as_float(uint32_t(v2)));
+    }
+  }
+  if (!ok) {
+    sh_fail = 1;
+    atomicCAS(a.status, 0, kDevTimeoutPeerStats);
+  }
+  __syncthreads();
+  if (sh_fail) return;
+  a.tot_ksum[col] = s;
+  a.tot_vamax[col] = vm;
+  __syncthreads();
+  if (t == 0) {
+    __threadfence();
+    uint32_t* done = reinterpret_cast<uint32_t*>(mine + xchg::kDone);
+    if (atomicAdd(done, 1u) == gridDim.x * gridDim.y - 1) {
+      *reinterpret_cast<uint32_t*>(mine + xchg::kCall) = call + 1u;
+      *done = 0;
+      __threadfence();
+    }
+  }
+}
+
+// ------------------------------------------------------------------ share -> every rank's cache
+// Persistent: `ctas` CTAs stride over the units (64-token block of the share, head,
+// batch). Thread = (row group of 4 rows, 16-byte chunk); a unit's K/V rows are read once into
+// registers and stored to every rank (CTAs start on different ranks), with the block's statistics row (already in
+// this rank's tables) copied to the other ranks' tables. One signal per CTA and peer at the end.
+__global__ void __launch_bounds__(256) share_push_kernel(SharePushArgs a) {
+  const int t = threadIdx.x, c16 = t & 15, rg = t >> 4;
+  const int units = a.nb_part * a.heads * a.batch;
+  const int nb_valid = (a.share_valid + 63) / 64;
+  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    const int blk = u % a.nb_part;
+    const int h = (u / a.nb_part) % a.heads;
+    const int b = u / (a.nb_part * a.heads);
+    if (blk >= nb_valid) continue;
+    uint4 kr[4], vr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t tok = int64_t(blk) * 64 + rg + 16 * i;
+      if (tok < a.share_valid) {
+        kr[i] = *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + tok * a.sk_l + h * a.sk_h + c16 * 8);
+        vr[i] = *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + tok * a.sv_l + h * a.sv_h + c16 * 8);
+      }
+    }
+    const int64_t row = a.dst_tok0 / 64 + blk;
+    const int64_t so = ((int64_t(b) * a.tbl_max_blocks + row) * a.heads + h) * 128 + (t & 127);
+    const char* mine = heap(a.peers, a.rank);
+    double bs = 0.0;
+    float bv = 0.f;
+    if (t < 128) bs = reinterpret_cast<const double*>(mine + a.tbl_ksum_off)[so];
+    else bv = reinterpret_cast<const float*>(mine + a.tbl_vamax_off)[so];
+    for (int q = 0; q < a.nranks; ++q) {
+      const int p = (a.rank + 1 + q + blockIdx.x) % a.nranks;   // CTAs start on different ranks
+      char* base = heap(a.peers, p);
+      __nv_bfloat16* dk = reinterpret_cast<__nv_bfloat16*>(base + a.cache_k_off);
+      __nv_bfloat16* dv = reinterpret_cast<__nv_bfloat16*>(base + a.cache_v_off);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t tok = int64_t(blk) * 64 + rg + 16 * i;
+        if (tok < a.share_valid) {
+          const int64_t o = ((int64_t(b) * a.cache_tokens + a.dst_tok0 + tok) * a.heads + h) * 128 + c16 * 8;
+          *reinterpret_cast<uint4*>(dk + o) = kr[i];
+          *reinterpret_cast<uint4*>(dv + o) = vr[i];
+        }
+      }
+      if (p != a.rank) {
+        if (t < 128) reinterpret_cast<double*>(base + a.tbl_ksum_off)[so] = bs;
+        else reinterpret_cast<float*>(base + a.tbl_vamax_off)[so] = bv;
+      }
+    }
+  }
+  __syncthreads();
+  if (t == 0) {
+    __threadfence_system();
+    for (int q = 0; q + 1 < a.nranks; ++q) {
+      char* dst = heap(a.peers, (a.rank + 1 + q) % a.nranks) + a.xchg_off;
+      red_release_sys_add(reinterpret_cast<uint32_t*>(dst + xchg::kFlagsData) + a.rank, 1u);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ wait for the other ranks' shares
+__global__ void __launch_bounds__(32) peer_wait_kernel(PeerWaitArgs a) {
+  const int t = threadIdx.x;
+  char* mine = heap(a.peers, a.rank) + a.xchg_off;
+  uint32_t* seen = reinterpret_cast<uint32_t*>(mine + xchg::kSeenData);
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(mine + xchg::kFlagsData);
+  if (t < a.nranks && t != a.rank) {
+    const uint32_t target = seen[t] + a.per_call;
+    if (wait_counter(flags + t, target, a.timeout_ns)) {
+      seen[t] = target;
+    } else {
+      atomicCAS(a.status, 0, kDevTimeoutPeerData);
+    }
+  }
+  __threadfence_system();
+}
+
+cudaError_t launch_share_totals_push(const ShareTotalsArgs& a, cudaStream_t st) {
+  if (cudaError_t e0 = prefer_max_shared<share_totals_push_kernel>(); e0 != cudaSuccess) return e0;
+  share_totals_push_kernel<<<dim3(4, a.heads, a.batch), 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t launch_chunk_totals(const ChunkTotalsArgs& a, cudaStream_t st) {
+  if (cudaError_t e0 = prefer_max_shared<chunk_totals_kernel>(); e0 != cudaSuccess) return e0;
+  chunk_totals_kernel<<<dim3(a.heads, a.batch), 128, 0, st>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t launch_share_push(const SharePushArgs& a, cudaStream_t st) {
+  if (cudaError_t e0 = prefer_max_shared<share_push_kernel>(); e0 != cudaSuccess) return e0;
+  share_push_kernel<<<a.ctas, 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t launch_peer_wait(const PeerWaitArgs& a, cudaStream_t st) {
+  if (cudaError_t e0 = prefer_max_shared<peer_wait_kernel>(); e0 != cudaSuccess) return e0;
+  peer_wait_kernel<<<1, 32, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace lbq

@@ -16,8 +16,8 @@
 //   k_scale  f32  [S][B][H][seg_pad/64]
 //   vt_codes e4m3 [S][B][H][128][seg_pad]       (V transposed: keys contiguous per channel)
 //   v_scale  f32  [B][H][128]
-// Tokens past the valid length are stored as code 0 so that the attention kernel's masked keys are
-// finite.
+// Tokens past the valid length, up to the next multiple of 128, are stored as code 0 so that the
+// attention kernel's masked keys are finite; key tiles past that are never read and not written.
 #include <cuda_bf16.h>
 #include <cstdint>
 
@@ -179,34 +179,52 @@ __device__ __forceinline__ float window_mean_bf16(const double* ksum_total, int6
   return __bfloat162float(__float2bfloat16_rn(__double2float_rn(mean)));
 }
 
-// ------------------------------------------------------------------ K quantizer
-// One CTA per (64-token block of this segment, head, batch). 128 threads: thread t handles the
-// 16-byte chunk (t & 15) of rows (t >> 4) + 8*i.
-__global__ void __launch_bounds__(128) quant_k_kernel(QuantKArgs a) {
-  const int blk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int t = threadIdx.x, c16 = t & 15, rg = t >> 4;
+// ------------------------------------------------------------------ K/V quantizer (one launch)
+// One CTA of 256 threads per (128-token tile of this segment, head, batch) and tensor: even
+// blockIdx.x = K tile x/2, odd = V tile x/2, so the K and V halves of the work stream through the
+// GPU together.
+//
+// K: the two 64-token blocks of the tile go to the two halves of the CTA; in a half, thread t handles
+// the 16-byte chunk (t & 15) of rows (t >> 4) + 8*i of its block. Codes RNE((k - km) * fl(fl(1/amax)
+// * 127)), scale amax / 127 per block.
+//
+// V: the bf16 tile [128 tokens][128 channels] is staged in shared memory with coalesced 16-byte loads
+// (row pitch 272 bytes, so the column reads below are conflict-free); then thread t takes the channel
+// pair (2*(t & 63), +1) over 32 tokens (32*(t >> 6) ...), converts to e4m3 and writes, per channel,
+// 32 consecutive key bytes of the transposed codes [channel][key].
+constexpr int kVtPitch = 272;   // bytes per staged token row
+
+struct QuantKvShared {
+  union {
+    uint8_t v[128 * kVtPitch];
+    float km[128];
+  };
+  float recp[128];
+  float red[8];
+};
+
+__device__ __forceinline__ void quant_k_tile(const QuantKArgs& a, QuantKvShared& sh, int tile, int h, int b) {
+  const int half = threadIdx.x >> 7, t = threadIdx.x & 127, c16 = t & 15, rg = t >> 4;
+  const int blk = tile * 2 + half;
   const int64_t bh = int64_t(b) * a.heads + h;
-  __shared__ float sh_km[128];
-  __shared__ float sh_red[4];
-  {
+  if (half == 0) {
     const float km = window_mean_bf16(a.ksum_total, bh * 128 + t, a.kv_len_total);
-    sh_km[t] = km;
-    if (a.km_out != nullptr && blk == 0 && a.write_km) a.km_out[bh * 128 + t] = __float2bfloat16_rn(km);
+    sh.km[t] = km;
+    if (a.km_out != nullptr && tile == 0 && a.write_km) a.km_out[bh * 128 + t] = __float2bfloat16_rn(km);
   }
-  __syncthreads();
-  float km[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) km[j] = sh_km[c16 * 8 + j];
   uint4 raw[8];
-  float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const int r = rg + 8 * i;
-    const int64_t tok = int64_t(blk) * 64 + r;      // token index inside this segment
+    const int64_t tok = int64_t(blk) * 64 + rg + 8 * i;      // token index inside this segment
     raw[i] = tok < a.seg_valid
                  ? *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + (a.tok0 + tok) * a.sk_l + h * a.sk_h + c16 * 8)
                  : make_uint4(0u, 0u, 0u, 0u);
   }
+  __syncthreads();
+  float km[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) km[j] = sh.km[c16 * 8 + j];
+  float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int64_t tok = int64_t(blk) * 64 + rg + 8 * i;
@@ -218,9 +236,10 @@ __global__ void __launch_bounds__(128) quant_k_kernel(QuantKArgs a) {
     }
   }
   amax = warp_max(amax);
-  if ((t & 31) == 0) sh_red[t >> 5] = amax;
+  if ((t & 31) == 0) sh.red[half * 4 + (t >> 5)] = amax;
   __syncthreads();
-  amax = fmaxf(fmaxf(fmaxf(sh_red[0], sh_red[1]), fmaxf(sh_red[2], sh_red[3])), 1e-7f);
+  const float* red = sh.red + half * 4;
+  amax = fmaxf(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])), 1e-7f);
   const float inv = __fmul_rn(__frcp_rn(amax), 127.f);
   const int64_t seg_bh = (int64_t(a.seg) * a.batch + b) * a.heads + h;
   if (t == 0) a.k_scale[seg_bh * (a.seg_pad / 64) + blk] = __fdiv_rn(amax, 127.f);
@@ -240,23 +259,12 @@ __global__ void __launch_bounds__(128) quant_k_kernel(QuantKArgs a) {
   }
 }
 
-// ------------------------------------------------------------------ V quantizer (transposing)
-// One CTA per (128-token tile of this segment, head, batch), 256 threads. The bf16 tile
-// [128 tokens][128 channels] is staged in shared memory with coalesced 16-byte loads (row pitch
-// 272 bytes, so the column reads below are conflict-free); then thread t takes the channel pair
-// (2*(t & 63), +1) over 32 tokens (32*(t >> 6) ...), converts to e4m3 and writes, per channel,
-// 32 consecutive key bytes of the transposed codes [channel][key].
-constexpr int kVtPitch = 272;   // bytes per staged token row
-
-__global__ void __launch_bounds__(256) quant_vt_kernel(QuantVArgs a) {
-  const int tile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+__device__ __forceinline__ void quant_v_tile(const QuantVArgs& a, QuantKvShared& sh, int tile, int h, int b) {
   const int t = threadIdx.x;
   const int64_t bh = int64_t(b) * a.heads + h;
-  __shared__ __align__(16) uint8_t sh_v[128 * kVtPitch];
-  __shared__ float sh_recp[128];
   if (t < 128) {
     const float amax = a.vamax_total[bh * 128 + t];
-    sh_recp[t] = __fmul_rn(__frcp_rn(amax), 2.25f);
+    sh.recp[t] = __fmul_rn(__frcp_rn(amax), 2.25f);
     if (tile == 0 && a.write_scale) a.v_scale[bh * 128 + t] = __fdiv_rn(amax, 2.25f);
   }
 #pragma unroll
@@ -267,11 +275,11 @@ __global__ void __launch_bounds__(256) quant_vt_kernel(QuantVArgs a) {
     const uint4 raw = tok < a.seg_valid
                           ? *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + (a.tok0 + tok) * a.sv_l + h * a.sv_h + c16 * 8)
                           : make_uint4(0u, 0u, 0u, 0u);
-    *reinterpret_cast<uint4*>(&sh_v[r * kVtPitch + c16 * 16]) = raw;
+    *reinterpret_cast<uint4*>(&sh.v[r * kVtPitch + c16 * 16]) = raw;
   }
   __syncthreads();
   const int cp = t & 63, tq = t >> 6;
-  const float r0 = sh_recp[2 * cp], r1 = sh_recp[2 * cp + 1];
+  const float r0 = sh.recp[2 * cp], r1 = sh.recp[2 * cp + 1];
   uint32_t w0[8], w1[8];                             // channel 2cp / 2cp+1: 32 key bytes each
 #pragma unroll
   for (int k4 = 0; k4 < 8; ++k4) {
@@ -279,7 +287,7 @@ __global__ void __launch_bounds__(256) quant_vt_kernel(QuantVArgs a) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int r = tq * 32 + 4 * k4 + e;
-      const uint32_t pair = *reinterpret_cast<const uint32_t*>(&sh_v[r * kVtPitch + cp * 4]);
+      const uint32_t pair = *reinterpret_cast<const uint32_t*>(&sh.v[r * kVtPitch + cp * 4]);
       lo[e] = fminf(fmaxf(__fmul_rn(__uint_as_float(pair << 16), r0), -2.25f), 2.25f);
       hi[e] = fminf(fmaxf(__fmul_rn(__uint_as_float(pair & 0xffff0000u), r1), -2.25f), 2.25f);
     }
@@ -297,30 +305,38 @@ __global__ void __launch_bounds__(256) quant_vt_kernel(QuantVArgs a) {
   d1[1] = make_uint4(w1[4], w1[5], w1[6], w1[7]);
 }
 
+__global__ void __launch_bounds__(256) quant_kv_kernel(QuantKArgs ka, QuantVArgs va) {
+  __shared__ __align__(16) QuantKvShared sh;
+  const int tile = blockIdx.x >> 1, h = blockIdx.y, b = blockIdx.z;
+  if (blockIdx.x & 1) quant_v_tile(va, sh, tile, h, b);
+  else quant_k_tile(ka, sh, tile, h, b);
+}
+
 // ------------------------------------------------------------------ launchers
 cudaError_t launch_kv_block_stats(const KvBlockStatsArgs& a, cudaStream_t st) {
   dim3 grid(a.blk_end - a.blk_begin, a.heads, a.batch);
+  if (cudaError_t e0 = prefer_max_shared<kv_block_stats_kernel>(); e0 != cudaSuccess) return e0;
   kv_block_stats_kernel<<<grid, 128, 0, st>>>(a);
   return cudaGetLastError();
 }
 cudaError_t launch_kv_window_sums(const KvWindowSumsArgs& a, cudaStream_t st) {
   dim3 grid(4, a.heads, a.batch);
+  if (cudaError_t e0 = prefer_max_shared<kv_window_sums_kernel>(); e0 != cudaSuccess) return e0;
   kv_window_sums_kernel<<<grid, 256, 0, st>>>(a);
   return cudaGetLastError();
 }
 cudaError_t launch_quant_q(const QuantQArgs& a, cudaStream_t st) {
   dim3 grid(a.q_pad / 128, a.heads, a.batch);
+  if (cudaError_t e0 = prefer_max_shared<quant_q_kernel>(); e0 != cudaSuccess) return e0;
   quant_q_kernel<<<grid, 256, 0, st>>>(a);
   return cudaGetLastError();
 }
-cudaError_t launch_quant_k(const QuantKArgs& a, cudaStream_t st) {
-  dim3 grid(a.seg_pad / 64, a.heads, a.batch);
-  quant_k_kernel<<<grid, 128, 0, st>>>(a);
-  return cudaGetLastError();
-}
-cudaError_t launch_quant_vt(const QuantVArgs& a, cudaStream_t st) {
-  dim3 grid(a.seg_pad / 128, a.heads, a.batch);
-  quant_vt_kernel<<<grid, 256, 0, st>>>(a);
+// The grid stops at the last 128-key tile holding valid tokens: a short last segment (the chunk of a
+// sequence split) does not pay for the padding of its seg_pad, which the attention never reads.
+cudaError_t launch_quant_kv(const QuantKArgs& ka, const QuantVArgs& va, cudaStream_t st) {
+  dim3 grid((ka.seg_valid + 127) / 128 * 2, ka.heads, ka.batch);
+  if (cudaError_t e0 = prefer_max_shared<quant_kv_kernel>(); e0 != cudaSuccess) return e0;
+  quant_kv_kernel<<<grid, 256, 0, st>>>(ka, va);
   return cudaGetLastError();
 }
 

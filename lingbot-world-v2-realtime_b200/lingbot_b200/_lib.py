@@ -11,6 +11,7 @@ _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "liblbq.so")
 
 _i32, _i64, _f32, _vp, _sz = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
+_u64 = ctypes.c_uint64
 
 # name -> (restype, argtypes)
 SIGNATURES = {
@@ -33,6 +34,15 @@ SIGNATURES = {
     "lbq_attn_fwd": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _f32, _vp, _i64,
                             _i64, _i64, _i32, _vp, _vp, ctypes.POINTER(_i32), _vp]),
     "lbq_splitkv_combine": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i32, _vp, _i64, _i64, _i64, _vp]),
+    "lbq_peer_export": (_i32, [_vp, _vp, ctypes.POINTER(ctypes.c_uint64)]),
+    "lbq_peer_open": (_i32, [_vp, ctypes.POINTER(_vp)]),
+    "lbq_peer_close": (_i32, [_vp]),
+    "lbq_exchange_bytes": (_i64, [_i32, _i32, _i32]),
+    "lbq_share_totals_push": (_i32, [_vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i32, _i32, _i64, _vp]),
+    "lbq_chunk_totals": (_i32, [_vp, _i32, _i32, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _u64, _vp]),
+    "lbq_share_push": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _i32, _i32,
+                              _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp]),
+    "lbq_peer_wait": (_i32, [_vp, _i32, _i32, _i64, _i32, _i32, _i32, _i32, _u64, _vp]),
 }
 
 _lock = threading.Lock()

@@ -10,7 +10,7 @@ PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(ROOT, "csrc")
 LIB = os.path.join(PKG_DIR, "liblbq.so")
-SOURCES = ["quant.cu", "attn.cu", "capi.cu", "noalloc.cu"]
+SOURCES = ["quant.cu", "attn.cu", "capi.cu", "noalloc.cu", "peer.cu", "capi_peer.cu"]
 HEADERS = ["lbq_ptx.cuh", "lbq_kernels.h", os.path.join("..", "..", "include", "lbq.h")]
 
 

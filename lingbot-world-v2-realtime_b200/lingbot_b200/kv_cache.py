@@ -26,14 +26,34 @@ def _stats_tables(shape, device):
             torch.zeros(b, nb, h, d, dtype=torch.float32, device=device))
 
 
-def allocate(num_layers, shape, dtype, device):
-    """One cache dict per layer; `shape` is [batch, window tokens, heads, head_dim] (kv_cache.py:11-20)."""
+def heap_bytes(num_layers, shape, dtype):
+    """Peer-heap bytes that `allocate(num_layers, shape, dtype, device, heap)` carves (K, V and the
+    block tables of every layer, each at a 256-byte aligned offset)."""
+    b, kv_size, h, d = shape
+    nb = (kv_size + BLK - 1) // BLK
+    esz = torch.empty((), dtype=dtype).element_size()
+    up = lambda x: (x + 255) // 256 * 256  # noqa: E731
+    return num_layers * (2 * up(b * kv_size * h * d * esz) + up(b * nb * h * d * 8) + up(b * nb * h * d * 4))
+
+
+def allocate(num_layers, shape, dtype, device, heap=None):
+    """One cache dict per layer; `shape` is [batch, window tokens, heads, head_dim] (kv_cache.py:11-20).
+    With a `peer.PeerHeap`, K, V and the block tables are carved from it (zeroed) so that the other
+    ranks of a sequence split can write the current chunk straight into this rank's replica."""
     caches = []
     for _ in range(num_layers):
-        ksum, vamax = _stats_tables(shape, device)
+        if heap is None:
+            ksum, vamax = _stats_tables(shape, device)
+            k = torch.zeros(shape, dtype=dtype, device=device)
+            v = torch.zeros(shape, dtype=dtype, device=device)
+        else:
+            b, kv_size, h, d = shape
+            nb = (kv_size + BLK - 1) // BLK
+            k, v = heap.carve(shape, dtype), heap.carve(shape, dtype)
+            ksum, vamax = heap.carve((b, nb, h, d), torch.float64), heap.carve((b, nb, h, d), torch.float32)
         caches.append({
-            'k': torch.zeros(shape, dtype=dtype, device=device),
-            'v': torch.zeros(shape, dtype=dtype, device=device),
+            'k': k,
+            'v': v,
             'global_end_index': torch.tensor([0], dtype=torch.long, device=device),
             'local_end_index': torch.tensor([0], dtype=torch.long, device=device),
             'global_end_int': 0,
