@@ -230,7 +230,8 @@ class Chunk:
         if world > 1:
             from lingbot_b200 import peer
             self.part = split.share_part(LQ, world)
-            self.heap = peer.PeerHeap(kv_cache.heap_bytes(LAYERS, [1, LK, H, D], torch.bfloat16) + (16 << 20), device)
+            self.heap = peer.PeerHeap(kv_cache.heap_bytes(LAYERS, [1, LK, H, D], torch.bfloat16)
+                                      + split.SplitAttention.heap_bytes(1, H, MEM, LQ, world), device)
         else:
             self.part = LQ
         g = torch.Generator(device=device).manual_seed(1234)
@@ -260,23 +261,26 @@ class Chunk:
             barrier(world)               # every exchange area zeroed before any rank signals into it
         self.graphs = None
 
-    def launches_per_call(self):
+    def launches_per_call(self, persist=True):
         from lingbot_b200 import ops
         splits = ops.pick_splits(1, H, self.r1 - self.r0, LK)
         if self.splitter is not None:
-            return self.splitter.launches(splits)
+            return self.splitter.launches(splits, persist)
         return 5 + (1 if splits > 1 else 0)    # block stats, window sums, K/V codes, Q codes, attention
 
-    def call(self, layer, q=None, kv_part=None, attn_events=None, out=None):
+    def call(self, layer, q=None, kv_part=None, attn_events=None, out=None, persist=True):
         """One (pass, layer): exchange the current chunk's K/V (N > 1), write it into the cache,
-        re-quantize the window, quantize Q, attend. Returns the number of our kernel launches."""
+        re-quantize the window, quantize Q, attend. Returns the number of our kernel launches.
+        persist=False (the denoise passes, N > 1): the chunk's bf16 K/V are not replicated into the
+        other ranks' caches, since the next pass of the chunk overwrites them before any read."""
         from lingbot_b200 import kv_cache, ops
         c = self.caches[layer]
         q = self.q[layer] if q is None else q
         kv_part = self.kv_parts[:, layer] if kv_part is None else kv_part
         if self.splitter is not None:
-            self.splitter(q, c, kv_part[0], kv_part[1], self.out if out is None else out, attn_events=attn_events)
-            return self.launches_per_call()
+            self.splitter(q, c, kv_part[0], kv_part[1], self.out if out is None else out, attn_events=attn_events,
+                          persist=persist)
+            return self.launches_per_call(persist)
         kcur, vcur = kv_part[0], kv_part[1]
         c["k"][:, MEM:LK] = kcur
         c["v"][:, MEM:LK] = vcur
@@ -290,40 +294,44 @@ class Chunk:
         return self.launches_per_call()
 
     def capture(self, bufs=None):
-        """One CUDA graph per layer (and per input slot of `bufs` = [(q, kv_part, out), ...]): the whole
-        call, with timing events around the attention launch. Returns [(graph, (ev0, ev1)), ...]."""
+        """CUDA graphs of the whole call, with timing events around the attention launch: per layer, per
+        input slot of `bufs` = [(q, kv_part, out), ...], and per `persist` (the memory-write pass
+        persists its K/V, the denoise passes do not). Returns {(layer, slot, persist): (graph, events)}."""
         torch.cuda.synchronize()
         barrier(self.world)
-        graphs = []
+        graphs = {}
         slots = bufs if bufs is not None else [None]
-        for li in range(LAYERS):
-            for sl in slots:
-                g = torch.cuda.CUDAGraph()
-                ev = (torch.cuda.Event(enable_timing=True, external=True),
-                      torch.cuda.Event(enable_timing=True, external=True))
-                with torch.cuda.graph(g):
-                    if sl is None:
-                        self.call(li, attn_events=ev)
-                    else:
-                        self.call(li, q=sl[0], kv_part=sl[1], out=sl[2], attn_events=ev)
-                graphs.append((g, ev))
+        for persist in (False, True):
+            for li in range(LAYERS):
+                for si, sl in enumerate(slots):
+                    g = torch.cuda.CUDAGraph()
+                    ev = (torch.cuda.Event(enable_timing=True, external=True),
+                          torch.cuda.Event(enable_timing=True, external=True))
+                    with torch.cuda.graph(g):
+                        if sl is None:
+                            self.call(li, attn_events=ev, persist=persist)
+                        else:
+                            self.call(li, q=sl[0], kv_part=sl[1], out=sl[2], attn_events=ev, persist=persist)
+                    graphs[(li, si, persist)] = (g, ev)
         torch.cuda.synchronize()
         barrier(self.world)
         return graphs
 
     def step(self, attn_times=None):
+        """One chunk: PASSES - 1 denoise passes and the memory-write pass (which persists its K/V)."""
         launches = 0
-        for _p in range(PASSES):
+        for p in range(PASSES):
+            persist = p == PASSES - 1
             for li in range(LAYERS):
                 if self.graphs is not None:
-                    self.graphs[li][0].replay()
-                    launches += self.launches_per_call()
+                    self.graphs[(li, 0, persist)][0].replay()
+                    launches += self.launches_per_call(persist)
                     continue
                 ev = None
                 if attn_times is not None:
                     ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                     attn_times.append(ev)
-                launches += self.call(li, attn_events=ev)
+                launches += self.call(li, attn_events=ev, persist=persist)
         return launches
 
 
@@ -354,7 +362,7 @@ def run_ours(args, world, rank, local):
         barrier(world)
     ms = max_over_ranks(t0.elapsed_time(t1), world) / args.steps
     if chunk.graphs is not None:         # each layer graph's last replay (inside the timed region)
-        attn_ev = [ev for _g, ev in chunk.graphs]
+        attn_ev = [ev for _g, ev in chunk.graphs.values()]
     attn_ms = sum(a.elapsed_time(b) for a, b in attn_ev) / len(attn_ev)
     status = _lib.device_status()
     if status:
@@ -419,10 +427,11 @@ def run_e2e(chunk, args, world):
             if i + 1 < n:
                 stage(i + 1)
             main.wait_event(ready[s])
+            persist = i // LAYERS == PASSES - 1
             if graphs is not None:
-                graphs[(i % LAYERS) * 2 + s][0].replay()
+                graphs[(i % LAYERS, s, persist)][0].replay()
             else:
-                chunk.call(i % LAYERS, q=d_q[s], kv_part=d_kv[s], out=d_out[s])
+                chunk.call(i % LAYERS, q=d_q[s], kv_part=d_kv[s], out=d_out[s], persist=persist)
             freed[s].record(main)
             h_out[s].copy_(d_out[s], non_blocking=True)
 

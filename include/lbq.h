@@ -203,7 +203,7 @@ LBQ_API int lbq_chunk_totals(const uint64_t* peers, int nranks, int rank, int64_
  * part / 64 on every rank) into every rank's cache replica (heap offsets cache_k_off / cache_v_off of
  * [B][cache_tokens][H][128] bf16 caches, starting at token dst_tok0, a multiple of 64) and the
  * share's block-statistics rows of this rank's tables into the other ranks' tables (heap offsets
- * tbl_ksum_off / tbl_vamax_off, [B][tbl_max_blocks][H][128]), then signals the other ranks. Must be
+ * tbl_ksum_off / tbl_vamax_off, [B][tbl_max_blocks][H][128]), then signals the other ranks once. Must be
  * ordered after this call's lbq_chunk_totals (which proves that every rank has finished reading its
  * cache in the previous call). `ctas` (0 = 148) CTAs stride over the share, bounding how many SMs the
  * push takes from concurrent kernels; every rank passes the same value, here and to lbq_peer_wait. Replaces the ZEROCOPY K/V write into the peer's buffer and the
@@ -216,11 +216,30 @@ LBQ_API int lbq_share_push(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk
                    int64_t tbl_ksum_off, int64_t tbl_vamax_off, int64_t tbl_max_blocks, int ctas,
                    void* stream);
 
-/* Waits until every other rank's lbq_share_push of this call has landed in this rank's cache
- * (this rank's own push is ordered by the caller's streams). Replaces the
- * `comp[c].wait_event(ev)` on the peer's inbox at lingbot/parallel/split_dit.py:384-386. */
-LBQ_API int lbq_peer_wait(const uint64_t* peers, int nranks, int rank, int64_t xchg_off, int nb_part,
-                  int batch, int heads, int push_ctas, uint64_t timeout_ns, void* stream);
+/* Quantizes this rank's share of the chunk (k/v [B, part, H, 128], share_valid valid tokens, chunk
+ * tokens [lo, lo + part) with lo and part multiples of 128) with the window totals from
+ * lbq_chunk_totals — the same codes lbq_quant_kv gives for those tokens of segment `seg` — into this
+ * rank's code buffers (k_codes / k_scale / vt_codes, inside the peer heap at the same offsets on every
+ * rank), then copies them into every other rank's buffers with `ctas` CTAs (0 = 32; the same on every
+ * rank) and signals the other ranks once. km_out / v_scale (this rank only) are written when
+ * write_totals != 0. Must be
+ * ordered after this call's lbq_chunk_totals (every rank has then finished its previous attention,
+ * the last reader of the code buffers). Replaces the per-rank quantization of the gathered chunk
+ * (sage_preq.py:115-124 after the exchange of lingbot/parallel/split_dit.py:371-386). */
+LBQ_API int lbq_share_quant_push(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h,
+                         const void* v, int64_t sv_b, int64_t sv_l, int64_t sv_h, int batch, int heads,
+                         int lo, int share_valid, int part, int seg, int num_segments, int seg_len,
+                         int64_t kv_len_total, const double* ksum_total, const float* vamax_total,
+                         int8_t* k_codes, float* k_scale, uint8_t* vt_codes, void* km_out, float* v_scale,
+                         int write_totals, const uint64_t* peers, int nranks, int rank, int64_t xchg_off,
+                         int ctas, void* stream);
+
+/* Waits until every other rank's pushes of this call have landed in this rank's buffers: `signals`
+ * (1 or 2) = the push launches every rank makes per call (lbq_share_quant_push, plus lbq_share_push
+ * when the call persists its K/V); this rank's own pushes are ordered by the caller's streams.
+ * Replaces the `comp[c].wait_event(ev)` on the peer's inbox at lingbot/parallel/split_dit.py:384-386. */
+LBQ_API int lbq_peer_wait(const uint64_t* peers, int nranks, int rank, int64_t xchg_off, int signals,
+                  uint64_t timeout_ns, void* stream);
 
 #ifdef __cplusplus
 }

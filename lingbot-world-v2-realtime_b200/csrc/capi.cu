@@ -178,7 +178,7 @@ int lbq_quant_kv(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const 
                      static_cast<__nv_bfloat16*>(km_out), write_totals};
   lbq::QuantVArgs va{static_cast<const __nv_bfloat16*>(v), sv_b, sv_l, sv_h, batch, heads, tok0, seg, seg_valid,
                      seg_pad, vamax_total, vt_codes, v_scale, write_totals};
-  cudaError_t e = lbq::launch_quant_kv(ka, va, st);
+  cudaError_t e = lbq::launch_quant_kv(ka, va, 0, (seg_valid + 127) / 128, st);
   return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "quant_kv launch");
 }
 

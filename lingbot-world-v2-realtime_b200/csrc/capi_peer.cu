@@ -155,15 +155,59 @@ int lbq_share_push(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, cons
   return e == cudaSuccess ? LBQ_OK : set_error(LBQ_ERR_CUDA, "share_push launch: %s", cudaGetErrorString(e));
 }
 
-int lbq_peer_wait(const uint64_t* peers, int nranks, int rank, int64_t xchg_off, int nb_part, int batch, int heads,
-                  int push_ctas, uint64_t timeout_ns, void* stream) {
+int lbq_share_quant_push(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,
+                         int64_t sv_l, int64_t sv_h, int batch, int heads, int lo, int share_valid, int part, int seg,
+                         int num_segments, int seg_len, int64_t kv_len_total, const double* ksum_total,
+                         const float* vamax_total, int8_t* k_codes, float* k_scale, uint8_t* vt_codes, void* km_out,
+                         float* v_scale, int write_totals, const uint64_t* peers, int nranks, int rank,
+                         int64_t xchg_off, int ctas, void* stream) {
   int r;
-  if ((r = check_group(peers, nranks, rank, xchg_off)) || (r = check_dims(batch, heads, nb_part))) return r;
-  if (push_ctas < 0 || push_ctas > 65535) return set_error(LBQ_ERR_ARG, "push_ctas %d outside [0, 65535]", push_ctas);
+  if ((r = check_share(k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h)) || (r = check_group(peers, nranks, rank, xchg_off)) ||
+      (r = check_dims(batch, heads, 1)))
+    return r;
+  if (!ksum_total || !vamax_total || !k_codes || !k_scale || !vt_codes)
+    return set_error(LBQ_ERR_ARG, "totals and code buffers must be non-null");
+  if (!aligned16(k_codes) || !aligned16(vt_codes)) return set_error(LBQ_ERR_ALIGN, "code buffers not 16-byte aligned");
+  if (write_totals && v_scale == nullptr) return set_error(LBQ_ERR_ARG, "v_scale is null");
+  if (part <= 0 || part % 128 || lo < 0 || lo % 128)
+    return set_error(LBQ_ERR_ARG, "share start %d and size %d must be multiples of 128", lo, part);
+  if (share_valid < 0 || share_valid > part) return set_error(LBQ_ERR_ARG, "share_valid %d not in [0, %d]", share_valid, part);
+  if (num_segments <= 0 || seg < 0 || seg >= num_segments || seg_len <= 0)
+    return set_error(LBQ_ERR_ARG, "segment %d of %d (%d tokens)", seg, num_segments, seg_len);
+  if (num_segments > 1 && seg_len % 64) return set_error(LBQ_ERR_ARG, "seg_len %d must be a multiple of 64", seg_len);
+  if (int64_t(lo) + share_valid > seg_len)
+    return set_error(LBQ_ERR_ARG, "share [%d, %d) past the %d-token segment", lo, lo + share_valid, seg_len);
+  if (kv_len_total <= 0) return set_error(LBQ_ERR_ARG, "kv_len_total must be positive");
+  if (ctas < 0 || ctas > 65535) return set_error(LBQ_ERR_ARG, "ctas %d outside [0, 65535]", ctas);
+  const int seg_pad = int((int64_t(seg_len) + 127) / 128 * 128);
+  const int tile0 = lo / 128;
+  int tile_end = (lo + share_valid + 127) / 128;
+  if (tile_end > seg_pad / 128) tile_end = seg_pad / 128;
+  if (share_valid == 0) tile_end = tile0;
+  const int64_t tok0 = -int64_t(lo);   // segment token t is share token t - lo
+  lbq::QuantKArgs ka{static_cast<const __nv_bfloat16*>(k), sk_b, sk_l, sk_h, batch, heads, tok0, seg, lo + share_valid,
+                     seg_pad, kv_len_total, ksum_total, k_codes, k_scale, static_cast<__nv_bfloat16*>(km_out),
+                     write_totals};
+  lbq::QuantVArgs va{static_cast<const __nv_bfloat16*>(v), sv_b, sv_l, sv_h, batch, heads, tok0, seg, lo + share_valid,
+                     seg_pad, vamax_total, vt_codes, v_scale, write_totals};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = lbq::launch_quant_kv(ka, va, tile0, tile_end - tile0, st);
+  if (e != cudaSuccess) return set_error(LBQ_ERR_CUDA, "share quant launch: %s", cudaGetErrorString(e));
+  if (nranks == 1) return LBQ_OK;
+  lbq::CodePushArgs ca{k_codes, k_scale, vt_codes, batch, heads, seg, seg_pad, lo, (tile_end - tile0) * 128,
+                       peers, nranks, rank, xchg_off};
+  e = lbq::launch_code_push(ca, ctas > 0 ? ctas : 32, st);
+  return e == cudaSuccess ? LBQ_OK : set_error(LBQ_ERR_CUDA, "code push launch: %s", cudaGetErrorString(e));
+}
+
+int lbq_peer_wait(const uint64_t* peers, int nranks, int rank, int64_t xchg_off, int signals, uint64_t timeout_ns,
+                  void* stream) {
+  int r;
+  if ((r = check_group(peers, nranks, rank, xchg_off))) return r;
+  if (signals < 1 || signals > 2) return set_error(LBQ_ERR_ARG, "signals %d not in [1, 2]", signals);
   int* status = lbq::device_status_ptr();
   if (status == nullptr) return set_error(LBQ_ERR_CUDA, "device status word unavailable");
-  lbq::PeerWaitArgs a{peers, nranks, rank, xchg_off,
-                      uint32_t(lbq::xchg::push_ctas(nb_part * heads * batch, push_ctas)), timeout_ns, status};
+  lbq::PeerWaitArgs a{peers, nranks, rank, xchg_off, uint32_t(signals), timeout_ns, status};
   cudaError_t e = lbq::launch_peer_wait(a, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LBQ_OK : set_error(LBQ_ERR_CUDA, "peer_wait launch: %s", cudaGetErrorString(e));
 }

@@ -97,6 +97,8 @@ constexpr int64_t kFlagsData = 32;    // u32[8]  share_push signals, raised by t
 constexpr int64_t kSeenData = 96;     // u32[8]  share signals consumed (local)
 constexpr int64_t kCall = 128;        // u32     calls completed: totals tag - 1 and slot parity (local)
 constexpr int64_t kDone = 132;        // u32     chunk_totals CTAs finished this call (local)
+constexpr int64_t kDonePush = 136;    // u32     share_push CTAs finished this launch (local)
+constexpr int64_t kDoneQuant = 140;   // u32     share_quant_push CTAs finished this launch (local)
 constexpr int64_t kSlots = 256;       // u64 tagged words [2 parity][ranks][3][B*H*128]
 constexpr int kPushCtas = 148;        // default share_push grid (persistent)
 __host__ __device__ inline int64_t slot_word(uint32_t par, int nranks, int r, int w, int64_t cols) {
@@ -150,11 +152,25 @@ struct SharePushArgs {
   int ctas;                             // grid size (the same on every rank)
 };
 
+// Copy of this rank's share of the chunk-segment codes into every other rank's code buffers: K codes
+// (B*H rows of `len` tokens x 128 bytes), transposed V codes (B*H*128 rows of `len` bytes) and K scales
+// (B*H rows of len/64 floats), all starting at token `lo` of segment `seg`.
+struct CodePushArgs {
+  const int8_t* k_codes;      // this rank's buffers (inside the peer heap)
+  const float* k_scale;
+  const uint8_t* vt_codes;
+  int batch, heads, seg, seg_pad;
+  int lo, len;                // tokens, multiples of 128
+  const uint64_t* peers;
+  int nranks, rank;
+  int64_t xchg_off;
+};
+
 struct PeerWaitArgs {
   const uint64_t* peers;
   int nranks, rank;
   int64_t xchg_off;
-  uint32_t per_call;          // share_push CTAs per rank and call
+  uint32_t signals;           // signals per rank and call (one per push kernel)
   uint64_t timeout_ns;
   int* status;
 };
@@ -162,7 +178,7 @@ struct PeerWaitArgs {
 cudaError_t launch_kv_block_stats(const KvBlockStatsArgs& a, cudaStream_t st);
 cudaError_t launch_kv_window_sums(const KvWindowSumsArgs& a, cudaStream_t st);
 cudaError_t launch_quant_q(const QuantQArgs& a, cudaStream_t st);
-cudaError_t launch_quant_kv(const QuantKArgs& ka, const QuantVArgs& va, cudaStream_t st);
+cudaError_t launch_quant_kv(const QuantKArgs& ka, const QuantVArgs& va, int tile0, int tiles, cudaStream_t st);
 cudaError_t launch_attn(const AttnArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                         const CUtensorMap& tm_v, cudaStream_t st);
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st);
@@ -170,21 +186,26 @@ cudaError_t launch_share_totals_push(const ShareTotalsArgs& a, cudaStream_t st);
 cudaError_t launch_chunk_totals(const ChunkTotalsArgs& a, cudaStream_t st);
 cudaError_t launch_share_push(const SharePushArgs& a, cudaStream_t st);
 cudaError_t launch_peer_wait(const PeerWaitArgs& a, cudaStream_t st);
+cudaError_t launch_code_push(const CodePushArgs& a, int ctas, cudaStream_t st);
 int* device_status_ptr();
 
-// Sets the largest shared-memory carveout for `Kernel` on the current device (once per device). All
-// kernels of this library prefer it, so an SM never has to drain to change its L1/shared split when
-// kernels of different shared-memory needs run concurrently (the share push beside the quantizers).
+// Sets the largest shared-memory carveout for `Kernel` on the current device (once per device). The
+// kernels that need little shared memory prefer it, so that one of them starting on an idle SM does
+// not configure it for a small shared-memory split, which would keep a concurrent quantizer CTA off
+// that SM until it drains (the split pushes run beside the quantizers).
+#ifndef LBQ_CARVEOUT
+#define LBQ_CARVEOUT 100   // preferred shared-memory carveout in percent (negative: leave the driver's choice)
+#endif
 template <auto Kernel>
 inline cudaError_t prefer_max_shared() {
+  if (LBQ_CARVEOUT < 0) return cudaSuccess;
   static bool done[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!done[dev]) {
-    e = cudaFuncSetAttribute(Kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             int(cudaSharedmemCarveoutMaxShared));
+    e = cudaFuncSetAttribute(Kernel, cudaFuncAttributePreferredSharedMemoryCarveout, int(LBQ_CARVEOUT));
     if (e != cudaSuccess) return e;
     done[dev] = true;
   }

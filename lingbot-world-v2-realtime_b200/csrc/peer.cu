@@ -12,15 +12,17 @@
 //                      into every rank's slot for this rank as tagged 8-byte words.
 //   chunk_totals       waits for every rank's tagged totals and adds the memory totals and the
 //                      shares' in rank order (bit-identical on every rank).
+//   code_push          copies this rank's share of the chunk-segment codes (quantized locally by
+//                      quant_kv_kernel) into every other rank's code buffers, then one signal per rank.
 //   share_push         copies this rank's bf16 K/V share and its block statistics into every rank's
-//                      cache replica and tables, then a signal per CTA.
-//   peer_wait          waits for every other rank's share_push signals.
+//                      cache replica and tables (calls whose K/V persist), then one signal per rank.
+//   peer_wait          waits for every other rank's signals of this call.
 //
 // The totals travel as tagged words: each 8-byte store carries 32 data bits and the call's tag (call
 // counter + 1, kept on the device by every rank in lockstep), so the receiver polls the data itself.
-// The share push signals with monotonic u32 counters in the receiver's exchange area, raised with a
-// system-scope release add by one thread per producer CTA after a CTA barrier and a system fence; the
-// receiver keeps how many it has consumed ("seen") in its own area. No host-side epoch is needed, so
+// The pushes signal with monotonic u32 counters in the receiver's exchange area: every CTA fences its
+// stores at system scope and counts itself done, and the last one raises each receiver's counter with
+// a system-scope release add; the receiver keeps how many it has consumed ("seen") in its own area. No host-side epoch is needed, so
 // the launches can be replayed from a CUDA graph. Every wait is bounded (time limit in the arguments)
 // and records a status code instead of hanging. Totals slots are double-buffered by call parity: rank
 // r writes its call-c+1 totals only after it read every rank's call-c totals, which each rank sends
@@ -30,43 +32,10 @@
 
 #include "lbq_ptx.cuh"
 #include "lbq_kernels.h"
+#include "lbq_peer.cuh"
 
 namespace lbq {
 
-namespace {
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
-  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ char* heap(const uint64_t* peers, int p) {
-  return reinterpret_cast<char*>(static_cast<uintptr_t>(peers[p]));
-}
-// Waits until counter `flag` reaches `target` (modular u32 order); false after `timeout_ns`.
-__device__ __forceinline__ bool wait_counter(const uint32_t* flag, uint32_t target, uint64_t timeout_ns) {
-  if (int32_t(ld_acquire_sys(flag) - target) >= 0) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 0; i < LBQ_SPIN_LIMIT; ++i) {
-    __nanosleep(64);
-    if (int32_t(ld_acquire_sys(flag) - target) >= 0) return true;
-    if ((i & 63) == 0 && globaltimer_ns() - t0 > timeout_ns) break;
-  }
-  return false;
-}
-
-}  // namespace
 
 // ------------------------------------------------------------------ share totals -> every rank
 // One CTA per (32-channel group, head, batch), 256 threads = 32 channels x 8 block groups: per
@@ -179,7 +148,7 @@ __global__ void __launch_bounds__(128) chunk_totals_kernel(ChunkTotalsArgs a) {
 // Persistent: `ctas` CTAs stride over the units (64-token block of the share, head,
 // batch). Thread = (row group of 4 rows, 16-byte chunk); a unit's K/V rows are read once into
 // registers and stored to every rank (CTAs start on different ranks), with the block's statistics row (already in
-// this rank's tables) copied to the other ranks' tables. One signal per CTA and peer at the end.
+// this rank's tables) copied to the other ranks' tables. One signal per peer after the last CTA.
 __global__ void __launch_bounds__(256) share_push_kernel(SharePushArgs a) {
   const int t = threadIdx.x, c16 = t & 15, rg = t >> 4;
   const int units = a.nb_part * a.heads * a.batch;
@@ -225,14 +194,62 @@ __global__ void __launch_bounds__(256) share_push_kernel(SharePushArgs a) {
       }
     }
   }
-  __syncthreads();
-  if (t == 0) {
-    __threadfence_system();
+  signal_after_last_cta(a.peers, a.nranks, a.rank, a.xchg_off, xchg::kDonePush);
+}
+
+// ------------------------------------------------------------------ share codes -> every other rank
+// `ctas` CTAs stride over the 16-byte pieces of this rank's share of the chunk-segment codes (K rows of
+// len*128 bytes, then V channel rows of len bytes); each piece is read once and stored to every other
+// rank at the same heap offset. CTA 0 also copies the K scales. One signal per rank after the last CTA.
+__global__ void __launch_bounds__(256) code_push_kernel(CodePushArgs a) {
+  const int64_t bh_rows = int64_t(a.batch) * a.heads;
+  const int64_t k_row = int64_t(a.len) * 8;            // 16-byte pieces per K row
+  const int64_t v_row = a.len / 16;                    // 16-byte pieces per V channel row
+  const int64_t pk = bh_rows * k_row, total = pk + bh_rows * 128 * v_row;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  const char* mine = heap(a.peers, a.rank);
+  const char* kbase = reinterpret_cast<const char*>(a.k_codes);
+  const char* vbase = reinterpret_cast<const char*>(a.vt_codes);
+  for (int64_t g0 = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; g0 < total; g0 += 4 * stride) {
+    uint4 val[4];
+    int64_t off[4];                                    // byte offset from this rank's heap base
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t g = g0 + i * stride;
+      off[i] = -1;
+      if (g < total) {
+        const char* src;
+        if (g < pk) {
+          const int64_t row = g / k_row, col = g - row * k_row;
+          src = kbase + ((a.seg * bh_rows + row) * a.seg_pad + a.lo) * 128 + col * 16;
+        } else {
+          const int64_t gv = g - pk, row = gv / v_row, col = gv - row * v_row;   // row = bh * 128 + channel
+          src = vbase + (a.seg * bh_rows * 128 + row) * a.seg_pad + a.lo + col * 16;
+        }
+        off[i] = src - mine;
+        val[i] = *reinterpret_cast<const uint4*>(src);
+      }
+    }
     for (int q = 0; q + 1 < a.nranks; ++q) {
-      char* dst = heap(a.peers, (a.rank + 1 + q) % a.nranks) + a.xchg_off;
-      red_release_sys_add(reinterpret_cast<uint32_t*>(dst + xchg::kFlagsData) + a.rank, 1u);
+      // every other rank once, CTAs starting on different ones
+      char* dst = heap(a.peers, (a.rank + 1 + (q + int(blockIdx.x)) % (a.nranks - 1)) % a.nranks);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (off[i] >= 0) *reinterpret_cast<uint4*>(dst + off[i]) = val[i];
     }
   }
+  if (blockIdx.x == 0) {
+    const int per = a.len / 64;
+    for (int64_t i = threadIdx.x; i < bh_rows * per; i += blockDim.x) {
+      const int64_t row = i / per;
+      const float* src = a.k_scale + (a.seg * bh_rows + row) * (a.seg_pad / 64) + a.lo / 64 + (i - row * per);
+      const int64_t off = reinterpret_cast<const char*>(src) - mine;
+      const float v = *src;
+      for (int q = 1; q < a.nranks; ++q)
+        *reinterpret_cast<float*>(heap(a.peers, (a.rank + q) % a.nranks) + off) = v;
+    }
+  }
+  signal_after_last_cta(a.peers, a.nranks, a.rank, a.xchg_off, xchg::kDoneQuant);
 }
 
 // ------------------------------------------------------------------ wait for the other ranks' shares
@@ -242,7 +259,7 @@ __global__ void __launch_bounds__(32) peer_wait_kernel(PeerWaitArgs a) {
   uint32_t* seen = reinterpret_cast<uint32_t*>(mine + xchg::kSeenData);
   const uint32_t* flags = reinterpret_cast<const uint32_t*>(mine + xchg::kFlagsData);
   if (t < a.nranks && t != a.rank) {
-    const uint32_t target = seen[t] + a.per_call;
+    const uint32_t target = seen[t] + a.signals;
     if (wait_counter(flags + t, target, a.timeout_ns)) {
       seen[t] = target;
     } else {
@@ -265,6 +282,11 @@ cudaError_t launch_chunk_totals(const ChunkTotalsArgs& a, cudaStream_t st) {
 cudaError_t launch_share_push(const SharePushArgs& a, cudaStream_t st) {
   if (cudaError_t e0 = prefer_max_shared<share_push_kernel>(); e0 != cudaSuccess) return e0;
   share_push_kernel<<<a.ctas, 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t launch_code_push(const CodePushArgs& a, int ctas, cudaStream_t st) {
+  if (cudaError_t e0 = prefer_max_shared<code_push_kernel>(); e0 != cudaSuccess) return e0;
+  code_push_kernel<<<ctas, 256, 0, st>>>(a);
   return cudaGetLastError();
 }
 cudaError_t launch_peer_wait(const PeerWaitArgs& a, cudaStream_t st) {

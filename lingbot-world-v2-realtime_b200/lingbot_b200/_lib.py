@@ -42,7 +42,10 @@ SIGNATURES = {
     "lbq_chunk_totals": (_i32, [_vp, _i32, _i32, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _u64, _vp]),
     "lbq_share_push": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _i32, _i32,
                               _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp]),
-    "lbq_peer_wait": (_i32, [_vp, _i32, _i32, _i64, _i32, _i32, _i32, _i32, _u64, _vp]),
+    "lbq_share_quant_push": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _i32, _i32, _i32, _i32,
+                                    _i32, _i32, _i32, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _i32,
+                                    _i32, _i64, _i32, _vp]),
+    "lbq_peer_wait": (_i32, [_vp, _i32, _i32, _i64, _i32, _u64, _vp]),
 }
 
 _lock = threading.Lock()

@@ -117,28 +117,41 @@ class SplitAttention:
     of n_tokens, token-sharded across ranks in `share_part` slices (rank r holds chunk tokens
     [r*part, (r+1)*part) as k/v shares, and attends the same query rows). Per call, on this rank:
 
-      1. lbq_kv_block_stats   — block statistics of the share into this rank's cache tables;
+      1. lbq_kv_block_stats    — block statistics of the share into this rank's cache tables;
       2. lbq_share_totals_push — the share's per-channel totals -> every rank's exchange area;
-         lbq_chunk_totals     — wait for every rank's totals; window totals (memory + shares in rank
-                                order, identical on every rank);
-      3. quantize the memory segment (K mean-smoothed int8, V e4m3), while on a side stream
-         lbq_share_push       — the bf16 share and its block statistics -> every rank's cache replica
-                                and tables (forked after the totals push when the cache was last used two
-                                or more calls ago, else after lbq_chunk_totals) and the query slice is
-                                quantized;
-      4. lbq_peer_wait        — wait for the other ranks' shares; quantize the chunk segment;
-      5. attention over the two segments.
-
-    A CUDA graph replays the launch order chosen at capture: replay per-cache calls in the order they
-    were captured (as a layer loop does).
+         lbq_chunk_totals      — wait for every rank's totals; window totals (memory + shares in rank
+                                 order, identical on every rank);
+      3. quantize the memory segment (K mean-smoothed int8, V e4m3) locally, while on a side stream
+         lbq_share_quant_push  — this rank's share is quantized into its chunk segment and the codes
+                                 copied into every other rank's,
+         lbq_share_push        — (persist=True) the bf16 share and its block statistics -> every rank's
+                                 cache replica and tables,
+         and the query slice is quantized;
+      4. lbq_peer_wait         — wait for the other ranks' pushes;
+      5. attention over the two segments (memory, chunk).
 
     Codes and scales are identical to quantizing the whole window in one piece (mem_len % 64 == 0
-    keeps the 64-token K blocks those of the whole window). The caches must be carved from `heap`
-    (kv_cache.allocate(..., heap=heap)), identically on every rank. Every launch is on the current
-    stream (plus one forked side stream), without host synchronisation, so a call can be captured in
-    a CUDA graph and replayed. `memory_changed(cache)` must be called whenever the memory part of a
-    cache changes.
+    keeps the 64-token K blocks those of the whole window). `persist=False` skips the bf16 replication
+    of the chunk into the caches: for the denoise passes of a chunk, whose K/V the next pass of the same
+    chunk overwrites before anything reads them (only the memory-write pass's K/V stay in the cache);
+    with persist=True a call leaves every rank's cache as kv_cache.write would. The caches and this
+    object's code buffers are carved from `heap` (kv_cache.allocate(..., heap=heap), then this
+    constructor), identically on every rank; size the heap with `heap_bytes`. Every launch is on the
+    current stream (plus one forked side stream), without host synchronisation, so a call can be
+    captured in a CUDA graph and replayed. `memory_changed(cache)` must be called whenever the memory
+    part of a cache changes.
     """
+
+    @staticmethod
+    def heap_bytes(batch, heads, mem_len, n_tokens, world):
+        """Peer-heap bytes this object carves (code buffers and exchange area, 256-byte aligned)."""
+        from . import _lib
+        seg_pad = -(-(mem_len if mem_len > 0 else n_tokens) // 128) * 128
+        nseg = 2 if mem_len > 0 else 1
+        up = lambda x: (x + 255) // 256 * 256  # noqa: E731
+        per_seg = batch * heads * seg_pad
+        return (up(nseg * per_seg * 128) + up(nseg * per_seg // 64 * 4) + up(nseg * per_seg * 128)
+                + up(_lib.load().lbq_exchange_bytes(world, batch, heads)))
 
     def __init__(self, batch, heads, q_rows, mem_len, n_tokens, device, heap, group=None, timeout_s=4.0):
         from . import _lib, ops
@@ -158,26 +171,31 @@ class SplitAttention:
         lo = min(n_tokens, self.rank * self.part)
         self.share_valid = min(n_tokens, lo + self.part) - lo
         self.lo = lo
+        self._lo = lo if self.share_valid > 0 else 0     # an empty share writes nothing; any aligned start
         self.timeout_ns = int(timeout_s * 1e9)
+        self.nseg = 2 if mem_len > 0 else 1
+        self.seg_len = mem_len if mem_len > 0 else n_tokens
+        seg_pad = -(-self.seg_len // 128) * 128
         cols = batch * heads * 128
+        # the code buffers live in the heap: every rank stores its share's codes into every rank's copy
+        self.k_codes = heap.carve((self.nseg, batch, heads, seg_pad, 128), torch.int8)
+        self.k_scale = heap.carve((self.nseg, batch, heads, seg_pad // 64), torch.float32)
+        self.vt_codes = heap.carve((self.nseg, batch, heads, 128, seg_pad), torch.uint8)
         xbytes = _lib.load().lbq_exchange_bytes(self.world, batch, heads)
         if xbytes <= 0:
             raise ValueError(f"no exchange layout for {self.world} ranks")
         self.xchg = heap.carve((xbytes,), torch.uint8)          # zeroed; caller barriers before first use
         self.xchg_off = heap.offset(self.xchg)
         self.q_codes, self.q_scale = ops.alloc_q(batch, heads, max(q_rows, 1), device)
-        (self.k_codes, self.k_scale, self.vt_codes, self.v_scale,
-         self.km) = ops.alloc_kv(batch, heads, mem_len, 2, device)
+        self.v_scale = torch.empty(batch, heads, 128, dtype=torch.float32, device=device)
+        self.km = torch.empty(batch, heads, 128, dtype=torch.bfloat16, device=device)
         self.tot_ksum = torch.zeros(cols, dtype=torch.float64, device=device)
         self.tot_vamax = torch.zeros(cols, dtype=torch.float32, device=device)
-        self.side = torch.cuda.Stream(device=device)
+        # high priority: the small push kernels get SMs as soon as a quantizer CTA retires
+        self.side = torch.cuda.Stream(device=device, priority=-1)
         self.fork, self.join = torch.cuda.Event(), torch.cuda.Event()
-        self._calls = 0
-        self._last_use = {}      # id(cache) -> index of the call that last used it
-        self.push_ctas = 64      # CTAs of the share push (measured best beside the quantizers); the same
-                                 # on every rank
-        self.early_push = False  # fork the share push before the totals wait (when the cache allows it);
-                                 # off: the bulk push then delays the tagged totals on NVLink
+        self.push_ctas = 64      # CTAs of the bf16 share push; the same on every rank
+        self.code_ctas = 32      # CTAs of the code push (few: it shares the GPU with the memory quantizer)
 
     def memory_changed(self, cache):
         """Per-channel totals of the memory part from the cache's block statistics, kept in the cache
@@ -204,11 +222,12 @@ class SplitAttention:
             raise ValueError(f"cache of {lk} tokens cannot hold {self.mem_len} memory + {self.n} chunk tokens")
         return self.heap.offset(k), self.heap.offset(cache["v"]), lk
 
-    def __call__(self, q_rows, cache, k_part, v_part, out, sm_scale=None, num_splits=None, attn_events=None):
+    def __call__(self, q_rows, cache, k_part, v_part, out, sm_scale=None, num_splits=None, attn_events=None,
+                 persist=True):
         """q_rows [B, rows, H, 128] (this rank's query slice), k_part/v_part [B, part, H, 128] (this rank's
-        share of the chunk, rows past the chunk's end ignored) -> out [B, rows, H, 128]; also writes the
-        whole chunk into `cache` at [mem_len, mem_len + n_tokens) and its block statistics, as
-        kv_cache.write does."""
+        share of the chunk, rows past the chunk's end ignored) -> out [B, rows, H, 128]. With persist=True
+        the whole chunk also lands in `cache` at [mem_len, mem_len + n_tokens), with its block statistics,
+        on every rank (as kv_cache.write does). Every rank makes the same calls with the same `persist`."""
         from . import _lib, ops
         st = torch.cuda.current_stream()
         stp = st.cuda_stream
@@ -218,65 +237,53 @@ class SplitAttention:
         k_off, v_off, lk = self._check_cache(cache)
         ksum, vamax = cache["lbq_ksum"], cache["lbq_vamax"]
         max_blocks = ksum.shape[1]
-        row0 = (self.mem_len + self.lo) // 64
+        row0 = (self.mem_len + self._lo) // 64
         nb_valid = (self.share_valid + 63) // 64
         peers = ops._ptr(self.heap.peers)
         group = (peers, self.world, self.rank, self.xchg_off)
         share = (ops._ptr(k_part), *k_part.stride()[:3], ops._ptr(v_part), *v_part.stride()[:3])
+        kv_len = self.mem_len + self.n
+        rows = q_rows.shape[1]
+        nseg = self.nseg
+        codes = (ops._ptr(self.tot_ksum), ops._ptr(self.tot_vamax), ops._ptr(self.k_codes), ops._ptr(self.k_scale),
+                 ops._ptr(self.vt_codes), ops._ptr(self.km), ops._ptr(self.v_scale))
         # 1. block statistics of the share into this rank's tables
         if nb_valid > 0:
             _lib.call("lbq_kv_block_stats", *share, b, h, self.share_valid, 0, nb_valid, max_blocks,
                       ksum.data_ptr() + row0 * h * 128 * 8, vamax.data_ptr() + row0 * h * 128 * 4, stp)
-        # 2. the share's totals -> every rank (before the bulk push, so that they do not queue behind it)
+        # 2. the share's totals -> every rank; every rank's totals -> the window totals (identical on
+        # every rank)
         _lib.call("lbq_share_totals_push", ops._ptr(ksum), ops._ptr(vamax), max_blocks, row0, nb_valid, b, h,
                   *group, stp)
-        # the share push may start now unless a rank could still be reading this cache's chunk region:
-        # every rank has started the previous call (its totals signal was consumed by the previous call's
-        # lbq_chunk_totals), so a cache last used two or more calls ago is free
-        last = self._last_use.get(id(cache))
-        early = self.early_push and last is not None and self._calls - last >= 2
-        self._last_use[id(cache)] = self._calls
-        self._calls += 1
-        kv_len = self.mem_len + self.n
-        rows = q_rows.shape[1]
-
-        def side_work():
-            # the bf16 share (+ its block statistics) -> every rank; the query slice's codes
-            self.fork.record(st)
-            self.side.wait_event(self.fork)
-            _lib.call("lbq_share_push", *share, b, h, self.share_valid, self.nb_part, *group, k_off, v_off, lk,
-                      self.mem_len + self.lo, self.heap.offset(ksum), self.heap.offset(vamax), max_blocks,
-                      self.push_ctas, self.side.cuda_stream)
-            if rows > 0:
-                _lib.call("lbq_quant_q", ops._ptr(q_rows), *q_rows.stride()[:3], b, h, rows, ops._ptr(self.q_codes),
-                          ops._ptr(self.q_scale), self.side.cuda_stream)
-            self.join.record(self.side)
-
-        if early:
-            side_work()
-        # every rank's totals -> the window totals (identical on every rank)
         _lib.call("lbq_chunk_totals", *group, b, h, ops._ptr(cache["lbq_mem_ksum"]), ops._ptr(cache["lbq_mem_vamax"]),
                   ops._ptr(self.tot_ksum), ops._ptr(self.tot_vamax), self.timeout_ns, stp)
-        if not early:
-            side_work()
-        # 3. the memory segment is quantized while the shares travel
-        kc, vc = cache["k"], cache["v"]
-        codes = (ops._ptr(self.tot_ksum), ops._ptr(self.tot_vamax), ops._ptr(self.k_codes), ops._ptr(self.k_scale),
-                 ops._ptr(self.vt_codes), ops._ptr(self.km), ops._ptr(self.v_scale))
-        src = (ops._ptr(kc), *kc.stride()[:3], ops._ptr(vc), *vc.stride()[:3], b, h)
-        nseg = 2 if self.mem_len > 0 else 1
-        seg_len = self.mem_len if self.mem_len > 0 else self.n
+        # 3. side stream: the share's codes (and, persisting, its bf16) -> every rank; the query slice
+        self.fork.record(st)
+        self.side.wait_event(self.fork)
+        sst = self.side.cuda_stream
+        _lib.call("lbq_share_quant_push", *share, b, h, self._lo, self.share_valid, self.part, nseg - 1, nseg,
+                  self.seg_len, kv_len, *codes, int(self.mem_len == 0), *group, self.code_ctas, sst)
+        if persist:
+            _lib.call("lbq_share_push", *share, b, h, self.share_valid, self.nb_part, *group, k_off, v_off, lk,
+                      self.mem_len + self._lo, self.heap.offset(ksum), self.heap.offset(vamax), max_blocks,
+                      self.push_ctas, sst)
+        if rows > 0:
+            _lib.call("lbq_quant_q", ops._ptr(q_rows), *q_rows.stride()[:3], b, h, rows, ops._ptr(self.q_codes),
+                      ops._ptr(self.q_scale), sst)
+        self.join.record(self.side)
+        # ... while the memory segment is quantized here
         if self.mem_len > 0:
-            _lib.call("lbq_quant_kv", *src, 0, 0, 2, self.mem_len, self.mem_len, kv_len, *codes, 1, stp)
-        # 4. every share has landed: quantize the chunk segment
+            kc, vc = cache["k"], cache["v"]
+            _lib.call("lbq_quant_kv", ops._ptr(kc), *kc.stride()[:3], ops._ptr(vc), *vc.stride()[:3], b, h, 0, 0, 2,
+                      self.mem_len, self.mem_len, kv_len, *codes, 1, stp)
+        # 4. every rank's pushes have landed
         st.wait_event(self.join)
-        _lib.call("lbq_peer_wait", *group, self.nb_part, b, h, self.push_ctas, self.timeout_ns, stp)
-        _lib.call("lbq_quant_kv", *src, self.mem_len, nseg - 1, nseg, self.n, seg_len, kv_len, *codes,
-                  int(self.mem_len == 0), stp)
+        _lib.call("lbq_peer_wait", *group, 1 + int(bool(persist)), self.timeout_ns, stp)
         if rows == 0:
             return out
+        # 5. attention over (memory, chunk)
         w = ops.QuantWindow(self.q_codes, self.q_scale, self.k_codes, self.k_scale, self.vt_codes, self.v_scale,
-                            self.km, rows, kv_len, seg_len, nseg)
+                            self.km, rows, kv_len, self.seg_len, nseg)
         if attn_events is not None:
             attn_events[0].record()
         ops.attn_from_codes(w, sm_scale=sm_scale, out=out, num_splits=num_splits)
@@ -284,8 +291,8 @@ class SplitAttention:
             attn_events[1].record()
         return out
 
-    def launches(self, num_splits):
-        """Our kernels per call: share block stats, totals push, window totals, share push, memory K/V
-        quantizer, Q quantizer, peer wait, chunk K/V quantizer, attention (+ split-KV combine)."""
-        return (1 + 2 + 1 + (1 if self.mem_len > 0 else 0) + (1 if self.q_rows > 0 else 0) + 1 + 1 + 1
-                + (1 if num_splits > 1 else 0))
+    def launches(self, num_splits, persist=True):
+        """Our kernels per call: share block stats, totals push, window totals, share quant push, (bf16
+        share push), Q quantizer, memory K/V quantizer, peer wait, attention (+ split-KV combine)."""
+        return (3 + 1 + int(bool(persist)) + (1 if self.q_rows > 0 else 0) + (1 if self.mem_len > 0 else 0) + 1
+                + (1 if self.q_rows > 0 else 0) + (1 if num_splits > 1 and self.q_rows > 0 else 0))

@@ -22,7 +22,8 @@ def main():
     world, rank = dist.get_world_size(), dist.get_rank()
     from lingbot_b200 import _lib, kv_cache, ops, peer, split
     H, mem, n, L = 3, 1280, 700, 2
-    heap = peer.PeerHeap(kv_cache.heap_bytes(L, [1, mem + n, H, 128], torch.bfloat16) + (1 << 20), dev)
+    heap = peer.PeerHeap(kv_cache.heap_bytes(L, [1, mem + n, H, 128], torch.bfloat16)
+                         + split.SplitAttention.heap_bytes(1, H, mem, n, world), dev)
     caches = kv_cache.allocate(L, [1, mem + n, H, 128], torch.bfloat16, dev, heap=heap)
     g = torch.Generator().manual_seed(3)
     for kc in caches:
@@ -44,26 +45,28 @@ def main():
         v = torch.randn(1, n, H, 128, generator=gi).bfloat16().to(dev)
         return q, k, v
 
-    def check(kc, q, k, v, out_rows):
-        assert torch.equal(kc["k"][:, mem:], k) and torch.equal(kc["v"][:, mem:], v), "cache replica differs"
-        ref_stats = {"k": kc["k"], "v": kc["v"]}
-        kv_cache.refresh_stats(ref_stats, 0, mem + n)
-        assert torch.equal(kc["lbq_ksum"], ref_stats["lbq_ksum"]), "block K sums differ"
-        assert torch.equal(kc["lbq_vamax"], ref_stats["lbq_vamax"]), "block V maxima differ"
-        w = ops.quantize_qkv(q, kc["k"], kc["v"])
+    def check(kc, q, k, v, out_rows, persisted=True):
+        if persisted:
+            assert torch.equal(kc["k"][:, mem:], k) and torch.equal(kc["v"][:, mem:], v), "cache replica differs"
+            ref_stats = {"k": kc["k"], "v": kc["v"]}
+            kv_cache.refresh_stats(ref_stats, 0, mem + n)
+            assert torch.equal(kc["lbq_ksum"], ref_stats["lbq_ksum"]), "block K sums differ"
+            assert torch.equal(kc["lbq_vamax"], ref_stats["lbq_vamax"]), "block V maxima differ"
+        w = ops.quantize_qkv(q, torch.cat([kc["k"][:, :mem], k], 1), torch.cat([kc["v"][:, :mem], v], 1))
         ref = ops.attn_from_codes(w)
         torch.cuda.synchronize()
         assert torch.equal(out_rows, ref[:, r0:r1]), "split output differs from the one-GPU output"
 
-    # eager calls over both layers
+    # eager calls over both layers (denoise passes do not persist their K/V)
     for seed in range(3):
+        persist = seed != 1
         for li, kc in enumerate(caches):
             q, k, v = inputs(100 * seed + li)
             out = torch.empty(1, r1 - r0, H, 128, dtype=torch.bfloat16, device=dev)
-            sp(q[:, r0:r1], kc, k[:, r0:r1], v[:, r0:r1], out)
+            sp(q[:, r0:r1], kc, k[:, r0:r1], v[:, r0:r1], out, persist=persist)
             torch.cuda.synchronize()
             assert _lib.device_status() == 0
-            check(kc, q, k, v, out)
+            check(kc, q, k, v, out, persisted=persist)
     # graph replay
     part = sp.part
     qs = torch.zeros(L, 1, r1 - r0, H, 128, dtype=torch.bfloat16, device=dev)

@@ -45,16 +45,19 @@ def _inputs(seed, mem, n, H, dev):
     return q, kcur, vcur
 
 
-def _check_against_one_piece(sp, kc, q, kcur, vcur, out, mem, n):
+def _check_against_one_piece(sp, kc, q, kcur, vcur, out, mem, n, persisted=True):
     from lingbot_b200 import kv_cache, ops
-    # the chunk landed in the cache, with the block statistics kv_cache.write keeps
-    assert torch.equal(kc["k"][:, mem:mem + n], kcur) and torch.equal(kc["v"][:, mem:mem + n], vcur)
-    ref_stats = {"k": kc["k"], "v": kc["v"]}
-    kv_cache.refresh_stats(ref_stats, 0, mem + n)
-    nb = (mem + n + 63) // 64
-    assert torch.equal(kc["lbq_ksum"][:, :nb], ref_stats["lbq_ksum"][:, :nb])
-    assert torch.equal(kc["lbq_vamax"][:, :nb], ref_stats["lbq_vamax"][:, :nb])
-    w = ops.quantize_qkv(q, kc["k"][:, :mem + n], kc["v"][:, :mem + n])
+    if persisted:
+        # the chunk landed in the cache, with the block statistics kv_cache.write keeps
+        assert torch.equal(kc["k"][:, mem:mem + n], kcur) and torch.equal(kc["v"][:, mem:mem + n], vcur)
+        ref_stats = {"k": kc["k"], "v": kc["v"]}
+        kv_cache.refresh_stats(ref_stats, 0, mem + n)
+        nb = (mem + n + 63) // 64
+        assert torch.equal(kc["lbq_ksum"][:, :nb], ref_stats["lbq_ksum"][:, :nb])
+        assert torch.equal(kc["lbq_vamax"][:, :nb], ref_stats["lbq_vamax"][:, :nb])
+    kwin = torch.cat([kc["k"][:, :mem], kcur], dim=1)
+    vwin = torch.cat([kc["v"][:, :mem], vcur], dim=1)
+    w = ops.quantize_qkv(q, kwin, vwin)
     ref = ops.attn_from_codes(w)
     torch.cuda.synchronize()
     # codes: segment 0 = tokens [0, mem), segment 1 = tokens [mem, mem + n) of the one-piece window
@@ -75,7 +78,8 @@ def _check_against_one_piece(sp, kc, q, kcur, vcur, out, mem, n):
 
 def _setup(mem, n, H, dev, layers=1):
     from lingbot_b200 import kv_cache, peer, split
-    heap = peer.PeerHeap(kv_cache.heap_bytes(layers, [1, mem + n, H, 128], torch.bfloat16) + (1 << 20), dev)
+    heap = peer.PeerHeap(kv_cache.heap_bytes(layers, [1, mem + n, H, 128], torch.bfloat16)
+                         + split.SplitAttention.heap_bytes(1, H, mem, n, 1), dev)
     caches = kv_cache.allocate(layers, [1, mem + n, H, 128], torch.bfloat16, dev, heap=heap)
     g = torch.Generator(device=dev).manual_seed(7)
     for kc in caches:
@@ -95,13 +99,16 @@ def test_split_attention_matches_single_segment(one_rank_group, mem, n):
     from lingbot_b200 import _lib
     dev, H = torch.device("cuda"), 2
     heap, (kc,), sp = _setup(mem, n, H, dev)
-    for seed in (0, 1, 2):                   # consecutive calls: counters and slot parity advance
+    for seed, persist in ((0, True), (1, False), (2, False), (3, True)):   # counters and slot parity advance
         q, kcur, vcur = _inputs(seed, mem, n, H, dev)
+        before = kc["k"][:, mem:mem + n].clone()
         out = torch.empty(1, n, H, 128, dtype=torch.bfloat16, device=dev)
-        sp(q, kc, kcur, vcur, out)
+        sp(q, kc, kcur, vcur, out, persist=persist)
         torch.cuda.synchronize()
         assert _lib.device_status() == 0
-        _check_against_one_piece(sp, kc, q, kcur, vcur, out, mem, n)
+        if not persist:                       # a denoise pass leaves the cache's chunk region alone
+            assert torch.equal(kc["k"][:, mem:mem + n], before)
+        _check_against_one_piece(sp, kc, q, kcur, vcur, out, mem, n, persisted=persist)
 
 
 def test_split_attention_graph_replay(one_rank_group):
