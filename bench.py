@@ -10,10 +10,13 @@ FLOPs/chunk = 150 x 4 x 6032 x 30160 x 12 x 128 = 167.66 TFLOP.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload chunk|call|requant]
 
-N > 1 is launched with torch.distributed.run (one rank per GPU, NCCL): the chunk's query tokens are
-sharded in 128-row slices; each rank all-gathers the current chunk's bf16 K/V over NVLink into its
-replica of the cache (the memory part is already replicated: it was gathered when it was current),
-re-quantizes the window and attends its queries. `value` = whole-job TOPS, time = max over ranks.
+N > 1 is launched with torch.distributed.run (one rank per GPU; NCCL only for the process-group
+plumbing): the chunk's tokens are sharded in 128-token slices (each rank holds its slice's q and k/v
+share and attends those query rows). Per call the ranks exchange the chunk's per-channel totals and
+quantized shares over NVLink peer memory (CUDA-IPC-mapped heaps) while each re-quantizes the replicated
+memory part, and the memory-write pass also replicates the bf16 chunk into every rank's cache
+(lingbot_b200.split.SplitAttention). `value` = whole-job TOPS, time = max over ranks. Each layer's call
+is one CUDA graph, replayed (--eager launches from Python).
 
 `--impl reference` times the reference's CPU restatement (the oracle: the reference's torch
 quantizers + a torch emulation of the Sage kernel) on the host cores on a bounded sample of the same
@@ -56,6 +59,9 @@ def parse():
     ap.add_argument("--call-kv", type=int, default=12064,
                     help="keys of the single-call workload (12064 = BASELINE config 1; 30160 = one chunk call)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--timeline", default=None, metavar="DIR",
+                    help="after timing, write each rank's kernel timeline of one pass (torch profiler) to "
+                    "DIR/timeline_rank<r>.txt")
     ap.add_argument("--eager", action="store_true", help="launch every kernel from Python instead of replaying "
                     "one CUDA graph per layer")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -378,8 +384,46 @@ def run_ours(args, world, rank, local):
                 "kernel": "attn_fwd_kernel", "peak_source": f"2 x bf16_tflops_sustained ({peak_src}); the "
                 "INT8/FP8 dense tensor rate of B200 is twice its bf16 rate",
                 "frac_of_nominal_4500": round(achieved / 4500.0, 4), "attn_ms_per_call": round(attn_ms, 4)}
+    if args.timeline:
+        write_timeline(chunk, args.timeline, world, rank)
     e2e = None if args.no_e2e else run_e2e(chunk, args, world)
     return dict(tops=tops, ms=ms, roofline=roofline, clocks=clk.summary(), launches=launches, e2e=e2e)
+
+
+def write_timeline(chunk, out_dir, world, rank):
+    """One denoise pass (30 calls) under the torch profiler: per-kernel device time per call and the
+    kernel timeline of one call, for this rank (not part of the timed region)."""
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    barrier(world)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for li in range(LAYERS):
+            if chunk.graphs is not None:
+                chunk.graphs[(li, 0, False)][0].replay()
+            else:
+                chunk.call(li, persist=False)
+        torch.cuda.synchronize()
+    barrier(world)
+    ev = sorted((e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA),
+                key=lambda e: e.time_range.start)
+    agg = {}
+    for e in ev:
+        a = agg.setdefault(e.name.split("(")[0], [0, 0.0])
+        a[0] += 1
+        a[1] += e.device_time
+    lines = [f"rank {rank} of {world}: per-kernel device time per (pass, layer) call, one denoise pass",
+             "kernel | launches | us per call"]
+    lines += [f"{k} | {n} | {t / LAYERS:.1f}" for k, (n, t) in sorted(agg.items(), key=lambda x: -x[1][1])]
+    calls = [i for i, e in enumerate(ev) if "kv_block_stats" in e.name]
+    if len(calls) > LAYERS // 2 + 1:
+        i0, i1 = calls[LAYERS // 2], calls[LAYERS // 2 + 1]
+        t0 = ev[i0].time_range.start
+        lines += ["", f"timeline of call {LAYERS // 2} (us from its first kernel): start | end | kernel"]
+        lines += [f"{e.time_range.start - t0:8.1f} | {e.time_range.end - t0:8.1f} | {e.name.split('(')[0]}"
+                  for e in ev[i0:i1]]
+    os.makedirs(out_dir, exist_ok=True)
+    with open(os.path.join(out_dir, f"timeline_rank{rank}.txt"), "w") as f:
+        f.write("\n".join(lines) + "\n")
 
 
 def run_e2e(chunk, args, world):
