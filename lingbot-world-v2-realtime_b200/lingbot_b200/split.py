@@ -192,8 +192,10 @@ class SplitAttention:
         self.tot_ksum = torch.zeros(cols, dtype=torch.float64, device=device)
         self.tot_vamax = torch.zeros(cols, dtype=torch.float32, device=device)
         # high priority: the small push kernels get SMs as soon as a quantizer CTA retires
-        self.side = torch.cuda.Stream(device=device, priority=-1)
-        self.fork, self.join = torch.cuda.Event(), torch.cuda.Event()
+        self.side = self.fork = self.join = None
+        if torch.device(device).type == "cuda":
+            self.side = torch.cuda.Stream(device=device, priority=-1)
+            self.fork, self.join = torch.cuda.Event(), torch.cuda.Event()
         self.push_ctas = 64      # CTAs of the bf16 share push; the same on every rank
         self.code_ctas = 32      # CTAs of the code push (few: it shares the GPU with the memory quantizer)
 
