@@ -22,11 +22,15 @@
 // counter + 1, kept on the device by every rank in lockstep), so the receiver polls the data itself.
 // The pushes signal with monotonic u32 counters in the receiver's exchange area: every CTA fences its
 // stores at system scope and counts itself done, and the last one raises each receiver's counter with
-// a system-scope release add; the receiver keeps how many it has consumed ("seen") in its own area. No host-side epoch is needed, so
-// the launches can be replayed from a CUDA graph. Every wait is bounded (time limit in the arguments)
-// and records a status code instead of hanging. Totals slots are double-buffered by call parity: rank
-// r writes its call-c+1 totals only after it read every rank's call-c totals, which each rank sends
-// after finishing its call c-1 reads, so a slot is never overwritten while it is read.
+// a system-scope release add; the receiver keeps how many it has consumed ("seen") in its own area.
+// No host-side epoch is needed, so the launches can be replayed from a CUDA graph. Every wait is
+// bounded (time limit in the arguments) and records a status code instead of hanging.
+//
+// Reuse without overwriting what a rank still reads: totals slots are double-buffered by call parity,
+// and rank r writes its call-c+1 totals only after it read every rank's call-c totals, which each rank
+// sends after finishing its call c-1 reads. The pushes of call c into another rank's code buffers and
+// cache start after this rank's call-c window totals, i.e. after every rank sent its call-c totals,
+// which each rank does after its call c-1 attention, the last reader of those buffers.
 #include <cuda_bf16.h>
 #include <cstdint>
 

@@ -294,7 +294,9 @@ class SplitAttention:
         return out
 
     def launches(self, num_splits, persist=True):
-        """Our kernels per call: share block stats, totals push, window totals, share quant push, (bf16
-        share push), Q quantizer, memory K/V quantizer, peer wait, attention (+ split-KV combine)."""
-        return (3 + 1 + int(bool(persist)) + (1 if self.q_rows > 0 else 0) + (1 if self.mem_len > 0 else 0) + 1
-                + (1 if self.q_rows > 0 else 0) + (1 if num_splits > 1 and self.q_rows > 0 else 0))
+        """Our kernels per call: share block stats, totals push, window totals, share K/V quantizer, code
+        push (more than one rank), bf16 share push (persist), Q quantizer, memory K/V quantizer, peer
+        wait, attention (+ split-KV combine)."""
+        rows = self.q_rows > 0
+        return (int(self.share_valid > 0) + 2 + 1 + int(self.world > 1) + int(bool(persist)) + int(rows)
+                + int(self.mem_len > 0) + 1 + int(rows) + int(num_splits > 1 and rows))
