@@ -428,8 +428,8 @@ def write_timeline(chunk, out_dir, world, rank):
 
 def run_e2e(chunk, args, world):
     """Same chunk through the public API with HOST inputs: every (pass, layer) copies its q and its
-    k/v share from pinned host memory (H2D) and reads the attention output back (D2H); copies of the
-    next call overlap the current call on a side stream."""
+    k/v share from pinned host memory (H2D) and reads the attention output back (D2H); the uploads of
+    the next call and the read-back of the previous one overlap the current call on copy streams."""
     dev = chunk.dev
     n_loc = chunk.r1 - chunk.r0
     pool = 4
@@ -439,10 +439,14 @@ def run_e2e(chunk, args, world):
     d_q = [torch.empty(1, n_loc, H, D, dtype=torch.bfloat16, device=dev) for _ in range(2)]
     d_kv = [torch.empty(2, 1, chunk.part, H, D, dtype=torch.bfloat16, device=dev) for _ in range(2)]
     d_out = [torch.empty(1, n_loc, H, D, dtype=torch.bfloat16, device=dev) for _ in range(2)]
-    copy = torch.cuda.Stream(device=dev)
+    # q and k/v uploads on two copy streams, the output read-back on a third, so that no copy sits on
+    # the compute stream between two calls
+    copy_q, copy_kv, copy_out = (torch.cuda.Stream(device=dev) for _ in range(3))
     main = torch.cuda.current_stream(dev)
-    ready = [torch.cuda.Event() for _ in range(2)]
-    freed = [torch.cuda.Event() for _ in range(2)]
+    ready_q = [torch.cuda.Event() for _ in range(2)]
+    ready_kv = [torch.cuda.Event() for _ in range(2)]
+    freed = [torch.cuda.Event() for _ in range(2)]      # slot's inputs consumed / output written
+    out_free = [torch.cuda.Event() for _ in range(2)]   # slot's output read back
     h2d = q_bytes = h_q[0].numel() * 2
     h2d += h_kv[0].numel() * 2
     d2h = h_out[0].numel() * 2
@@ -457,11 +461,12 @@ def run_e2e(chunk, args, world):
 
     def stage(i):
         s = i % 2
-        with torch.cuda.stream(copy):
-            copy.wait_event(freed[s])
-            d_q[s].copy_(h_q[i % pool], non_blocking=True)
-            d_kv[s].copy_(h_kv[i % pool], non_blocking=True)
-            ready[s].record(copy)
+        for st, ev, dst, src in ((copy_q, ready_q[s], d_q[s], h_q[i % pool]),
+                                 (copy_kv, ready_kv[s], d_kv[s], h_kv[i % pool])):
+            with torch.cuda.stream(st):
+                st.wait_event(freed[s])
+                dst.copy_(src, non_blocking=True)
+                ev.record(st)
 
     def one_step():
         n = PASSES * LAYERS
@@ -470,14 +475,21 @@ def run_e2e(chunk, args, world):
             s = i % 2
             if i + 1 < n:
                 stage(i + 1)
-            main.wait_event(ready[s])
+            main.wait_event(ready_q[s])
+            main.wait_event(ready_kv[s])
+            main.wait_event(out_free[s])
             persist = i // LAYERS == PASSES - 1
             if graphs is not None:
                 graphs[(i % LAYERS, s, persist)][0].replay()
             else:
                 chunk.call(i % LAYERS, q=d_q[s], kv_part=d_kv[s], out=d_out[s], persist=persist)
             freed[s].record(main)
-            h_out[s].copy_(d_out[s], non_blocking=True)
+            with torch.cuda.stream(copy_out):
+                copy_out.wait_event(freed[s])
+                h_out[s].copy_(d_out[s], non_blocking=True)
+                out_free[s].record(copy_out)
+        for ev in out_free:          # the step ends when its last outputs are on the host
+            main.wait_event(ev)
 
     for _ in range(max(1, args.warmup // 2)):
         one_step()
