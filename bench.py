@@ -24,7 +24,9 @@ workload (one (pass, layer) call, 2 heads, 2048 query rows against the full 3016
 
 Other workloads (not the headline line): `--workload call` = BASELINE config 1 (one call, q 6032 x
 kv 12064: quantize + attend), `--workload requant` = BASELINE config 2 (re-quantize 30 layers of
-24128-token bf16 memory caches; HBM GB/s).
+24128-token bf16 memory caches; HBM GB/s), `--workload streams` = BASELINE config 5 (independent
+streams, one per GPU, 54288-key windows with outlier K channels; aggregate TOPS). BASELINE config 3
+(one DiT pass) is one fifth of the chunk: 30 calls.
 """
 import argparse
 import json
@@ -55,7 +57,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["chunk", "call", "requant"], default="chunk")
+    ap.add_argument("--workload", choices=["chunk", "call", "requant", "streams"], default="chunk")
     ap.add_argument("--call-kv", type=int, default=12064,
                     help="keys of the single-call workload (12064 = BASELINE config 1; 30160 = one chunk call)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -540,6 +542,69 @@ def _timed(fn, steps, warmup, dev, world):
     return max_over_ranks(t0.elapsed_time(t1), world) / steps, clk.summary()
 
 
+STREAM_MEM = 48256                 # config 5: 8 memory chunks
+STREAM_LK = STREAM_MEM + LQ        # 54288-token window
+STREAM_LAYERS = 8                  # layer caches cycled (333 MB each, 2.7 GB: inputs larger than L2)
+
+
+def run_streams(args, world, rank, local):
+    """independent streams, one per GPU (here one per rank: replicas, no exchange),
+    each a window of 48256 memory + 6032 current tokens, q 6032, 12 heads x 128, K with 4 of its 128
+    channels scaled x20. One step = one call on every stream: the current chunk written into a layer
+    cache (block stats refreshed), the window re-quantized, Q quantized, attention. value = aggregate
+    TOPS of the N streams."""
+    from lingbot_b200 import kv_cache, ops
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev).manual_seed(5000 + rank)
+    caches = kv_cache.allocate(STREAM_LAYERS, [1, STREAM_LK, H, D], torch.bfloat16, dev)
+    for c in caches:
+        c["k"][:, :STREAM_MEM].normal_(generator=g)
+        c["k"][:, :STREAM_MEM, :, :4] *= 20.0
+        c["v"][:, :STREAM_MEM].normal_(generator=g)
+        kv_cache.refresh_stats(c, 0, STREAM_MEM)
+    q = torch.randn(STREAM_LAYERS, 1, LQ, H, D, generator=g, device=dev).bfloat16()
+    kcur = torch.randn(STREAM_LAYERS, 1, LQ, H, D, generator=g, device=dev)
+    kcur[..., :4] *= 20.0
+    kcur = kcur.bfloat16()
+    vcur = torch.randn(STREAM_LAYERS, 1, LQ, H, D, generator=g, device=dev).bfloat16()
+    quantizer = kv_cache.WindowQuantizer()
+    out = torch.empty(1, LQ, H, D, dtype=torch.bfloat16, device=dev)
+    it = [0]
+    ev = []
+
+    def fn():
+        li = it[0] % STREAM_LAYERS
+        it[0] += 1
+        c = caches[li]
+        c["k"][:, STREAM_MEM:STREAM_LK] = kcur[li]
+        c["v"][:, STREAM_MEM:STREAM_LK] = vcur[li]
+        kv_cache.refresh_stats(c, STREAM_MEM, STREAM_LK)
+        w = kv_cache.quantize_window(q[li], c, STREAM_LK, quantizer)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        ops.attn_from_codes(w, out=out)
+        b.record()
+        ev.append((a, b))
+
+    ms, clocks = _timed(fn, args.steps, args.warmup, dev, world)
+    flops = 4.0 * LQ * STREAM_LK * H * D
+    attn_ms = statistics.mean(a.elapsed_time(b) for a, b in ev[args.warmup:])
+    peaks, src = measured_peaks()
+    peak = 2.0 * peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops", 1400.0))
+    ach = flops / (attn_ms * 1e-3) / 1e12
+    splits = ops.pick_splits(1, H, LQ, STREAM_LK)
+    return dict(tops=world * flops / (ms * 1e-3) / 1e12, ms=ms, clocks=clocks, scaling="weak",
+                launches=(5 + (1 if splits > 1 else 0)) * args.steps * world, e2e=None,
+                config={"workload": "BASELINE config 5: independent streams, one per GPU, window 48256 memory + "
+                                    "6032 current tokens, K channels 0-3 x20",
+                        "q_len": LQ, "kv_len": STREAM_LK, "memory_tokens": STREAM_MEM, "heads": H, "head_dim": D,
+                        "parallelism": f"replicas x{world}",
+                        "l2": f"inputs larger than L2 ({STREAM_LAYERS} layer caches of 333 MB, cycled)"},
+                roofline={"bound": "tensor", "achieved": round(ach, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                          "frac": round(ach / peak, 4), "traffic": None, "kernel": "attn_fwd_kernel",
+                          "peak_source": f"2 x bf16_tflops_sustained ({src})", "attn_ms_per_call": round(attn_ms, 4)})
+
+
 def run_call(args, world, rank, local):
     """q 6032 x kv 12064 x 12 heads, quantize + attend per step. Inputs cycle
     through 8 sets (> L2)."""
@@ -660,6 +725,8 @@ def main():
             res = run_ours(args, world, rank, local)
         elif args.workload == "call":
             res = run_call(args, world, rank, local)
+        elif args.workload == "streams":
+            res = run_streams(args, world, rank, local)
         else:
             res = run_requant(args, world, rank, local)
         if rank == 0:
@@ -672,11 +739,12 @@ def main():
                                                  f"({fl / 1e9:.1f} GFLOP, {dt:.2f} s) on {model}"}
             metric = {"chunk": "DiT self-attention TOPS (full chunk: 5 passes x 30 layers)",
                       "call": "attention TOPS, one call (BASELINE config 1, quantize + attend)",
-                      "requant": "K/V re-quant HBM GB/s (BASELINE config 2, 30 layers x 24128 tokens)"}[args.workload]
+                      "requant": "K/V re-quant HBM GB/s (BASELINE config 2, 30 layers x 24128 tokens)",
+                      "streams": "aggregate attention TOPS, independent streams (BASELINE config 5)"}[args.workload]
             line = {"metric": metric,
                     "value": round(res["tops"], 2), "unit": res.get("unit", "TOPS"), "n_gpus": world, "steps": args.steps,
                     "warmup": args.warmup, "ms_per_step": round(res["ms"], 3), "s_per_chunk": round(res["ms"] / 1e3, 5),
-                    "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                    "higher_is_better": True, "scaling": res.get("scaling", "strong"), "vs_baseline": None,
                     "dtype": "int8 QK^T / fp8 e4m3 PV (bf16 in/out)", "data": "synthetic",
                     "config": {"workload": {"chunk": "BASELINE config 4: full chunk, 4 denoise + 1 memory-write pass x 30 layers",
                                             "call": f"BASELINE config 1: q 6032 x kv {args.call_kv}",
@@ -684,7 +752,8 @@ def main():
                                "q_len": LQ, "kv_len": LK, "memory_tokens": MEM, "heads": H, "head_dim": D,
                                "parallelism": f"query shards x{world}" if world > 1 else "single GPU",
                                "l2": "inputs larger than L2 (30 layer caches of 92.6 MB each, cycled)",
-                               "eviction": "not in the timed region (window steady)"},
+                               "eviction": "not in the timed region (window steady)"} if "config" not in res
+                    else res["config"],
                     "roofline": res["roofline"], "clocks": res["clocks"], "gpu_launches": res["launches"],
                     "e2e": res["e2e"], "cpu_baseline": cpu}
             print(json.dumps(line), flush=True)
