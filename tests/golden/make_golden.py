@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this directory from the reference's OWN code.
 
-Run in a container that has the reference checked out (default path below; override with
---ref). The GPU box never runs this: it only reads the committed .npz / .json outputs.
+Run where the reference is checked out (--ref or LINGBOT_REF). The GPU box never runs this: it only
+reads the committed .npz / .json outputs.
 
     python tests/golden/make_golden.py --ref <path to lingbot-world-v2-realtime>
 
@@ -115,8 +115,11 @@ def kv_schedule(kvc):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("LINGBOT_REF", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("LINGBOT_REF"),
+                    help="checkout of the reference project (or set LINGBOT_REF)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give the reference checkout with --ref or LINGBOT_REF")
     kvq = load(os.path.join(args.ref, "experiments/modules/sage_kvq.py"), "ref_sage_kvq")
     kvc = load(os.path.join(args.ref, "lingbot/layers/kv_cache.py"), "ref_kv_cache")
     torch.set_num_threads(4)
