@@ -15,8 +15,11 @@ plumbing): the chunk's tokens are sharded in 128-token slices (each rank holds i
 share and attends those query rows). Per call the ranks exchange the chunk's per-channel totals and
 quantized shares over NVLink peer memory (CUDA-IPC-mapped heaps) while each re-quantizes the replicated
 memory part, and the memory-write pass also replicates the bf16 chunk into every rank's cache
-(lingbot_b200.split.SplitAttention). `value` = whole-job TOPS, time = max over ranks. Each layer's call
-is one CUDA graph, replayed (--eager launches from Python).
+(lingbot_b200.split.SplitAttention). `--split keys` shards the keys instead: each rank re-quantizes only
+its slice of the memory part plus its own chunk share, receives every rank's query codes, attends every
+query row against its keys and sends the partial outputs to the rows' owners, which merge them
+(lingbot_b200.split.KeySplitAttention). `value` = whole-job TOPS, time = max over ranks. Each layer's
+call is one CUDA graph, replayed (--eager launches from Python).
 
 `--impl reference` times the reference's CPU restatement (the oracle: the reference's torch
 quantizers + a torch emulation of the Sage kernel) on the host cores on a bounded sample of the same
@@ -67,6 +70,9 @@ def parse():
     ap.add_argument("--eager", action="store_true", help="launch every kernel from Python instead of replaying "
                     "one CUDA graph per layer")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--split", choices=["queries", "keys"], default="queries",
+                    help="N > 1: shard the query rows (SplitAttention) or the keys (KeySplitAttention: each rank "
+                         "quantizes and attends its key range for every query row; partials merged by the row owners)")
     return ap.parse_args()
 
 
@@ -230,16 +236,17 @@ class Chunk:
     current-chunk q/k/v, the quantizer buffers and the output. With N > 1 the caches are carved from
     a peer heap mapped by every rank, and the sequence split exchanges over NVLink peer memory."""
 
-    def __init__(self, world, rank, device):
+    def __init__(self, world, rank, device, split_mode="queries"):
         from lingbot_b200 import kv_cache, split
         self.world, self.rank, self.dev = world, rank, device
+        cls = split.KeySplitAttention if split_mode == "keys" else split.SplitAttention
         self.r0, self.r1 = shard_rows(world, rank)
         self.heap = None
         if world > 1:
             from lingbot_b200 import peer
             self.part = split.share_part(LQ, world)
             self.heap = peer.PeerHeap(kv_cache.heap_bytes(LAYERS, [1, LK, H, D], torch.bfloat16)
-                                      + split.SplitAttention.heap_bytes(1, H, MEM, LQ, world), device)
+                                      + cls.heap_bytes(1, H, MEM, LQ, world), device)
         else:
             self.part = LQ
         g = torch.Generator(device=device).manual_seed(1234)
@@ -262,7 +269,7 @@ class Chunk:
         self.quantizer = kv_cache.WindowQuantizer()
         self.splitter = None
         if world > 1:
-            self.splitter = split.SplitAttention(1, H, n_loc, MEM, LQ, device, self.heap)
+            self.splitter = cls(1, H, n_loc, MEM, LQ, device, self.heap)
             for c in self.caches:
                 self.splitter.memory_changed(c)
             torch.cuda.synchronize()
@@ -347,7 +354,7 @@ def run_ours(args, world, rank, local):
     from lingbot_b200 import _lib
     dev = torch.device("cuda", local)
     peaks, peak_src = measured_peaks()
-    chunk = Chunk(world, rank, dev)
+    chunk = Chunk(world, rank, dev, args.split)
     torch.cuda.synchronize()
     chunk.step()                         # eager warm-up (allocations, tensor maps, lazy loading)
     if not args.eager:
@@ -376,9 +383,13 @@ def run_ours(args, world, rank, local):
     if status:
         raise RuntimeError(f"device status {status:#x}: a kernel's bounded wait gave up")
     tops = FLOPS_CHUNK / (ms * 1e-3) / 1e12
-    # dominant kernel: attention over one (pass, layer); per-rank FLOPs share
+    # dominant kernel: attention over one (pass, layer); this rank's FLOPs share (its query rows against
+    # the window, or every query row against its keys)
     rows = chunk.r1 - chunk.r0
     flops_launch = 4.0 * rows * LK * H * D
+    if world > 1 and args.split == "keys":
+        keys = sum(min(valid, (t0 + nt) * 128) - t0 * 128 for t0, nt, valid in chunk.splitter.ranges() if nt > 0)
+        flops_launch = 4.0 * LQ * keys * H * D
     achieved = flops_launch / (attn_ms * 1e-3) / 1e12
     peak = 2.0 * peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
@@ -750,7 +761,8 @@ def main():
                                             "call": f"BASELINE config 1: q 6032 x kv {args.call_kv}",
                                             "requant": "BASELINE config 2: bf16 cache [30, 24128, 12, 128]"}[args.workload],
                                "q_len": LQ, "kv_len": LK, "memory_tokens": MEM, "heads": H, "head_dim": D,
-                               "parallelism": f"query shards x{world}" if world > 1 else "single GPU",
+                               "parallelism": (f"{dict(queries='query', keys='key')[args.split]} shards x{world}" if world > 1
+                                               else "single GPU"),
                                "l2": "inputs larger than L2 (30 layer caches of 92.6 MB each, cycled)",
                                "eviction": "not in the timed region (window steady)"} if "config" not in res
                     else res["config"],

@@ -150,6 +150,46 @@ LBQ_API int lbq_attn_fwd(const int8_t* q_codes, const float* q_scale, int q_len,
                  int64_t so_h, int num_splits, float* o_part, float* ml_part, int* splits_used,
                  void* stream);
 
+/* lbq_quant_kv restricted to the 128-token tiles [tile_begin, tile_end) of the segment (those holding
+ * valid tokens: tile_end <= ceil(seg_valid / 128)); segment token t reads source token tok0 + t, and
+ * tok0 may be negative as long as tok0 + 128 * tile_begin >= 0 (a share whose first token is segment
+ * token -tok0). km_out / v_scale are written by the range's first tile when write_totals != 0. Codes are
+ * those of lbq_quant_kv for the same tokens: the key-range split quantizes only its own tiles of the
+ * window (the per-rank quantization of sage_preq.py:115-124 after lingbot/parallel/split_dit.py:371-386,
+ * cut to the rank's keys). */
+LBQ_API int lbq_quant_kv_tiles(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h,
+                       const void* v, int64_t sv_b, int64_t sv_l, int64_t sv_h, int batch, int heads,
+                       int64_t tok0, int seg, int num_segments, int seg_valid, int seg_len,
+                       int64_t kv_len_total, const double* ksum_total, const float* vamax_total,
+                       int8_t* k_codes, float* k_scale, uint8_t* vt_codes, void* km_out, float* v_scale,
+                       int write_totals, int tile_begin, int tile_end, void* stream);
+
+/* Key-range split attention: every query row (q_codes / q_scale [B][H][q_pad][128] / [B][H][q_pad/32],
+ * q_len valid rows) against this rank's keys only — for each code segment s < num_segments (1 or 2,
+ * [S][B][H][seg_pad] layouts as lbq_attn_fwd), tiles [range_lt0[s], range_lt0[s] + range_tiles[s]) of
+ * segment s, keys >= range_valid[s] of the segment masked (host arrays of num_segments ints; at least
+ * one tile in total). Instead of an output, each query tile's partial — O / row sum as fp16 in V-code
+ * units ([B*H][part][128]) and the row's (max, sum) as f32 pairs ([B*H][part]) — is stored into slot
+ * `rank` of the receive buffers of the rank owning the tile (rows [p*part, (p+1)*part) belong to rank
+ * p; heap offsets recv_o_off / recv_ml_off of [nranks] slots each), through peer memory; the last CTA
+ * then raises every other rank's data signal once. Ranks combine with lbq_keys_combine after
+ * lbq_peer_wait(signals = 1). Replaces the Ulysses head exchange around the attention of
+ * lingbot/parallel/split_dit.py:366-445: here heads stay whole and the keys are split. */
+LBQ_API int lbq_attn_fwd_keys(const int8_t* q_codes, const float* q_scale, int q_len, int q_pad,
+                      const int8_t* k_codes, const float* k_scale, const uint8_t* vt_codes,
+                      int num_segments, int seg_len, int batch, int heads, float sm_scale,
+                      const int* range_lt0, const int* range_tiles, const int* range_valid,
+                      const uint64_t* peers, int nranks, int rank, int64_t xchg_off, int part,
+                      int64_t recv_o_off, int64_t recv_ml_off, void* stream);
+
+/* Merge of the key-range partials in this rank's receive buffers (recv_o fp16 [nranks][B*H][part][128],
+ * recv_ml f32 pairs [nranks][B*H][part]) for its first `rows` query rows into out [B, rows, H, 128]
+ * (bf16, element strides so_*), applying the V scale: the split-KV merge of
+ * experiments/bench_attn/splitkv/README.md:60-69 over ranks instead of splits. */
+LBQ_API int lbq_keys_combine(const void* recv_o, const float* recv_ml, int nranks, int part, int rows,
+                     const float* v_scale, int batch, int heads, void* out, int64_t so_b,
+                     int64_t so_l, int64_t so_h, void* stream);
+
 /* Flash-decoding merge of lbq_attn_fwd's split partials into out (bf16), applying the V scale.
  * The combine kernel of experiments/bench_attn/splitkv/README.md:67-69 (`splitkv_combine_kernel`). */
 LBQ_API int lbq_splitkv_combine(const float* o_part, const float* ml_part, int num_splits,
@@ -234,9 +274,22 @@ LBQ_API int lbq_share_quant_push(const void* k, int64_t sk_b, int64_t sk_l, int6
                          int write_totals, const uint64_t* peers, int nranks, int rank, int64_t xchg_off,
                          int ctas, void* stream);
 
+/* Key-range split: copies this rank's query-slice codes (q_codes [B][H][rows_pad][128] and q_scale
+ * [B][H][rows_pad/32], from lbq_quant_q) to rows [row0, row0 + rows_pad) of every rank's full query
+ * buffers (heap offsets q_off / q_scale_off of [B][H][q_pad][128] / [B][H][q_pad/32]), this rank's own
+ * included, with `ctas` CTAs (0 = 32), then signals the other ranks once. Must be ordered after this
+ * call's lbq_chunk_totals (every rank has then finished its previous attention, the last reader of the
+ * query buffers). Replaces the q all-to-all of the Ulysses split (lingbot/parallel/split_dit.py:371-386):
+ * every rank needs every query row once the keys are split. */
+LBQ_API int lbq_q_push(const int8_t* q_codes, const float* q_scale, int rows_pad, int row0, int q_pad,
+               int batch, int heads, int64_t q_off, int64_t q_scale_off, const uint64_t* peers,
+               int nranks, int rank, int64_t xchg_off, int ctas, void* stream);
+
 /* Waits until every other rank's pushes of this call have landed in this rank's buffers: `signals`
  * (1 or 2) = the push launches every rank makes per call (lbq_share_quant_push, plus lbq_share_push
- * when the call persists its K/V); this rank's own pushes are ordered by the caller's streams.
+ * when the call persists its K/V; with the key-range split lbq_q_push [+ lbq_share_push] before the
+ * attention, then lbq_attn_fwd_keys before the combine); this rank's own pushes are ordered by the
+ * caller's streams.
  * Replaces the `comp[c].wait_event(ev)` on the peer's inbox at lingbot/parallel/split_dit.py:384-386. */
 LBQ_API int lbq_peer_wait(const uint64_t* peers, int nranks, int rank, int64_t xchg_off, int signals,
                   uint64_t timeout_ns, void* stream);

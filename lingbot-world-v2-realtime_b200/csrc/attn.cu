@@ -27,9 +27,11 @@
 // written (e4m3, 128-byte-swizzled K-major rows) to a double-buffered shared-memory tile that the
 // P.V product reads as its A operand; the next Q.K^T therefore does not wait for P.V.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cstdint>
 
 #include "lbq_kernels.h"
+#include "lbq_peer.cuh"
 #include "lbq_ptx.cuh"
 
 namespace lbq {
@@ -67,9 +69,22 @@ constexpr size_t kAttnSmemBytes = 1024 /*alignment slack*/ + kTile * (6 + 2 * kS
 
 __device__ int g_status;
 
+template <bool kKeyRange>
 __device__ __forceinline__ int seg_valid(const AttnArgs& a, int seg) {
+  if constexpr (kKeyRange) return a.range_valid[seg];
   const int rest = a.kv_len - seg * a.seg_len;
   return rest < a.seg_len ? rest : a.seg_len;
+}
+// Key tile jt of the call's tile sequence -> (code segment, tile inside the segment).
+template <bool kKeyRange>
+__device__ __forceinline__ void tile_seg(const AttnArgs& a, int jt, int tiles_per_seg, int& seg, int& lt) {
+  if constexpr (kKeyRange) {
+    seg = jt >= a.range_tile0[1] ? 1 : 0;
+    lt = jt - a.range_tile0[seg] + a.range_lt0[seg];
+  } else {
+    seg = jt / tiles_per_seg;
+    lt = jt - seg * tiles_per_seg;
+  }
 }
 
 // Softmax of one 128-key tile for the calling thread's row. `sv` holds the scores as the bits of
@@ -152,7 +167,52 @@ __device__ __forceinline__ float softmax_tile(uint32_t (&sv)[4][32], int valid, 
   return alpha;
 }
 
+// Key-range epilogue of one softmax warp: its 32 rows of O / row sum as fp16 (V-code units, |x| <= 448)
+// are staged in the tile's P buffers (free once O is complete; 16-byte chunks of a 256-byte row
+// XOR-swizzled by row) and stored to the owner rank's receive slot for this rank as whole rows, two
+// rows per warp instruction; the (max, sum) of each row follows. Rows past q_len are not stored.
+__device__ __forceinline__ void store_key_partial(const AttnArgs& a, uint32_t tO, uint8_t* stage, int quarter,
+                                                  int lane, int qtile, int bh, int bhs, float m, float dsum) {
+  const float rd = __frcp_rn(dsum);
+  const int rl = quarter * 32 + lane;                    // row inside the tile (TMEM lane)
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t ov[32];
+    tmem_ld32(tO + 32 * c, ov);
+    tmem_ld_wait();
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      uint32_t hw[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const __half2 p = __floats2half2_rn(__fmul_rn(__uint_as_float(ov[8 * e + 2 * k]), rd),
+                                            __fmul_rn(__uint_as_float(ov[8 * e + 2 * k + 1]), rd));
+        hw[k] = *reinterpret_cast<const uint32_t*>(&p);
+      }
+      const int chunk = 4 * c + e;
+      *reinterpret_cast<uint4*>(stage + rl * 256 + ((chunk ^ (rl & 15)) << 4)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    }
+  }
+  __syncwarp();
+  const int qrow0 = qtile * 128;
+  const int owner = qrow0 / a.part;                      // part % 128 == 0: one owner per Q tile
+  const int64_t slot = (int64_t(a.rank) * bhs + bh) * a.part + (qrow0 - owner * a.part);
+  char* dst = reinterpret_cast<char*>(static_cast<uintptr_t>(a.peers[owner]));
+  uint8_t* dst_o = reinterpret_cast<uint8_t*>(dst + a.recv_o_off) + slot * 256;
+#pragma unroll 4
+  for (int i = 0; i < 16; ++i) {
+    const int r = quarter * 32 + 2 * i + (lane >> 4), ch = lane & 15;
+    if (qrow0 + r < a.q_len)
+      *reinterpret_cast<uint4*>(dst_o + r * 256 + ch * 16) =
+          *reinterpret_cast<const uint4*>(stage + r * 256 + ((ch ^ (r & 15)) << 4));
+  }
+  if (qrow0 + rl < a.q_len) reinterpret_cast<float2*>(dst + a.recv_ml_off)[slot + rl] = make_float2(m, dsum);
+}
+
 // 320 threads hold registers as 384 (whole warpgroups), so at one CTA per SM a thread gets <= 168.
+// kKeyRange: the key-range split's variant (tile pieces of AttnArgs::range_*, partials to the query
+// tile's owner rank); false: the whole window in uniform segments.
+template <bool kKeyRange>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const AttnArgs a) {
@@ -214,7 +274,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       int issued = 0;
       for (int i = 0; i < n; ++i) {
         const int jt = t_begin + i;
-        const int seg = jt / tiles_per_seg, lt = jt - seg * tiles_per_seg;
+        int seg, lt;
+        tile_seg<kKeyRange>(a, jt, tiles_per_seg, seg, lt);
         const int s = i % kStages;
         const uint32_t ph = (i / kStages) & 1;
         if (!mbar_wait(&sh->k_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) break;
@@ -305,7 +366,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int kspb = a.seg_pad / 64;
     auto kscale_ptr = [&](int i) {
       const int jt = t_begin + i;
-      const int seg = jt / tiles_per_seg, lt = jt - seg * tiles_per_seg;
+      int seg, lt;
+      tile_seg<kKeyRange>(a, jt, tiles_per_seg, seg, lt);
       return a.k_scale + int64_t(seg * bhs + bh) * kspb + lt * 2;
     };
     float m = -INFINITY, dsum = 0.f;
@@ -321,8 +383,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     float2 ks_next = ok ? *reinterpret_cast<const float2*>(kscale_ptr(0)) : make_float2(0.f, 0.f);
     for (int i = 0; ok && i < n; ++i) {
       const int jt = t_begin + i;
-      const int seg = jt / tiles_per_seg, lt = jt - seg * tiles_per_seg;
-      const int valid = min(128, seg_valid(a, seg) - lt * 128);
+      int seg, lt;
+      tile_seg<kKeyRange>(a, jt, tiles_per_seg, seg, lt);
+      const int valid = min(128, seg_valid<kKeyRange>(a, seg) - lt * 128);
       const float2 ks = ks_next;
       if (i + 1 < n) ks_next = *reinterpret_cast<const float2*>(kscale_ptr(i + 1));   // prefetch
       const float c1a = __fmul_rn(__fmul_rn(qs, ks.x), a.sm_log2);
@@ -382,7 +445,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_before();
       mbar_arrive(&sh->p_full[t]);
     }
-    if (ok && mbar_wait(&sh->o_done[t], (n - 1) & 1, abort_flag, a.status, kDevTimeoutO)) {
+    const bool o_ready = ok && mbar_wait(&sh->o_done[t], (n - 1) & 1, abort_flag, a.status, kDevTimeoutO);
+    if constexpr (kKeyRange) {
+      // warp-uniform: tcgen05.ld is a whole-warp instruction
+      if (__all_sync(0xffffffffu, o_ready) && qtile * 128 < a.q_len) {
+        tc_fence_after();
+        store_key_partial(a, tO, sP + 2 * t * kTile, quarter, lane, qtile, bh, bhs, m, dsum);
+      }
+    } else if (o_ready) {
       tc_fence_after();
       if (a.num_splits == 1) {
         const float rd = __frcp_rn(dsum);
@@ -432,6 +502,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, 512);
+  // the owners of the query tiles may read this rank's partials once every CTA has stored them
+  if constexpr (kKeyRange) signal_after_last_cta(a.peers, a.nranks, a.rank, a.xchg_off, xchg::kDoneAttn);
 }
 
 // Flash-decoding merge of the per-split partials (splitkv/README.md:60-69): one warp per
@@ -468,28 +540,84 @@ __global__ void __launch_bounds__(128) splitkv_combine_kernel(const CombineArgs 
   *reinterpret_cast<uint2*>(a.out + b * a.so_b + int64_t(row) * a.so_l + h * a.so_h + lane * 4) = st;
 }
 
-cudaError_t launch_attn(const AttnArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                        cudaStream_t st) {
+// Merge of the key-range partials this rank received for its query rows: slot s holds rank s's
+// O / row sum (fp16) and (max, sum) over rank s's keys; out = sum_s w_s o_s / sum_s w_s * v_scale with
+// w_s = exp2(max_s - max) * sum_s (the split-KV merge of splitkv/README.md:60-69 on normalised
+// partials). One warp per (row, batch*head), 4 channels per lane.
+__global__ void __launch_bounds__(128) keys_combine_kernel(const KeysCombineArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 4 + warp;
+  const int bh = blockIdx.y;
+  if (row >= a.rows) return;
+  const int bhs = a.batch * a.heads;
+  float mx = -INFINITY;
+  for (int s = 0; s < a.nranks; ++s) mx = fmaxf(mx, a.recv_ml[(int64_t(s) * bhs + bh) * a.part + row].x);
+  float L = 0.f;
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < a.nranks; ++s) {
+    const int64_t prow = (int64_t(s) * bhs + bh) * a.part + row;
+    const float2 ml = a.recv_ml[prow];
+    const float w = ml.x == -INFINITY ? 0.f : ex2_approx(ml.x - mx) * ml.y;
+    L += w;
+    const uint2 raw = reinterpret_cast<const uint2*>(a.recv_o + prow * 128)[lane];
+    const float2 p0 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+    const float2 p1 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+    o.x = fmaf(w, p0.x, o.x);
+    o.y = fmaf(w, p0.y, o.y);
+    o.z = fmaf(w, p1.x, o.z);
+    o.w = fmaf(w, p1.y, o.w);
+  }
+  const float rl = __frcp_rn(L);
+  const float4 vs = reinterpret_cast<const float4*>(a.v_scale + int64_t(bh) * 128)[lane];
+  const int b = bh / a.heads, h = bh - b * a.heads;
+  const __nv_bfloat162 q0 = __floats2bfloat162_rn(o.x * rl * vs.x, o.y * rl * vs.y);
+  const __nv_bfloat162 q1 = __floats2bfloat162_rn(o.z * rl * vs.z, o.w * rl * vs.w);
+  uint2 st;
+  st.x = *reinterpret_cast<const uint32_t*>(&q0);
+  st.y = *reinterpret_cast<const uint32_t*>(&q1);
+  *reinterpret_cast<uint2*>(a.out + b * a.so_b + int64_t(row) * a.so_l + h * a.so_h + lane * 4) = st;
+}
+
+template <bool kKeyRange>
+cudaError_t launch_attn_variant(const AttnArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                                const CUtensorMap& tm_v, cudaStream_t st) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   static bool configured[64] = {};
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    e = cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kAttnSmemBytes));
+    e = cudaFuncSetAttribute(attn_fwd_kernel<kKeyRange>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(kAttnSmemBytes));
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   dim3 grid((a.q_pad / 128 + 1) / 2, a.batch * a.heads, a.num_splits);
-  if (cudaError_t e0 = prefer_max_shared<attn_fwd_kernel>(); e0 != cudaSuccess) return e0;
-  attn_fwd_kernel<<<grid, kAttnThreads, kAttnSmemBytes, st>>>(tm_q, tm_k, tm_v, a);
+  if (cudaError_t e0 = prefer_max_shared<attn_fwd_kernel<kKeyRange>>(); e0 != cudaSuccess) return e0;
+  attn_fwd_kernel<kKeyRange><<<grid, kAttnThreads, kAttnSmemBytes, st>>>(tm_q, tm_k, tm_v, a);
   return cudaGetLastError();
+}
+
+cudaError_t launch_attn(const AttnArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                        cudaStream_t st) {
+  return launch_attn_variant<false>(a, tm_q, tm_k, tm_v, st);
+}
+cudaError_t launch_attn_keys(const AttnArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                             const CUtensorMap& tm_v, cudaStream_t st) {
+  return launch_attn_variant<true>(a, tm_q, tm_k, tm_v, st);
 }
 
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st) {
   dim3 grid((a.q_len + 3) / 4, a.batch * a.heads);
   if (cudaError_t e0 = prefer_max_shared<splitkv_combine_kernel>(); e0 != cudaSuccess) return e0;
   splitkv_combine_kernel<<<grid, 128, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_keys_combine(const KeysCombineArgs& a, cudaStream_t st) {
+  dim3 grid((a.rows + 3) / 4, a.batch * a.heads);
+  if (cudaError_t e0 = prefer_max_shared<keys_combine_kernel>(); e0 != cudaSuccess) return e0;
+  keys_combine_kernel<<<grid, 128, 0, st>>>(a);
   return cudaGetLastError();
 }
 

@@ -153,11 +153,11 @@ int lbq_quant_q(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, int bat
   return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "quant_q launch");
 }
 
-int lbq_quant_kv(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b, int64_t sv_l,
-                 int64_t sv_h, int batch, int heads, int64_t tok0, int seg, int num_segments, int seg_valid,
-                 int seg_len, int64_t kv_len_total, const double* ksum_total, const float* vamax_total,
-                 int8_t* k_codes, float* k_scale, uint8_t* vt_codes, void* km_out, float* v_scale, int write_totals,
-                 void* stream) {
+int lbq_quant_kv_tiles(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,
+                       int64_t sv_l, int64_t sv_h, int batch, int heads, int64_t tok0, int seg, int num_segments,
+                       int seg_valid, int seg_len, int64_t kv_len_total, const double* ksum_total,
+                       const float* vamax_total, int8_t* k_codes, float* k_scale, uint8_t* vt_codes, void* km_out,
+                       float* v_scale, int write_totals, int tile_begin, int tile_end, void* stream) {
   int r;
   if ((r = check_act("k", k, sk_b, sk_l, sk_h)) || (r = check_act("v", v, sv_b, sv_l, sv_h))) return r;
   if ((r = check_ptr("ksum_total", ksum_total)) || (r = check_ptr("vamax_total", vamax_total)) ||
@@ -170,16 +170,31 @@ int lbq_quant_kv(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const 
   if (seg_len % 64 && num_segments > 1)
     return fail(LBQ_ERR_ARG, "seg_len %d must be a multiple of 64 so K blocks match the whole window's", seg_len);
   if (seg_valid <= 0 || seg_valid > seg_len) return fail(LBQ_ERR_ARG, "seg_valid %d not in (0, %d]", seg_valid, seg_len);
-  if (tok0 < 0) return fail(LBQ_ERR_ARG, "tok0 must be >= 0");
+  if (tile_begin < 0 || tile_end < tile_begin || tile_end > (seg_valid + 127) / 128)
+    return fail(LBQ_ERR_ARG, "tiles [%d, %d) outside the %d tiles holding valid tokens", tile_begin, tile_end,
+                (seg_valid + 127) / 128);
+  if (tile_end > tile_begin && tok0 + int64_t(tile_begin) * 128 < 0)
+    return fail(LBQ_ERR_ARG, "tile %d maps to source token %lld < 0", tile_begin,
+                (long long)(tok0 + int64_t(tile_begin) * 128));
   const int seg_pad = int(round_up(seg_len, 128));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   lbq::QuantKArgs ka{static_cast<const __nv_bfloat16*>(k), sk_b, sk_l, sk_h, batch, heads, tok0, seg, seg_valid,
                      seg_pad, kv_len_total, ksum_total, k_codes, k_scale,
                      static_cast<__nv_bfloat16*>(km_out), write_totals};
   lbq::QuantVArgs va{static_cast<const __nv_bfloat16*>(v), sv_b, sv_l, sv_h, batch, heads, tok0, seg, seg_valid,
                      seg_pad, vamax_total, vt_codes, v_scale, write_totals};
-  cudaError_t e = lbq::launch_quant_kv(ka, va, 0, (seg_valid + 127) / 128, st);
+  cudaError_t e = lbq::launch_quant_kv(ka, va, tile_begin, tile_end - tile_begin, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "quant_kv launch");
+}
+
+int lbq_quant_kv(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b, int64_t sv_l,
+                 int64_t sv_h, int batch, int heads, int64_t tok0, int seg, int num_segments, int seg_valid,
+                 int seg_len, int64_t kv_len_total, const double* ksum_total, const float* vamax_total,
+                 int8_t* k_codes, float* k_scale, uint8_t* vt_codes, void* km_out, float* v_scale, int write_totals,
+                 void* stream) {
+  if (tok0 < 0) return fail(LBQ_ERR_ARG, "tok0 must be >= 0");
+  return lbq_quant_kv_tiles(k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h, batch, heads, tok0, seg, num_segments,
+                            seg_valid, seg_len, kv_len_total, ksum_total, vamax_total, k_codes, k_scale, vt_codes,
+                            km_out, v_scale, write_totals, 0, seg_valid > 0 ? (seg_valid + 127) / 128 : 0, stream);
 }
 
 size_t lbq_quant_qkv_workspace(int batch, int heads, int64_t kv_len) {
@@ -309,6 +324,99 @@ int lbq_splitkv_combine(const float* o_part, const float* ml_part, int num_split
                      so_b, so_l, so_h, batch, heads, q_len, int(round_up(q_len, 128)), num_splits};
   cudaError_t e = lbq::launch_combine(a, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "splitkv_combine launch");
+}
+
+int lbq_attn_fwd_keys(const int8_t* q_codes, const float* q_scale, int q_len, int q_pad, const int8_t* k_codes,
+                      const float* k_scale, const uint8_t* vt_codes, int num_segments, int seg_len, int batch,
+                      int heads, float sm_scale, const int* range_lt0, const int* range_tiles, const int* range_valid,
+                      const uint64_t* peers, int nranks, int rank, int64_t xchg_off, int part, int64_t recv_o_off,
+                      int64_t recv_ml_off, void* stream) {
+  int r;
+  if ((r = check_ptr("q_codes", q_codes)) || (r = check_ptr("q_scale", q_scale)) || (r = check_ptr("k_codes", k_codes)) ||
+      (r = check_ptr("k_scale", k_scale)) || (r = check_ptr("vt_codes", vt_codes)))
+    return r;
+  if (!range_lt0 || !range_tiles || !range_valid) return fail(LBQ_ERR_ARG, "key ranges are null");
+  if (peers == nullptr) return fail(LBQ_ERR_ARG, "peers table is null");
+  if (nranks < 1 || nranks > lbq::xchg::kMaxRanks || rank < 0 || rank >= nranks)
+    return fail(LBQ_ERR_ARG, "rank %d of %d ranks (at most %d)", rank, nranks, lbq::xchg::kMaxRanks);
+  if (xchg_off < 0 || xchg_off % 256 || recv_o_off < 0 || recv_o_off % 16 || recv_ml_off < 0 || recv_ml_off % 16)
+    return fail(LBQ_ERR_ALIGN, "xchg_off must be a multiple of 256 and the receive offsets of 16 bytes");
+  if (batch <= 0 || heads <= 0 || q_len <= 0 || seg_len <= 0) return fail(LBQ_ERR_ARG, "batch, heads, q_len and seg_len must be positive");
+  if (num_segments < 1 || num_segments > 2) return fail(LBQ_ERR_ARG, "num_segments %d not in [1, 2]", num_segments);
+  if (num_segments > 1 && seg_len % 64)
+    return fail(LBQ_ERR_ARG, "seg_len %d must be a multiple of 64 with several segments", seg_len);
+  if (q_pad % 128 || q_pad < q_len || q_pad > (1 << 30)) return fail(LBQ_ERR_ARG, "q_pad %d must be a multiple of 128 >= q_len %d", q_pad, q_len);
+  if (part <= 0 || part % 128 || int64_t(part) * nranks < q_len)
+    return fail(LBQ_ERR_ARG, "part %d must be a multiple of 128 with part * nranks >= q_len", part);
+  if (int64_t(batch) * heads * num_segments > 65535 * 32) return fail(LBQ_ERR_ARG, "too many batch*heads*segments");
+  const int seg_pad = int(round_up(seg_len, 128));
+  lbq::AttnArgs a{};
+  int tiles = 0;
+  a.range_tile0[0] = 0;
+  for (int s = 0; s < num_segments; ++s) {
+    if (range_valid[s] <= 0 || range_valid[s] > seg_len)
+      return fail(LBQ_ERR_ARG, "range %d: %d valid keys, segment of %d", s, range_valid[s], seg_len);
+    if (range_lt0[s] < 0 || range_tiles[s] < 0 || range_lt0[s] + range_tiles[s] > (range_valid[s] + 127) / 128)
+      return fail(LBQ_ERR_ARG, "range %d: tiles [%d, %d) outside the %d tiles holding valid keys", s, range_lt0[s],
+                  range_lt0[s] + range_tiles[s], (range_valid[s] + 127) / 128);
+    a.range_valid[s] = range_valid[s];
+    a.range_lt0[s] = range_lt0[s];
+    tiles += range_tiles[s];
+    a.range_tile0[s + 1] = tiles;
+  }
+  for (int s = num_segments; s < 2; ++s) {
+    a.range_valid[s] = 0;
+    a.range_lt0[s] = 0;
+    a.range_tile0[s + 1] = tiles;
+  }
+  if (tiles <= 0) return fail(LBQ_ERR_ARG, "empty key range: every rank needs at least one key tile");
+  const uint64_t bhs = uint64_t(batch) * heads;
+  CUtensorMap tq, tk, tv;
+  if ((r = make_map(&tq, q_codes, 128, q_pad, bhs, 128, uint64_t(q_pad) * 128, "q_codes"))) return r;
+  if ((r = make_map(&tk, k_codes, 128, seg_pad, bhs * num_segments, 128, uint64_t(seg_pad) * 128, "k_codes"))) return r;
+  if ((r = make_map(&tv, vt_codes, seg_pad, 128, bhs * num_segments, seg_pad, uint64_t(seg_pad) * 128, "vt_codes")))
+    return r;
+  if (sm_scale <= 0.f) sm_scale = 0.08838834764831845f;   // 128 ** -0.5
+  a.q_scale = q_scale;
+  a.k_scale = k_scale;
+  a.batch = batch;
+  a.heads = heads;
+  a.q_len = q_len;
+  a.q_pad = q_pad;
+  a.kv_len = 0;                 // unused: the ranges carry the valid lengths
+  a.nseg = num_segments;
+  a.seg_len = seg_len;
+  a.seg_pad = seg_pad;
+  a.num_splits = 1;
+  a.tiles_per_split = tiles;
+  a.total_tiles = tiles;
+  a.sm_log2 = sm_scale * 1.4426950408889634f;
+  a.status = lbq::device_status_ptr();
+  a.peers = peers;
+  a.nranks = nranks;
+  a.rank = rank;
+  a.part = part;
+  a.xchg_off = xchg_off;
+  a.recv_o_off = recv_o_off;
+  a.recv_ml_off = recv_ml_off;
+  cudaError_t e = lbq::launch_attn_keys(a, tq, tk, tv, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "attn_fwd (key range) launch");
+}
+
+int lbq_keys_combine(const void* recv_o, const float* recv_ml, int nranks, int part, int rows, const float* v_scale,
+                     int batch, int heads, void* out, int64_t so_b, int64_t so_l, int64_t so_h, void* stream) {
+  int r;
+  if (nranks < 1 || nranks > lbq::xchg::kMaxRanks || batch <= 0 || heads <= 0 || rows < 0 || part <= 0 || rows > part)
+    return fail(LBQ_ERR_ARG, "nranks %d, batch %d, heads %d, rows %d, part %d out of range", nranks, batch, heads,
+                rows, part);
+  if (rows == 0) return LBQ_OK;               // an empty query slice: nothing to merge (out may be empty)
+  if ((r = check_ptr("recv_o", recv_o)) || (r = check_ptr("recv_ml", recv_ml)) || (r = check_ptr("v_scale", v_scale)))
+    return r;
+  if ((r = check_act("out", out, so_b, so_l, so_h))) return r;
+  lbq::KeysCombineArgs a{static_cast<const __half*>(recv_o), reinterpret_cast<const float2*>(recv_ml), v_scale,
+                         static_cast<__nv_bfloat16*>(out), so_b, so_l, so_h, batch, heads, rows, part, nranks};
+  cudaError_t e = lbq::launch_keys_combine(a, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "keys_combine launch");
 }
 
 }  // extern "C"

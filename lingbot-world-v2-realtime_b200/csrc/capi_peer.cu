@@ -200,6 +200,24 @@ int lbq_share_quant_push(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h
   return e == cudaSuccess ? LBQ_OK : set_error(LBQ_ERR_CUDA, "code push launch: %s", cudaGetErrorString(e));
 }
 
+int lbq_q_push(const int8_t* q_codes, const float* q_scale, int rows_pad, int row0, int q_pad, int batch, int heads,
+               int64_t q_off, int64_t q_scale_off, const uint64_t* peers, int nranks, int rank, int64_t xchg_off,
+               int ctas, void* stream) {
+  int r;
+  if ((r = check_group(peers, nranks, rank, xchg_off)) || (r = check_dims(batch, heads, 1))) return r;
+  if (q_codes == nullptr || q_scale == nullptr) return set_error(LBQ_ERR_ARG, "query codes are null");
+  if (!aligned16(q_codes) || !aligned16(q_scale)) return set_error(LBQ_ERR_ALIGN, "query codes not 16-byte aligned");
+  if (rows_pad < 0 || rows_pad % 128 || row0 < 0 || row0 % 128 || q_pad % 128 || row0 + rows_pad > q_pad)
+    return set_error(LBQ_ERR_ARG, "rows [%d, %d) of %d: all multiples of 128 and inside", row0, row0 + rows_pad, q_pad);
+  if (q_off < 0 || q_off % 16 || q_scale_off < 0 || q_scale_off % 16)
+    return set_error(LBQ_ERR_ALIGN, "heap offsets must be non-negative multiples of 16 bytes");
+  if (ctas < 0 || ctas > 65535) return set_error(LBQ_ERR_ARG, "ctas %d outside [0, 65535]", ctas);
+  lbq::QPushArgs a{q_codes, q_scale, rows_pad, row0, q_pad, batch, heads, q_off, q_scale_off, peers, nranks, rank,
+                   xchg_off};
+  cudaError_t e = lbq::launch_q_push(a, ctas > 0 ? ctas : 32, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LBQ_OK : set_error(LBQ_ERR_CUDA, "q_push launch: %s", cudaGetErrorString(e));
+}
+
 int lbq_peer_wait(const uint64_t* peers, int nranks, int rank, int64_t xchg_off, int signals, uint64_t timeout_ns,
                   void* stream) {
   int r;

@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -79,6 +80,44 @@ struct AttnArgs {
   int num_splits, tiles_per_split, total_tiles;
   float sm_log2;              // softmax scale * log2(e)
   int* status;                // device status word (timeouts)
+  // Key-range mode only (attn_fwd_kernel<true>): the CTA's key tiles are one piece per code segment;
+  // piece s is tiles [range_tile0[s], range_tile0[s + 1]) of the tile sequence, i.e. tiles
+  // range_lt0[s] + ... of segment s, whose keys >= range_valid[s] are masked. The output is a partial
+  // (O / row sum as fp16 V-code units, and the row's (max, sum)) stored into this rank's receive slot
+  // at the rank that owns the query tile, through peer memory.
+  int range_valid[2];
+  int range_tile0[3];
+  int range_lt0[2];
+  const uint64_t* peers;
+  int nranks, rank;
+  int part;                   // query rows per owner rank (multiple of 128)
+  int64_t xchg_off;
+  int64_t recv_o_off;         // heap offset of the receive slots [ranks][B*H][part][128] fp16
+  int64_t recv_ml_off;        //                                  [ranks][B*H][part] float2
+};
+
+// Merge of the key-range partials a rank received for its query rows (flash-decoding merge).
+struct KeysCombineArgs {
+  const __half* recv_o;       // [ranks][B*H][part][128]
+  const float2* recv_ml;      // [ranks][B*H][part]
+  const float* v_scale;       // [B*H][128]
+  __nv_bfloat16* out;         // [B, rows, H, 128] with the strides below
+  int64_t so_b, so_l, so_h;
+  int batch, heads, rows, part, nranks;
+};
+
+// This rank's query-slice codes (a [B][H][rows_pad][128] buffer and its [B][H][rows_pad/32] scales)
+// into row `row0` of every rank's full query buffers ([B][H][q_pad][128] at heap offset q_off and
+// [B][H][q_pad/32] at q_scale_off), this rank's own included.
+struct QPushArgs {
+  const int8_t* q_codes;
+  const float* q_scale;
+  int rows_pad, row0, q_pad;
+  int batch, heads;
+  int64_t q_off, q_scale_off;
+  const uint64_t* peers;
+  int nranks, rank;
+  int64_t xchg_off;
 };
 
 struct CombineArgs {
@@ -98,7 +137,8 @@ constexpr int64_t kSeenData = 96;     // u32[8]  share signals consumed (local)
 constexpr int64_t kCall = 128;        // u32     calls completed: totals tag - 1 and slot parity (local)
 constexpr int64_t kDone = 132;        // u32     chunk_totals CTAs finished this call (local)
 constexpr int64_t kDonePush = 136;    // u32     share_push CTAs finished this launch (local)
-constexpr int64_t kDoneQuant = 140;   // u32     share_quant_push CTAs finished this launch (local)
+constexpr int64_t kDoneQuant = 140;   // u32     share_quant_push / q_push CTAs finished this launch (local)
+constexpr int64_t kDoneAttn = 144;    // u32     key-range attention CTAs finished this launch (local)
 constexpr int64_t kSlots = 256;       // u64 tagged words [2 parity][ranks][3][B*H*128]
 constexpr int kPushCtas = 148;        // default share_push grid (persistent)
 __host__ __device__ inline int64_t slot_word(uint32_t par, int nranks, int r, int w, int64_t cols) {
@@ -182,6 +222,10 @@ cudaError_t launch_quant_kv(const QuantKArgs& ka, const QuantVArgs& va, int tile
 cudaError_t launch_attn(const AttnArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                         const CUtensorMap& tm_v, cudaStream_t st);
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st);
+cudaError_t launch_attn_keys(const AttnArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                             const CUtensorMap& tm_v, cudaStream_t st);
+cudaError_t launch_keys_combine(const KeysCombineArgs& a, cudaStream_t st);
+cudaError_t launch_q_push(const QPushArgs& a, int ctas, cudaStream_t st);
 cudaError_t launch_share_totals_push(const ShareTotalsArgs& a, cudaStream_t st);
 cudaError_t launch_chunk_totals(const ChunkTotalsArgs& a, cudaStream_t st);
 cudaError_t launch_share_push(const SharePushArgs& a, cudaStream_t st);

@@ -17,6 +17,9 @@
 //   share_push         copies this rank's bf16 K/V share and its block statistics into every rank's
 //                      cache replica and tables (calls whose K/V persist), then one signal per rank.
 //   peer_wait          waits for every other rank's signals of this call.
+//   q_push             (key-range split) this rank's query-slice codes into every rank's full query
+//                      buffers, then one signal per rank; the partials come back from the attention
+//                      kernel itself (attn.cu, key-range variant) and are merged by keys_combine.
 //
 // The totals travel as tagged words: each 8-byte store carries 32 data bits and the call's tag (call
 // counter + 1, kept on the device by every rank in lockstep), so the receiver polls the data itself.
@@ -256,6 +259,50 @@ __global__ void __launch_bounds__(256) code_push_kernel(CodePushArgs a) {
   signal_after_last_cta(a.peers, a.nranks, a.rank, a.xchg_off, xchg::kDoneQuant);
 }
 
+// ------------------------------------------------------------------ query-slice codes -> every rank
+// Key-range split: every rank attends every query row against its own keys, so each rank's query-slice
+// codes (quantized locally into a [B][H][rows_pad][128] buffer) and scales go to rows [row0, row0 +
+// rows_pad) of every rank's full query buffers, this rank's own included, in 16-byte pieces (CTAs start
+// on different ranks); then one signal per other rank.
+__global__ void __launch_bounds__(256) q_push_kernel(QPushArgs a) {
+  const int64_t bh_rows = int64_t(a.batch) * a.heads;
+  const int64_t code_row = int64_t(a.rows_pad) * 8;    // 16-byte pieces of one (b, h) block of codes
+  const int64_t scale_row = a.rows_pad / 128;          // 16-byte pieces of its rows_pad / 32 scales
+  const int64_t pc = bh_rows * code_row, total = pc + bh_rows * scale_row;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  const char* codes = reinterpret_cast<const char*>(a.q_codes);
+  const char* scales = reinterpret_cast<const char*>(a.q_scale);
+  for (int64_t g0 = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; g0 < total; g0 += 4 * stride) {
+    uint4 val[4];
+    int64_t off[4];                                    // byte offset of the destination in every heap
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t g = g0 + i * stride;
+      off[i] = -1;
+      if (g < total) {
+        const char* src;
+        if (g < pc) {
+          const int64_t row = g / code_row, col = g - row * code_row;
+          src = codes + row * a.rows_pad * 128 + col * 16;
+          off[i] = a.q_off + (row * a.q_pad + a.row0) * 128 + col * 16;
+        } else {
+          const int64_t gs = g - pc, row = gs / scale_row, col = gs - row * scale_row;
+          src = scales + row * (a.rows_pad / 8) + col * 16;
+          off[i] = a.q_scale_off + row * (a.q_pad / 8) + a.row0 / 8 + col * 16;
+        }
+        val[i] = *reinterpret_cast<const uint4*>(src);
+      }
+    }
+    for (int q = 0; q < a.nranks; ++q) {
+      char* dst = heap(a.peers, (a.rank + q + int(blockIdx.x)) % a.nranks);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (off[i] >= 0) *reinterpret_cast<uint4*>(dst + off[i]) = val[i];
+    }
+  }
+  signal_after_last_cta(a.peers, a.nranks, a.rank, a.xchg_off, xchg::kDoneQuant);
+}
+
 // ------------------------------------------------------------------ wait for the other ranks' shares
 __global__ void __launch_bounds__(32) peer_wait_kernel(PeerWaitArgs a) {
   const int t = threadIdx.x;
@@ -291,6 +338,11 @@ cudaError_t launch_share_push(const SharePushArgs& a, cudaStream_t st) {
 cudaError_t launch_code_push(const CodePushArgs& a, int ctas, cudaStream_t st) {
   if (cudaError_t e0 = prefer_max_shared<code_push_kernel>(); e0 != cudaSuccess) return e0;
   code_push_kernel<<<ctas, 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t launch_q_push(const QPushArgs& a, int ctas, cudaStream_t st) {
+  if (cudaError_t e0 = prefer_max_shared<q_push_kernel>(); e0 != cudaSuccess) return e0;
+  q_push_kernel<<<ctas, 256, 0, st>>>(a);
   return cudaGetLastError();
 }
 cudaError_t launch_peer_wait(const PeerWaitArgs& a, cudaStream_t st) {

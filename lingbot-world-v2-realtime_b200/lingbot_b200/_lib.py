@@ -46,6 +46,12 @@ SIGNATURES = {
                                     _i32, _i32, _i32, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _i32,
                                     _i32, _i64, _i32, _vp]),
     "lbq_peer_wait": (_i32, [_vp, _i32, _i32, _i64, _i32, _u64, _vp]),
+    "lbq_quant_kv_tiles": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _i32, _i64, _i32, _i32, _i32,
+                                  _i32, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
+    "lbq_attn_fwd_keys": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp,
+                                 _vp, _i32, _i32, _i64, _i32, _i64, _i64, _vp]),
+    "lbq_keys_combine": (_i32, [_vp, _vp, _i32, _i32, _i32, _vp, _i32, _i32, _vp, _i64, _i64, _i64, _vp]),
+    "lbq_q_push": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _i64, _vp, _i32, _i32, _i64, _i32, _vp]),
 }
 
 _lock = threading.Lock()

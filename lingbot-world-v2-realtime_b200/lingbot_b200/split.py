@@ -224,6 +224,41 @@ class SplitAttention:
             raise ValueError(f"cache of {lk} tokens cannot hold {self.mem_len} memory + {self.n} chunk tokens")
         return self.heap.offset(k), self.heap.offset(cache["v"]), lk
 
+    def _group(self):
+        from . import ops
+        return (ops._ptr(self.heap.peers), self.world, self.rank, self.xchg_off)
+
+    @staticmethod
+    def _share(k_part, v_part):
+        from . import ops
+        return (ops._ptr(k_part), *k_part.stride()[:3], ops._ptr(v_part), *v_part.stride()[:3])
+
+    def _codes(self):
+        from . import ops
+        return (ops._ptr(self.tot_ksum), ops._ptr(self.tot_vamax), ops._ptr(self.k_codes), ops._ptr(self.k_scale),
+                ops._ptr(self.vt_codes), ops._ptr(self.km), ops._ptr(self.v_scale))
+
+    def _window_totals(self, cache, k_part, v_part, stp):
+        """Steps 1-2 of a call: the share's block statistics into this rank's tables, its per-channel
+        totals to every rank, and the window totals (memory + every share in rank order, identical on
+        every rank) into tot_ksum / tot_vamax."""
+        from . import _lib, ops
+        if k_part.shape[1] < self.share_valid or v_part.shape[1] < self.share_valid:
+            raise ValueError(f"shares of {k_part.shape[1]} tokens, expected {self.part}")
+        b, h = self.b, self.h
+        ksum, vamax = cache["lbq_ksum"], cache["lbq_vamax"]
+        max_blocks = ksum.shape[1]
+        row0 = (self.mem_len + self._lo) // 64
+        nb_valid = (self.share_valid + 63) // 64
+        group = self._group()
+        if nb_valid > 0:
+            _lib.call("lbq_kv_block_stats", *self._share(k_part, v_part), b, h, self.share_valid, 0, nb_valid,
+                      max_blocks, ksum.data_ptr() + row0 * h * 128 * 8, vamax.data_ptr() + row0 * h * 128 * 4, stp)
+        _lib.call("lbq_share_totals_push", ops._ptr(ksum), ops._ptr(vamax), max_blocks, row0, nb_valid, b, h,
+                  *group, stp)
+        _lib.call("lbq_chunk_totals", *group, b, h, ops._ptr(cache["lbq_mem_ksum"]), ops._ptr(cache["lbq_mem_vamax"]),
+                  ops._ptr(self.tot_ksum), ops._ptr(self.tot_vamax), self.timeout_ns, stp)
+
     def __call__(self, q_rows, cache, k_part, v_part, out, sm_scale=None, num_splits=None, attn_events=None,
                  persist=True):
         """q_rows [B, rows, H, 128] (this rank's query slice), k_part/v_part [B, part, H, 128] (this rank's
@@ -234,31 +269,17 @@ class SplitAttention:
         st = torch.cuda.current_stream()
         stp = st.cuda_stream
         b, h = self.b, self.h
-        if k_part.shape[1] < self.share_valid or v_part.shape[1] < self.share_valid:
-            raise ValueError(f"shares of {k_part.shape[1]} tokens, expected {self.part}")
         k_off, v_off, lk = self._check_cache(cache)
         ksum, vamax = cache["lbq_ksum"], cache["lbq_vamax"]
         max_blocks = ksum.shape[1]
-        row0 = (self.mem_len + self._lo) // 64
-        nb_valid = (self.share_valid + 63) // 64
-        peers = ops._ptr(self.heap.peers)
-        group = (peers, self.world, self.rank, self.xchg_off)
-        share = (ops._ptr(k_part), *k_part.stride()[:3], ops._ptr(v_part), *v_part.stride()[:3])
+        group = self._group()
+        share = self._share(k_part, v_part)
         kv_len = self.mem_len + self.n
         rows = q_rows.shape[1]
         nseg = self.nseg
-        codes = (ops._ptr(self.tot_ksum), ops._ptr(self.tot_vamax), ops._ptr(self.k_codes), ops._ptr(self.k_scale),
-                 ops._ptr(self.vt_codes), ops._ptr(self.km), ops._ptr(self.v_scale))
-        # 1. block statistics of the share into this rank's tables
-        if nb_valid > 0:
-            _lib.call("lbq_kv_block_stats", *share, b, h, self.share_valid, 0, nb_valid, max_blocks,
-                      ksum.data_ptr() + row0 * h * 128 * 8, vamax.data_ptr() + row0 * h * 128 * 4, stp)
-        # 2. the share's totals -> every rank; every rank's totals -> the window totals (identical on
-        # every rank)
-        _lib.call("lbq_share_totals_push", ops._ptr(ksum), ops._ptr(vamax), max_blocks, row0, nb_valid, b, h,
-                  *group, stp)
-        _lib.call("lbq_chunk_totals", *group, b, h, ops._ptr(cache["lbq_mem_ksum"]), ops._ptr(cache["lbq_mem_vamax"]),
-                  ops._ptr(self.tot_ksum), ops._ptr(self.tot_vamax), self.timeout_ns, stp)
+        codes = self._codes()
+        # 1.-2. block statistics of the share, window totals
+        self._window_totals(cache, k_part, v_part, stp)
         # 3. side stream: the share's codes (and, persisting, its bf16) -> every rank; the query slice
         self.fork.record(st)
         self.side.wait_event(self.fork)
@@ -300,3 +321,156 @@ class SplitAttention:
         rows = self.q_rows > 0
         return (int(self.share_valid > 0) + 2 + 1 + int(self.world > 1) + int(bool(persist)) + int(rows)
                 + int(self.mem_len > 0) + 1 + int(rows) + int(num_splits > 1 and rows))
+
+
+def key_tiles(mem_len, world, rank):
+    """Rank `rank`'s 128-token tiles [t0, t1) of the memory segment under the key-range split: the
+    ceil(mem_len / 128) tiles dealt out contiguously, as evenly as whole tiles allow."""
+    tiles = -(-mem_len // 128)
+    return rank * tiles // world, (rank + 1) * tiles // world
+
+
+class KeySplitAttention(SplitAttention):
+    """One rank's self-attention for one layer of a chunk under the key-range split: the rank attends
+    EVERY query row of the chunk, but only against its own keys — its slice of the memory part
+    (`key_tiles`) and its own share of the chunk — and sends each query tile's partial result to the
+    rank that owns those rows, which merges the partials of all ranks.
+
+    Against the query split (SplitAttention) this removes the one step that does not shrink with N: the
+    re-quantization of the whole memory part on every rank (Sage's codes depend on the window-global K
+    mean and V absmax, so memory codes change with every call). Here a rank quantizes 1/N of the memory
+    and its own share and never sends K/V codes; the exchange is the query codes (all-gathered through
+    peer memory) and the partial outputs (fp16 O / row sum plus the row's (max, sum), stored by the
+    attention kernel itself into the owner's receive slots). Codes are identical to quantizing the whole
+    window in one piece; the merged output equals the split-KV combine over N key ranges.
+
+    Per call, on this rank (every launch on the current stream or one forked side stream, no host
+    synchronisation, so a call can be captured in a CUDA graph):
+
+      1.-2. block statistics of the share and window totals, as SplitAttention;
+      3. side stream: lbq_quant_q of the query slice, lbq_q_push into every rank's full query buffers,
+         lbq_share_push (persist=True) of the bf16 share into every rank's cache replica;
+         main stream: lbq_quant_kv_tiles of this rank's memory tiles and of its chunk share;
+      4. lbq_peer_wait (query codes, shares);
+      5. lbq_attn_fwd_keys — partials into the owners' receive slots, then a signal per rank;
+      6. lbq_peer_wait (partials); lbq_keys_combine -> this rank's output rows.
+
+    Requirements beyond SplitAttention's: with a memory part, at least one memory tile per rank; without
+    one, a non-empty chunk share per rank (every rank needs a key tile).
+    """
+
+    @staticmethod
+    def heap_bytes(batch, heads, mem_len, n_tokens, world):
+        """Peer-heap bytes this object carves: SplitAttention's plus the full query buffers and the
+        receive slots."""
+        part = share_part(n_tokens, world)
+        q_pad = world * part
+        up = lambda x: (x + 255) // 256 * 256  # noqa: E731
+        bh = batch * heads
+        return (SplitAttention.heap_bytes(batch, heads, mem_len, n_tokens, world) + up(bh * q_pad * 128)
+                + up(bh * q_pad // 32 * 4) + up(world * bh * part * 128 * 2) + up(world * bh * part * 8))
+
+    def __init__(self, batch, heads, q_rows, mem_len, n_tokens, device, heap, group=None, timeout_s=4.0):
+        super().__init__(batch, heads, q_rows, mem_len, n_tokens, device, heap, group=group, timeout_s=timeout_s)
+        if mem_len > 0 and -(-mem_len // 128) < self.world:
+            raise ValueError(f"a {mem_len}-token memory part has fewer 128-token tiles than {self.world} ranks")
+        if mem_len == 0 and n_tokens <= (self.world - 1) * self.part:
+            raise ValueError(f"a {n_tokens}-token chunk leaves rank {self.world - 1} without keys")
+        self.q_pad = self.world * self.part
+        bh = batch * heads
+        self.mem_tiles = key_tiles(mem_len, self.world, self.rank) if mem_len > 0 else (0, 0)
+        self.q_all = heap.carve((batch, heads, self.q_pad, 128), torch.int8)
+        self.q_all_scale = heap.carve((batch, heads, self.q_pad // 32), torch.float32)
+        self.recv_o = heap.carve((self.world, bh, self.part, 128), torch.float16)
+        self.recv_ml = heap.carve((self.world, bh, self.part, 2), torch.float32)
+        self.q_ctas = 32          # CTAs of the query-code push (few: it runs beside the quantizers)
+
+    def ranges(self):
+        """(tile start, tiles, valid keys) of each code segment this rank attends."""
+        chunk_t0 = self._lo // 128
+        chunk = (chunk_t0, -(-(self._lo + self.share_valid) // 128) - chunk_t0 if self.share_valid else 0, self.n)
+        if self.mem_len == 0:
+            return [chunk]
+        m0, m1 = self.mem_tiles
+        return [(m0, m1 - m0, self.mem_len), chunk]
+
+    def __call__(self, q_rows, cache, k_part, v_part, out, sm_scale=None, num_splits=None, attn_events=None,
+                 persist=True):
+        """q_rows [B, rows, H, 128] (this rank's query slice, rows = its share of the chunk), k_part /
+        v_part [B, part, H, 128] (its share, rows past the chunk's end ignored) -> out [B, rows, H, 128].
+        `num_splits` is ignored (one partial per rank). persist=True also lands the whole chunk in every
+        rank's `cache` at [mem_len, mem_len + n_tokens), as kv_cache.write would."""
+        import ctypes
+        from . import _lib, ops
+        st = torch.cuda.current_stream()
+        stp = st.cuda_stream
+        b, h = self.b, self.h
+        k_off, v_off, lk = self._check_cache(cache)
+        ksum, vamax = cache["lbq_ksum"], cache["lbq_vamax"]
+        max_blocks = ksum.shape[1]
+        group = self._group()
+        share = self._share(k_part, v_part)
+        kv_len = self.mem_len + self.n
+        rows = q_rows.shape[1]
+        if rows > self.part:
+            raise ValueError(f"{rows} query rows, the slice holds {self.part}")
+        nseg = self.nseg
+        codes = self._codes()
+        # 1.-2. block statistics of the share, window totals
+        self._window_totals(cache, k_part, v_part, stp)
+        # 3. side stream: the query slice -> every rank (and, persisting, the bf16 share)
+        self.fork.record(st)
+        self.side.wait_event(self.fork)
+        sst = self.side.cuda_stream
+        rows_pad = ops.round_up(rows, 128)
+        if rows > 0:
+            _lib.call("lbq_quant_q", ops._ptr(q_rows), *q_rows.stride()[:3], b, h, rows, ops._ptr(self.q_codes),
+                      ops._ptr(self.q_scale), sst)
+        _lib.call("lbq_q_push", ops._ptr(self.q_codes), ops._ptr(self.q_scale), rows_pad, self.rank * self.part,
+                  self.q_pad, b, h, self.heap.offset(self.q_all), self.heap.offset(self.q_all_scale), *group,
+                  self.q_ctas, sst)
+        if persist:
+            _lib.call("lbq_share_push", *share, b, h, self.share_valid, self.nb_part, *group, k_off, v_off, lk,
+                      self.mem_len + self._lo, self.heap.offset(ksum), self.heap.offset(vamax), max_blocks,
+                      self.push_ctas, sst)
+        self.join.record(self.side)
+        # ... while this rank's keys are quantized here: its memory tiles, then its chunk share
+        if self.mem_len > 0:
+            m0, m1 = self.mem_tiles
+            kc, vc = cache["k"], cache["v"]
+            _lib.call("lbq_quant_kv_tiles", ops._ptr(kc), *kc.stride()[:3], ops._ptr(vc), *vc.stride()[:3], b, h, 0, 0,
+                      nseg, self.mem_len, self.mem_len, kv_len, *codes, 1, m0, m1, stp)
+        if self.share_valid > 0:
+            t0 = self._lo // 128
+            _lib.call("lbq_quant_kv_tiles", *share, b, h, -self._lo, nseg - 1, nseg, self._lo + self.share_valid,
+                      self.seg_len, kv_len, *codes, int(self.mem_len == 0), t0,
+                      -(-(self._lo + self.share_valid) // 128), stp)
+        # 4. every rank's query codes (and shares) have landed
+        st.wait_event(self.join)
+        _lib.call("lbq_peer_wait", *group, 1 + int(bool(persist)), self.timeout_ns, stp)
+        # 5. partials of every query tile over this rank's keys -> the tiles' owners
+        rg = self.ranges()
+        arr = ctypes.c_int * len(rg)
+        if attn_events is not None:
+            attn_events[0].record()
+        _lib.call("lbq_attn_fwd_keys", ops._ptr(self.q_all), ops._ptr(self.q_all_scale), self.n, self.q_pad,
+                  ops._ptr(self.k_codes), ops._ptr(self.k_scale), ops._ptr(self.vt_codes), nseg, self.seg_len, b, h,
+                  float(sm_scale or 0.0), arr(*[r[0] for r in rg]), arr(*[r[1] for r in rg]),
+                  arr(*[r[2] for r in rg]), *group, self.part, self.heap.offset(self.recv_o),
+                  self.heap.offset(self.recv_ml), stp)
+        if attn_events is not None:
+            attn_events[1].record()
+        # 6. every rank's partials for this rank's rows -> out
+        _lib.call("lbq_peer_wait", *group, 1, self.timeout_ns, stp)
+        if rows > 0:
+            _lib.call("lbq_keys_combine", ops._ptr(self.recv_o), ops._ptr(self.recv_ml), self.world, self.part, rows,
+                      ops._ptr(self.v_scale), b, h, ops._ptr(out), *out.stride()[:3], stp)
+        return out
+
+    def launches(self, num_splits=1, persist=True):
+        """Our kernels per call: share block stats, totals push, window totals, Q quantizer, query push,
+        bf16 share push (persist), memory-tile quantizer, share quantizer, peer wait, attention, peer
+        wait, combine."""
+        rows = self.q_rows > 0
+        return (int(self.share_valid > 0) + 2 + int(rows) + 1 + int(bool(persist)) + int(self.mem_len > 0)
+                + int(self.share_valid > 0) + 1 + 1 + 1 + int(rows))

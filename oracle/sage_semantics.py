@@ -124,7 +124,8 @@ def quantize_qkv(q, k, v):
 
 
 def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_scale=None,
-                    tile=BLK_K, pv_accum="fp16", rows=None, heads=None, splits=1):
+                    tile=BLK_K, pv_accum="fp16", rows=None, heads=None, splits=1, key_ranges=None,
+                    partial_fp16=False):
     """Torch emulation of Sage's `qk_int8_sv_f8_accum_f16_fuse_v_scale_attn_inst_buf` (the call at
     sage_preq.py:126-127 / sage_kvq.py:107-110), non-causal, per-warp Q granularity.
 
@@ -141,6 +142,11 @@ def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_sca
     `splits` > 1 emulates split-KV (splitkv/README.md:36-69): the key tiles are cut into `splits`
     contiguous ranges (ceil division, empty ranges dropped), each runs the loop above from a fresh
     running max, and the partials merge as out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) d_s.
+    `key_ranges` replaces the split ranges with the key-range sequence split: one partial per rank,
+    each a list of (lo, hi) key ranges that the rank's loop runs through in order with one running
+    max (its memory tiles, then its chunk share). With `partial_fp16` each partial travels as
+    fp16(O_s / d_s) with (m_s, d_s), and the merge is out = sum_s w_s fp16(O_s / d_s) / sum_s w_s with
+    w_s = 2^(m_s - M) d_s.
     """
     b, lq, h, d = q_codes.shape
     lk = k_codes.shape[1]
@@ -154,20 +160,30 @@ def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_sca
     off = torch.tensor(S_FP8_OFFSET, dtype=torch.float32)
     ntiles = (lk + tile - 1) // tile
     per = (ntiles + splits - 1) // splits
-    ranges = [(s0 * tile, min(lk, (s0 + per) * tile)) for s0 in range(0, ntiles, per)]
+    partials = [[(s0 * tile, min(lk, (s0 + per) * tile))] for s0 in range(0, ntiles, per)]
+    if key_ranges is not None:
+        partials = [[(lo, hi_) for lo, hi_ in pieces if hi_ > lo] for pieces in key_ranges]
+        partials = [p for p in partials if p]
     for bi in range(b):
         for hi in heads:
             qf = q_codes[bi, rows, hi].float()                          # [R, D]
             qs = q_scale[bi, hi][rows // WARP_Q]                         # [R]
             kf = k_codes[bi, :, hi].float()                             # [Lk, D]
             vf = vq_all[bi, :, hi]                                       # [Lk, D]
-            parts = [_attn_range(qf, qs, kf, vf, k_scale[bi, hi], lo, hi_, tile, pv_accum, sm_log2, off)
-                     for lo, hi_ in ranges]
+            parts = []
+            for pieces in partials:
+                state = None
+                for lo, hi_ in pieces:
+                    state = _attn_range(qf, qs, kf, vf, k_scale[bi, hi], lo, hi_, tile, pv_accum, sm_log2, off,
+                                        state)
+                parts.append(state)
             mx = torch.stack([p[0] for p in parts]).max(dim=0).values
             acc = torch.zeros(qf.shape[0], d)
             dsum = torch.zeros(qf.shape[0])
             for m_s, d_s, o_s in parts:
                 w = torch.exp2((m_s - mx) * sm_log2)
+                if partial_fp16:
+                    o_s = (o_s / d_s[:, None]).half().float() * d_s[:, None]
                 acc += w[:, None] * o_s
                 dsum += w * d_s
             o = acc * (1.0 / dsum)[:, None] * v_scale[bi, hi][None, :]
@@ -175,12 +191,16 @@ def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_sca
     return out
 
 
-def _attn_range(qf, qs, kf, vf, ks_all, lo, hi, tile, pv_accum, sm_log2, off):
-    """The kernel loop over keys [lo, hi): returns (running max m, row sum d, unnormalized O)."""
+def _attn_range(qf, qs, kf, vf, ks_all, lo, hi, tile, pv_accum, sm_log2, off, state=None):
+    """The kernel loop over keys [lo, hi), continuing from `state` (running max m, row sum d,
+    unnormalized O) when given: returns the updated (m, d, O)."""
     r, d = qf.shape[0], vf.shape[1]
-    m = torch.full((r,), -math.inf)
-    dsum = torch.zeros(r)
-    acc = torch.zeros(r, d)
+    if state is None:
+        m = torch.full((r,), -math.inf)
+        dsum = torch.zeros(r)
+        acc = torch.zeros(r, d)
+    else:
+        m, dsum, acc = state
     for t0 in range(lo, hi, tile):
         t1 = min(t0 + tile, hi)
         s_int = qf @ kf[t0:t1].T                                 # exact integers

@@ -1,7 +1,9 @@
 """One rank of the multi-GPU SplitAttention check (launched by tests/test_split_gpu.py with
 torch.distributed.run, one process per GPU). Every rank builds the same inputs, attends its query slice
 through the peer-memory split (eagerly, then from a CUDA graph) and compares it with the single-GPU
-quantized attention of the whole window; prints "RANK OK" on success."""
+quantized attention of the whole window; prints "RANK OK" on success. With --keys (launched by
+tests/test_keysplit_gpu.py) the split is KeySplitAttention, whose output matches within tolerance
+(per-rank key-range partials) instead of bit for bit."""
 import datetime
 import os
 import sys
@@ -21,9 +23,12 @@ def main():
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
     world, rank = dist.get_world_size(), dist.get_rank()
     from lingbot_b200 import _lib, kv_cache, ops, peer, split
+    from oracle import sage_semantics as O
+    keys = "--keys" in sys.argv
+    cls = split.KeySplitAttention if keys else split.SplitAttention
     H, mem, n, L = 3, 1280, 700, 2
     heap = peer.PeerHeap(kv_cache.heap_bytes(L, [1, mem + n, H, 128], torch.bfloat16)
-                         + split.SplitAttention.heap_bytes(1, H, mem, n, world), dev)
+                         + cls.heap_bytes(1, H, mem, n, world), dev)
     caches = kv_cache.allocate(L, [1, mem + n, H, 128], torch.bfloat16, dev, heap=heap)
     g = torch.Generator().manual_seed(3)
     for kc in caches:
@@ -31,7 +36,7 @@ def main():
         kc["v"][:, :mem] = torch.randn(1, mem, H, 128, generator=g).bfloat16().to(dev)
         kv_cache.refresh_stats(kc, 0, mem)
     r0, r1 = split.shard_rows(n, world, rank)
-    sp = split.SplitAttention(1, H, r1 - r0, mem, n, dev, heap)
+    sp = cls(1, H, r1 - r0, mem, n, dev, heap)
     assert sp.lo == r0 and sp.share_valid == r1 - r0
     for kc in caches:
         sp.memory_changed(kc)
@@ -55,7 +60,11 @@ def main():
         w = ops.quantize_qkv(q, torch.cat([kc["k"][:, :mem], k], 1), torch.cat([kc["v"][:, :mem], v], 1))
         ref = ops.attn_from_codes(w)
         torch.cuda.synchronize()
-        assert torch.equal(out_rows, ref[:, r0:r1]), "split output differs from the one-GPU output"
+        if keys:
+            m = O.compare(out_rows.float().cpu(), ref[:, r0:r1].float().cpu())
+            assert m["cos"] >= 0.9995 and m["max_abs"] <= 2e-2, f"key split far from the one-GPU output: {m}"
+        else:
+            assert torch.equal(out_rows, ref[:, r0:r1]), "split output differs from the one-GPU output"
 
     # eager calls over both layers (denoise passes do not persist their K/V)
     for seed in range(3):

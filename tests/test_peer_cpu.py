@@ -112,15 +112,16 @@ def one_rank_gloo():
     dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("cls", [split.SplitAttention, split.KeySplitAttention], ids=["queries", "keys"])
 @pytest.mark.parametrize("mem,n,heads,layers", [(24128, 6032, 12, 2), (640, 300, 2, 3), (0, 300, 2, 1)])
-def test_heap_bytes_cover_the_caches_and_the_split(one_rank_gloo, mem, n, heads, layers):
-    """kv_cache.heap_bytes + SplitAttention.heap_bytes is exactly what the carves take."""
+def test_heap_bytes_cover_the_caches_and_the_split(one_rank_gloo, cls, mem, n, heads, layers):
+    """kv_cache.heap_bytes + <split>.heap_bytes is exactly what the carves take."""
     need = kv_cache.heap_bytes(layers, [1, mem + n, heads, 128], torch.bfloat16)
-    need += split.SplitAttention.heap_bytes(1, heads, mem, n, 1)
+    need += cls.heap_bytes(1, heads, mem, n, 1)
     heap = peer.PeerHeap(need, torch.device("cpu"))
     heap.nbytes = need                        # no slack from the 2 MiB rounding
     caches = kv_cache.allocate(layers, [1, mem + n, heads, 128], torch.bfloat16, "cpu", heap=heap)
-    sp = split.SplitAttention(1, heads, n, mem, n, torch.device("cpu"), heap)
+    sp = cls(1, heads, n, mem, n, torch.device("cpu"), heap)
     assert heap.top <= need
     for c in caches:
         for key in ("k", "v", "lbq_ksum", "lbq_vamax"):
