@@ -543,25 +543,39 @@ __global__ void __launch_bounds__(128) splitkv_combine_kernel(const CombineArgs 
 // Merge of the key-range partials this rank received for its query rows: slot s holds rank s's
 // O / row sum (fp16) and (max, sum) over rank s's keys; out = sum_s w_s o_s / sum_s w_s * v_scale with
 // w_s = exp2(max_s - max) * sum_s (the split-KV merge of splitkv/README.md:60-69 on normalised
-// partials). One warp per (row, batch*head), 4 channels per lane.
+// partials). One warp per (row, batch*head), 4 channels per lane; every slot's loads are issued before
+// any arithmetic (up to kMaxRanks slots).
 __global__ void __launch_bounds__(128) keys_combine_kernel(const KeysCombineArgs a) {
+  constexpr int kMax = xchg::kMaxRanks;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 4 + warp;
   const int bh = blockIdx.y;
   if (row >= a.rows) return;
-  const int bhs = a.batch * a.heads;
+  const int64_t slot_rows = int64_t(a.batch) * a.heads * a.part;   // rows of one rank's slot
+  const int64_t prow0 = int64_t(bh) * a.part + row;
+  float2 ml[kMax];
+  uint2 raw[kMax];
+#pragma unroll
+  for (int s = 0; s < kMax; ++s) {
+    if (s < a.nranks) {
+      ml[s] = a.recv_ml[s * slot_rows + prow0];
+      raw[s] = reinterpret_cast<const uint2*>(a.recv_o + (s * slot_rows + prow0) * 128)[lane];
+    } else {
+      ml[s] = make_float2(-INFINITY, 0.f);
+      raw[s] = make_uint2(0u, 0u);
+    }
+  }
   float mx = -INFINITY;
-  for (int s = 0; s < a.nranks; ++s) mx = fmaxf(mx, a.recv_ml[(int64_t(s) * bhs + bh) * a.part + row].x);
+#pragma unroll
+  for (int s = 0; s < kMax; ++s) mx = fmaxf(mx, ml[s].x);
   float L = 0.f;
   float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int s = 0; s < a.nranks; ++s) {
-    const int64_t prow = (int64_t(s) * bhs + bh) * a.part + row;
-    const float2 ml = a.recv_ml[prow];
-    const float w = ml.x == -INFINITY ? 0.f : ex2_approx(ml.x - mx) * ml.y;
+#pragma unroll
+  for (int s = 0; s < kMax; ++s) {
+    const float w = ml[s].x == -INFINITY ? 0.f : ex2_approx(ml[s].x - mx) * ml[s].y;
     L += w;
-    const uint2 raw = reinterpret_cast<const uint2*>(a.recv_o + prow * 128)[lane];
-    const float2 p0 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-    const float2 p1 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+    const float2 p0 = __half22float2(*reinterpret_cast<const __half2*>(&raw[s].x));
+    const float2 p1 = __half22float2(*reinterpret_cast<const __half2*>(&raw[s].y));
     o.x = fmaf(w, p0.x, o.x);
     o.y = fmaf(w, p0.y, o.y);
     o.z = fmaf(w, p1.x, o.z);
