@@ -278,8 +278,9 @@ LBQ_API int lbq_share_quant_push(const void* k, int64_t sk_b, int64_t sk_l, int6
  * [B][H][rows_pad/32], from lbq_quant_q) to rows [row0, row0 + rows_pad) of every rank's full query
  * buffers (heap offsets q_off / q_scale_off of [B][H][q_pad][128] / [B][H][q_pad/32]), this rank's own
  * included, with `ctas` CTAs (0 = 32), then signals the other ranks once. Must be ordered after this
- * call's lbq_chunk_totals (every rank has then finished its previous attention, the last reader of the
- * query buffers). Replaces the q all-to-all of the Ulysses split (lingbot/parallel/split_dit.py:371-386):
+ * rank's previous wait for the partials (lbq_peer_wait before lbq_keys_combine): every rank signals
+ * its partials after its attention's last CTA, so every rank has then finished reading the query
+ * buffers. Replaces the q all-to-all of the Ulysses split (lingbot/parallel/split_dit.py:371-386):
  * every rank needs every query row once the keys are split. */
 LBQ_API int lbq_q_push(const int8_t* q_codes, const float* q_scale, int rows_pad, int row0, int q_pad,
                int batch, int heads, int64_t q_off, int64_t q_scale_off, const uint64_t* peers,

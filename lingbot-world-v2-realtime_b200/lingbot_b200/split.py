@@ -347,9 +347,10 @@ class KeySplitAttention(SplitAttention):
     Per call, on this rank (every launch on the current stream or one forked side stream, no host
     synchronisation, so a call can be captured in a CUDA graph):
 
+      0. side stream, from the start: lbq_quant_q of the query slice, lbq_q_push into every rank's full
+         query buffers;
       1.-2. block statistics of the share and window totals, as SplitAttention;
-      3. side stream: lbq_quant_q of the query slice, lbq_q_push into every rank's full query buffers,
-         lbq_share_push (persist=True) of the bf16 share into every rank's cache replica;
+      3. side stream: lbq_share_push (persist=True) of the bf16 share into every rank's cache replica;
          main stream: lbq_quant_kv_tiles of this rank's memory tiles and of its chunk share;
       4. lbq_peer_wait (query codes, shares);
       5. lbq_attn_fwd_keys — partials into the owners' receive slots, then a signal per rank;
@@ -384,6 +385,7 @@ class KeySplitAttention(SplitAttention):
         self.recv_o = heap.carve((self.world, bh, self.part, 128), torch.float16)
         self.recv_ml = heap.carve((self.world, bh, self.part, 2), torch.float32)
         self.q_ctas = 32          # CTAs of the query-code push (few: it runs beside the quantizers)
+        self.totals_done = torch.cuda.Event() if self.side is not None else None
 
     def ranges(self):
         """(tile start, tiles, valid keys) of each code segment this rank attends."""
@@ -416,9 +418,9 @@ class KeySplitAttention(SplitAttention):
             raise ValueError(f"{rows} query rows, the slice holds {self.part}")
         nseg = self.nseg
         codes = self._codes()
-        # 1.-2. block statistics of the share, window totals
-        self._window_totals(cache, k_part, v_part, stp)
-        # 3. side stream: the query slice -> every rank (and, persisting, the bf16 share)
+        # side stream, from the start of the call: the query slice -> every rank. Every rank has finished
+        # its previous attention, the last reader of the query buffers: this rank's previous merge waited
+        # for every rank's partials, which each rank signals after its attention's last CTA.
         self.fork.record(st)
         self.side.wait_event(self.fork)
         sst = self.side.cuda_stream
@@ -429,7 +431,13 @@ class KeySplitAttention(SplitAttention):
         _lib.call("lbq_q_push", ops._ptr(self.q_codes), ops._ptr(self.q_scale), rows_pad, self.rank * self.part,
                   self.q_pad, b, h, self.heap.offset(self.q_all), self.heap.offset(self.q_all_scale), *group,
                   self.q_ctas, sst)
+        # 1.-2. block statistics of the share, window totals
+        self._window_totals(cache, k_part, v_part, stp)
         if persist:
+            # the bf16 share -> every rank's cache, after the window totals (every rank is past its
+            # previous call's reads of its cache)
+            self.totals_done.record(st)
+            self.side.wait_event(self.totals_done)
             _lib.call("lbq_share_push", *share, b, h, self.share_valid, self.nb_part, *group, k_off, v_off, lk,
                       self.mem_len + self._lo, self.heap.offset(ksum), self.heap.offset(vamax), max_blocks,
                       self.push_ctas, sst)
