@@ -29,7 +29,8 @@ Other workloads (not the headline line): `--workload call` = BASELINE config 1 (
 kv 12064: quantize + attend), `--workload requant` = BASELINE config 2 (re-quantize 30 layers of
 24128-token bf16 memory caches; HBM GB/s), `--workload streams` = BASELINE config 5 (independent
 streams, one per GPU, 54288-key windows with outlier K channels; aggregate TOPS). BASELINE config 3
-(one DiT pass) is one fifth of the chunk: 30 calls.
+(one DiT pass) is one fifth of the chunk: 30 calls. `--workload cross` = the DiT's cross-attention (q 6032 x
+512 text keys) through the same quantized kernels, with the paper's bf16 SDPA timed beside it.
 """
 import argparse
 import json
@@ -60,7 +61,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["chunk", "call", "requant", "streams"], default="chunk")
+    ap.add_argument("--workload", choices=["chunk", "call", "requant", "streams", "cross"], default="chunk")
     ap.add_argument("--call-kv", type=int, default=12064,
                     help="keys of the single-call workload (12064 = BASELINE config 1; 30160 = one chunk call)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -656,6 +657,69 @@ def run_call(args, world, rank, local):
                           "peak_source": f"2 x bf16_tflops burst ({src})", "attn_ms_per_call": round(attn_ms, 4)})
 
 
+TEXT_LEN = 512                     # text tokens of the cross-attention (T5 context, padded)
+
+
+def run_cross(args, world, rank, local):
+    """Cross-attention: the chunk's 6032 query rows against the 512 text keys, 12
+    heads x 128, through the reference's cross-attention entry `flash_attention(q, k, v, k_lens=None)`
+    (transformer.py:272) in the quantized mode: Q, K and V quantized and the same attention kernel as
+    self-attention. Inputs cycle through 8 sets (> L2): q ~ N(0, 1), text K/V ~ N(0, 0.5). The paper's
+    unquantized attention (torch SDPA, bf16) is timed on the same inputs beside it."""
+    from lingbot_b200 import attention, ops
+    dev = torch.device("cuda", local)
+    lq, lk = LQ, TEXT_LEN
+    g = torch.Generator(device=dev).manual_seed(7)
+    sets = [(torch.randn(1, lq, H, D, generator=g, device=dev).bfloat16(),
+             (0.5 * torch.randn(1, lk, H, D, generator=g, device=dev)).bfloat16(),
+             (0.5 * torch.randn(1, lk, H, D, generator=g, device=dev)).bfloat16()) for _ in range(8)]
+    def graphs(mode):
+        """One CUDA graph per input set of the cross-attention call in `mode` (host launch cost out of
+        the timed region, as the DiT's graph-captured layers have it)."""
+        attention.set_cross_attention(mode)
+        try:
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                for q, k, v in sets:                       # warm-up outside capture
+                    attention.flash_attention(q, k, v, k_lens=None)
+            torch.cuda.current_stream().wait_stream(side)
+            out = []
+            for q, k, v in sets:
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr):
+                    attention.flash_attention(q, k, v, k_lens=None)
+                out.append(gr)
+            return out
+        finally:
+            attention.set_cross_attention("paper")
+
+    it = [0]
+
+    def replay(gs):
+        gs[it[0] % 8].replay()
+        it[0] += 1
+
+    paper_graphs = graphs("paper")
+    paper_ms, _ = _timed(lambda: replay(paper_graphs), args.steps, args.warmup, dev, world)
+    sage_graphs = graphs("sage")
+    ms, clocks = _timed(lambda: replay(sage_graphs), args.steps, args.warmup, dev, world)
+    flops = 4.0 * lq * lk * H * D
+    peaks, src = measured_peaks()
+    peak = 2.0 * peaks.get("bf16_tflops", 1590.0)
+    ach = flops / (ms * 1e-3) / 1e12
+    return dict(tops=world * flops / (ms * 1e-3) / 1e12, ms=ms, clocks=clocks, scaling="weak",
+                launches=5 * args.steps * world, e2e=None,
+                config={"workload": "cross-attention: q 6032 x 512 text keys (transformer.py:272), quantized",
+                        "q_len": lq, "kv_len": lk, "heads": H, "head_dim": D,
+                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                        "l2": "inputs larger than L2 (8 input sets of 21.5 MB, cycled)",
+                        "paper_sdpa_bf16_ms_per_call": round(paper_ms, 4)},
+                roofline={"bound": "tensor", "achieved": round(ach, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                          "frac": round(ach / peak, 4), "traffic": None, "kernel": "attn_fwd_kernel (+ quantizers)",
+                          "peak_source": f"2 x bf16_tflops burst ({src})"})
+
+
 def run_requant(args, world, rank, local):
     """re-quantize the 30-layer bf16 memory cache [30, 24128, 12, 128] (K int8 per
     64-token block after the channel mean, V e4m3 per channel) from its block statistics."""
@@ -738,6 +802,8 @@ def main():
             res = run_call(args, world, rank, local)
         elif args.workload == "streams":
             res = run_streams(args, world, rank, local)
+        elif args.workload == "cross":
+            res = run_cross(args, world, rank, local)
         else:
             res = run_requant(args, world, rank, local)
         if rank == 0:
@@ -751,7 +817,8 @@ def main():
             metric = {"chunk": "DiT self-attention TOPS (full chunk: 5 passes x 30 layers)",
                       "call": "attention TOPS, one call (BASELINE config 1, quantize + attend)",
                       "requant": "K/V re-quant HBM GB/s (BASELINE config 2, 30 layers x 24128 tokens)",
-                      "streams": "aggregate attention TOPS, independent streams (BASELINE config 5)"}[args.workload]
+                      "streams": "aggregate attention TOPS, independent streams (BASELINE config 5)",
+                      "cross": "cross-attention TOPS, quantized (q 6032 x 512 text keys; quantize + attend)"}[args.workload]
             line = {"metric": metric,
                     "value": round(res["tops"], 2), "unit": res.get("unit", "TOPS"), "n_gpus": world, "steps": args.steps,
                     "warmup": args.warmup, "ms_per_step": round(res["ms"], 3), "s_per_chunk": round(res["ms"] / 1e3, 5),

@@ -7,13 +7,21 @@ SageAttention-2 semantics). Every other call takes the reference's non-Sage bran
 paper's attention (wan/modules/attention.py:132-178); here that is torch's SDPA on the GPU.
 The quantized path is registered as the custom op `lbq::sage_attn` (with a fake implementation) so
 torch.compile keeps the DiT in one graph, as the reference relied on for `sageattn`.
+
+`flash_attention(q, k, v, k_lens=None)` is the reference's cross-attention entry
+(lingbot/layers/attention.py:16-20, called at models/lingbot_world/transformer.py:272 with
+k_lens=None, transformer.py:658). Like the reference it is not quantized by default. With
+`LBQ_CROSS_ATTN=sage` in the environment (or `set_cross_attention("sage")`), its plain calls run
+through the same quantized kernels: q of the chunk against the 512 text keys.
 """
+import os
+
 import torch
 import torch.nn.functional as F
 
 from . import ops
 
-__all__ = ["attention", "flash_attention"]
+__all__ = ["attention", "flash_attention", "set_cross_attention"]
 
 
 @torch.library.custom_op("lbq::sage_attn", mutates_args=())
@@ -45,12 +53,35 @@ def _paper_attention(q, k, v, q_lens=None, k_lens=None, dropout_p=0., softmax_sc
     return o.to(out_dtype)
 
 
+_CROSS_MODES = ("paper", "sage")
+_cross_mode = os.environ.get("LBQ_CROSS_ATTN", "paper")
+if _cross_mode not in _CROSS_MODES:
+    raise ValueError(f"LBQ_CROSS_ATTN={_cross_mode!r}: expected one of {_CROSS_MODES}")
+
+
+def set_cross_attention(mode):
+    """Route flash_attention's plain calls to the paper's attention ("paper", the default, as the
+    reference does) or to the quantized kernels ("sage")."""
+    global _cross_mode
+    if mode not in _CROSS_MODES:
+        raise ValueError(f"cross-attention mode {mode!r}: expected one of {_CROSS_MODES}")
+    _cross_mode = mode
+
+
 def flash_attention(q, k, v, k_lens=None, **kw):
-    """The reference's cross-attention entry (lingbot/layers/attention.py:16-20): not quantized."""
+    """The reference's cross-attention entry (lingbot/layers/attention.py:16-20). Quantized only in
+    the "sage" cross-attention mode and only for plain calls (no k_lens, no dropout, not causal)."""
     kw.pop("fa_version", None)
     kw.pop("q_scale", None)
     kw.pop("window_size", None)
     kw.pop("deterministic", None)
+    if (_cross_mode == "sage" and k_lens is None and kw.get("q_lens") is None and not kw.get("dropout_p")
+            and not kw.get("causal")):
+        scale = kw.get("softmax_scale")
+        out_dtype = q.dtype
+        x = sage_attn(q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16),
+                      float(scale) if scale else 0.0)
+        return x.to(out_dtype)
     return _paper_attention(q, k, v, k_lens=k_lens, **kw)
 
 

@@ -128,3 +128,31 @@ def test_drop_in_attention_signature():
     # non-Sage branch (k_lens) goes to the paper's attention, as in the reference
     o3 = attention(q, k, v, k_lens=torch.tensor([300]))
     assert o3.shape == q.shape
+
+
+def test_cross_attention_through_the_quantized_kernel():
+    """Cross-attention (transformer.py:272: flash_attention(q, k, v, k_lens=None), 512 text keys):
+    the paper's attention by default, as in the reference; in the "sage" cross-attention mode the same
+    quantized kernels as self-attention, bit-identical to them."""
+    from lingbot_b200 import _lib, attention, ops
+    g = torch.Generator().manual_seed(21)
+    q = torch.randn(1, 700, 3, 128, generator=g).bfloat16().cuda()
+    k = (0.5 * torch.randn(1, 512, 3, 128, generator=g)).bfloat16().cuda()
+    v = (0.5 * torch.randn(1, 512, 3, 128, generator=g)).bfloat16().cuda()
+    fp32 = O.sdpa_fp32(q.cpu(), k.cpu(), v.cpu())
+    paper = attention.flash_attention(q, k, v, k_lens=None)
+    assert O.compare(paper.float().cpu(), fp32)["cos"] >= 0.9999
+    try:
+        attention.set_cross_attention("sage")
+        out = attention.flash_attention(q, k, v, k_lens=None)
+        torch.cuda.synchronize()
+        assert _lib.device_status() == 0
+        assert torch.equal(out, ops.sage_attn(q, k, v))
+        sage = O.compare(out.float().cpu(), O.sage_attention(q.cpu(), k.cpu(), v.cpu()).float())
+        assert sage["cos"] >= COS_MIN and sage["max_abs"] <= MAX_ABS, sage
+        assert O.compare(out.float().cpu(), fp32)["cos"] > 0.995
+        # key lengths keep the paper's masked attention, as in the reference
+        masked = attention.flash_attention(q, k, v, k_lens=torch.tensor([300]))
+        assert not torch.equal(masked, out)
+    finally:
+        attention.set_cross_attention("paper")

@@ -43,3 +43,4 @@ def test_argument_validation_without_a_gpu():
     rc = lib.lbq_quant_q(mis, 0, 0, 0, 1, 1, 1, mis, mis, None)
     assert rc == 2 and b"aligned" in lib.lbq_last_error()
     assert lib.lbq_abi_version() == 100
+
