@@ -61,7 +61,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["chunk", "call", "requant", "streams", "cross"], default="chunk")
+    ap.add_argument("--workload", choices=["chunk", "call", "requant", "streams", "cross", "keys-rank"],
+                    default="chunk")
+    ap.add_argument("--ranks", type=int, default=8, help="--workload keys-rank: ranks of the emulated split")
+    ap.add_argument("--rank", type=int, default=1, help="--workload keys-rank: the emulated rank")
     ap.add_argument("--call-kv", type=int, default=12064,
                     help="keys of the single-call workload (12064 = BASELINE config 1; 30160 = one chunk call)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -720,6 +723,104 @@ def run_cross(args, world, rank, local):
                           "peak_source": f"2 x bf16_tflops burst ({src})"})
 
 
+def run_keys_rank(args, world, rank, local):
+    """One rank of the key-range split at config 4, emulated on one GPU: every query row of the chunk
+    (6032) against rank `--rank`'s keys of the 30160-key window under an `--ranks`-way split (its
+    memory tiles, then its chunk share), through lbq_attn_fwd_keys. The partials go to per-owner
+    regions of one local buffer standing in for the other ranks' heaps (no NVLink, no waits); the
+    merge of one owner's rows (lbq_keys_combine) is timed from a CUDA graph. A profiling and sizing
+    tool for the key-range kernel, not a headline line."""
+    import ctypes
+    from lingbot_b200 import _lib, ops, split
+    dev = torch.device("cuda", local)
+    n_ranks, r = args.ranks, args.rank
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(1, LQ, H, D, generator=g, device=dev).bfloat16()
+    k = (torch.randn(1, LK, H, D, generator=g, device=dev) + 3 * torch.randn(1, 1, H, D, generator=g, device=dev)).bfloat16()
+    v = torch.randn(1, LK, H, D, generator=g, device=dev).bfloat16()
+    w = ops.quantize_qkv(q, k, v)
+    del k, v
+    seg_pad = ops.round_up(MEM, 128)
+    kc = torch.zeros(2, 1, H, seg_pad, D, dtype=torch.int8, device=dev)
+    ks = torch.zeros(2, 1, H, seg_pad // 64, dtype=torch.float32, device=dev)
+    vt = torch.zeros(2, 1, H, D, seg_pad, dtype=torch.uint8, device=dev)
+    for s_, (t0, t1) in enumerate([(0, MEM), (MEM, LK)]):
+        kc[s_][:, :, :t1 - t0] = w.k_codes[0][:, :, t0:t1]
+        vt[s_][..., :t1 - t0] = w.vt_codes[0][..., t0:t1]
+        ks[s_][:, :, :(t1 - t0 + 63) // 64] = w.k_scale[0][:, :, t0 // 64:(t1 + 63) // 64]
+    part = split.share_part(LQ, n_ranks)
+    q_pad = n_ranks * part
+    q_all = torch.zeros(1, H, q_pad, D, dtype=torch.int8, device=dev)
+    q_all_scale = torch.zeros(1, H, q_pad // 32, dtype=torch.float32, device=dev)
+    q_all[:, :, :w.q_codes.shape[2]] = w.q_codes
+    q_all_scale[:, :, :w.q_scale.shape[2]] = w.q_scale
+    up = lambda x: (x + 255) // 256 * 256  # noqa: E731
+    xbytes = up(_lib.load().lbq_exchange_bytes(n_ranks, 1, H))
+    o_bytes, ml_bytes = up(n_ranks * H * part * 256), up(n_ranks * H * part * 8)
+    delta = xbytes + o_bytes + ml_bytes
+    region = torch.zeros(n_ranks * delta, dtype=torch.uint8, device=dev)
+    peers = torch.tensor([region.data_ptr() + p * delta for p in range(n_ranks)], dtype=torch.int64, device=dev)
+    lo = min(LQ, r * part)
+    hi = min(LQ, lo + part)
+    m0, m1 = split.key_tiles(MEM, n_ranks, r)
+    rg = [(m0, m1 - m0, MEM), (lo // 128, -(-hi // 128) - lo // 128 if hi > lo else 0, LQ)]
+    keys = sum(min(x[2], (x[0] + x[1]) * 128) - x[0] * 128 for x in rg if x[1])
+    arr = ctypes.c_int * 2
+    ranges = (arr(*[x[0] for x in rg]), arr(*[x[1] for x in rg]), arr(*[x[2] for x in rg]))
+    ev = []
+
+    def fn():
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        _lib.call("lbq_attn_fwd_keys", ops._ptr(q_all), ops._ptr(q_all_scale), LQ, q_pad, ops._ptr(kc), ops._ptr(ks),
+                  ops._ptr(vt), 2, MEM, 1, H, 0.0, *ranges, ops._ptr(peers), n_ranks, r, 0, part, xbytes,
+                  xbytes + o_bytes, ops._stream())
+        b.record()
+        ev.append((a, b))
+
+    ms, clocks = _timed(fn, args.steps, args.warmup, dev, world)
+    attn_ms = statistics.mean(a.elapsed_time(b) for a, b in ev[args.warmup:])
+    # merge of owner 0's rows, 20 launches in one graph (Python launch cost out of the timing)
+    rows = min(LQ, part)
+    out = torch.empty(1, rows, H, D, dtype=torch.bfloat16, device=dev)
+    combine = lambda: _lib.call("lbq_keys_combine", ctypes.c_void_p(region.data_ptr() + xbytes),  # noqa: E731
+                                ctypes.c_void_p(region.data_ptr() + xbytes + o_bytes), n_ranks, part, rows,
+                                ops._ptr(w.v_scale), 1, H, ops._ptr(out), *out.stride()[:3], ops._stream())
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        combine()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(20):
+            combine()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    graph.replay()
+    a.record()
+    graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    combine_us = a.elapsed_time(b) / 20 * 1e3
+    status = _lib.device_status()
+    if status:
+        raise RuntimeError(f"device status {status:#x}")
+    flops = 4.0 * LQ * keys * H * D
+    peaks, src = measured_peaks()
+    peak = 2.0 * peaks.get("bf16_tflops", 1590.0)
+    ach = flops / (attn_ms * 1e-3) / 1e12
+    merge_bytes = n_ranks * H * rows * 264 + H * rows * 256
+    return dict(tops=flops / (ms * 1e-3) / 1e12, ms=ms, clocks=clocks, launches=args.steps, e2e=None,
+                config={"workload": f"key-range split, one emulated rank ({r} of {n_ranks}) at BASELINE config 4: "
+                                    f"6032 query rows x {keys} keys ({m1 - m0} memory tiles + chunk share)",
+                        "q_len": LQ, "kv_len": keys, "heads": H, "head_dim": D, "parallelism": "single GPU",
+                        "merge_us_per_launch": round(combine_us, 2),
+                        "merge_gbs": round(merge_bytes / (combine_us * 1e-6) / 1e9, 1)},
+                roofline={"bound": "tensor", "achieved": round(ach, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                          "frac": round(ach / peak, 4), "traffic": None, "kernel": "attn_fwd_kernel<true>",
+                          "peak_source": f"2 x bf16_tflops burst ({src})", "attn_ms_per_call": round(attn_ms, 4)})
+
+
 def run_requant(args, world, rank, local):
     """re-quantize the 30-layer bf16 memory cache [30, 24128, 12, 128] (K int8 per
     64-token block after the channel mean, V e4m3 per channel) from its block statistics."""
@@ -804,6 +905,8 @@ def main():
             res = run_streams(args, world, rank, local)
         elif args.workload == "cross":
             res = run_cross(args, world, rank, local)
+        elif args.workload == "keys-rank":
+            res = run_keys_rank(args, world, rank, local)
         else:
             res = run_requant(args, world, rank, local)
         if rank == 0:
@@ -818,7 +921,8 @@ def main():
                       "call": "attention TOPS, one call (BASELINE config 1, quantize + attend)",
                       "requant": "K/V re-quant HBM GB/s (BASELINE config 2, 30 layers x 24128 tokens)",
                       "streams": "aggregate attention TOPS, independent streams (BASELINE config 5)",
-                      "cross": "cross-attention TOPS, quantized (q 6032 x 512 text keys; quantize + attend)"}[args.workload]
+                      "cross": "cross-attention TOPS, quantized (q 6032 x 512 text keys; quantize + attend)",
+                      "keys-rank": "key-range attention TOPS of one emulated rank (BASELINE config 4)"}[args.workload]
             line = {"metric": metric,
                     "value": round(res["tops"], 2), "unit": res.get("unit", "TOPS"), "n_gpus": world, "steps": args.steps,
                     "warmup": args.warmup, "ms_per_step": round(res["ms"], 3), "s_per_chunk": round(res["ms"] / 1e3, 5),
