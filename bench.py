@@ -865,7 +865,7 @@ def run_requant(args, world, rank, local):
 def run_reference(args, world, rank):
     if rank != 0:
         return
-    model, cores = cpu_info()
+    model, _cores = cpu_info()
     times, flops = [], 0.0
     for i in range(args.warmup + args.steps):
         dt, flops = cpu_oracle_sample(seed=i)

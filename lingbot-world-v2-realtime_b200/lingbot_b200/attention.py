@@ -38,7 +38,7 @@ def _paper_attention(q, k, v, q_lens=None, k_lens=None, dropout_p=0., softmax_sc
                      dtype=torch.bfloat16):
     """The reference's non-Sage branch: padded-batch attention with optional key lengths."""
     out_dtype = q.dtype
-    b, lq, h, d = q.shape
+    lq = q.shape[1]
     qh, kh, vh = (x.to(dtype).transpose(1, 2) for x in (q, k, v))
     mask = None
     if k_lens is not None:
