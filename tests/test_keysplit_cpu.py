@@ -90,3 +90,24 @@ def test_key_split_entry_points_check_their_arguments():
     assert lib.lbq_keys_combine(fake, fake, 2, 256, 300, fake, 1, 2, *act, None) == 1 and b"rows 300" in _err()
     assert lib.lbq_q_push(fake, fake, 128, 64, 512, 1, 2, 0, 0, fake, 2, 0, 0, 0, None) == 1
     assert b"multiples of 128" in _err()
+
+
+def test_key_ranges_restate_the_split_emulation():
+    """The oracle's key-range partials are the split-KV partials generalised: one whole-window range is
+    the unsplit emulation, and the split ranges as key ranges are `splits` exactly."""
+    g = torch.Generator().manual_seed(2)
+    q = torch.randn(1, 96, 2, 128, generator=g).bfloat16()
+    k = torch.randn(1, 700, 2, 128, generator=g).bfloat16()
+    v = torch.randn(1, 700, 2, 128, generator=g).bfloat16()
+    qq = O.quantize_qkv(q, k, v)
+    codes = (qq["q_codes"], qq["q_scale"], qq["k_codes"], qq["k_scale"], qq["v_codes"], qq["v_scale"])
+    kernel = dict(tile=128, pv_accum="fp32")
+    assert torch.equal(O.attn_from_codes(*codes, **kernel, key_ranges=[[(0, 700)]]),
+                       O.attn_from_codes(*codes, **kernel))
+    per = 2 * 128                                  # 6 tiles in 3 splits
+    ranges = [[(s, min(700, s + per))] for s in range(0, 700, per)]
+    assert torch.equal(O.attn_from_codes(*codes, **kernel, key_ranges=ranges),
+                       O.attn_from_codes(*codes, **kernel, splits=3))
+    # a partial made of two pieces runs them under one running max: the same as one piece
+    assert torch.equal(O.attn_from_codes(*codes, **kernel, key_ranges=[[(0, 256), (256, 700)]]),
+                       O.attn_from_codes(*codes, **kernel))
