@@ -197,6 +197,7 @@ __device__ __forceinline__ void store_key_partial(const AttnArgs& a, uint32_t tO
   __syncwarp();
   const int qrow0 = qtile * 128;
   const int owner = qrow0 / a.part;                      // part % 128 == 0: one owner per Q tile
+  if (!LBQ_CHECK(owner < a.nranks && qrow0 - owner * a.part + 128 <= a.part, a.status, kDevBadOwner)) return;
   const int64_t slot = (int64_t(a.rank) * bhs + bh) * a.part + (qrow0 - owner * a.part);
   char* dst = reinterpret_cast<char*>(static_cast<uintptr_t>(a.peers[owner]));
   uint8_t* dst_o = reinterpret_cast<uint8_t*>(dst + a.recv_o_off) + slot * 256;
@@ -277,6 +278,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int jt = t_begin + i;
         int seg, lt;
         tile_seg<kKeyRange>(a, jt, tiles_per_seg, seg, lt);
+        (void)LBQ_CHECK(seg < a.nseg && lt >= 0 && lt < tiles_per_seg, a.status, kDevBadTile);
         const int s = i % kStages;
         const uint32_t ph = (i / kStages) & 1;
         if (!mbar_wait(&sh->k_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) break;
@@ -369,6 +371,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int jt = t_begin + i;
       int seg, lt;
       tile_seg<kKeyRange>(a, jt, tiles_per_seg, seg, lt);
+      if (!LBQ_CHECK(seg < a.nseg && lt >= 0 && lt * 2 + 1 < kspb, a.status, kDevBadTile)) seg = lt = 0;
       return a.k_scale + int64_t(seg * bhs + bh) * kspb + lt * 2;
     };
     float m = -INFINITY, dsum = 0.f;
@@ -607,6 +610,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int i = 0; i < w.n; ++i, ++g) {
           int seg, lt;
           tile_seg<kKeyRange>(a, w.t_begin + i, tiles_per_seg, seg, lt);
+          (void)LBQ_CHECK(seg < a.nseg && lt >= 0 && lt < tiles_per_seg, a.status, kDevBadTile);
           const int s = g % kStages;
           const uint32_t ph = (g / kStages) & 1;
           if (!mbar_wait(&sh->k_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) {
@@ -728,6 +732,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       auto kscale_ptr = [&](int i) {
         int seg, lt;
         tile_seg<kKeyRange>(a, w.t_begin + i, tiles_per_seg, seg, lt);
+        if (!LBQ_CHECK(seg < a.nseg && lt >= 0 && lt * 2 + 1 < kspb, a.status, kDevBadTile)) seg = lt = 0;
         return a.k_scale + int64_t(seg * bhs + bh) * kspb + lt * 2;
       };
       float m = -INFINITY, dsum = 0.f;

@@ -120,7 +120,7 @@ int lbq_kv_block_stats(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, 
   if (blk_end <= blk_begin) return LBQ_OK;
   lbq::KvBlockStatsArgs a{static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v),
                           sk_b, sk_l, sk_h, sv_b, sv_l, sv_h, batch, heads, kv_len, blk_begin, blk_end,
-                          max_blocks, ksum, vamax};
+                          max_blocks, ksum, vamax, lbq::device_status_ptr()};
   cudaError_t e = lbq::launch_kv_block_stats(a, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "kv_block_stats launch");
 }
@@ -179,9 +179,9 @@ int lbq_quant_kv_tiles(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, 
   const int seg_pad = int(round_up(seg_len, 128));
   lbq::QuantKArgs ka{static_cast<const __nv_bfloat16*>(k), sk_b, sk_l, sk_h, batch, heads, tok0, seg, seg_valid,
                      seg_pad, kv_len_total, ksum_total, k_codes, k_scale,
-                     static_cast<__nv_bfloat16*>(km_out), write_totals};
+                     static_cast<__nv_bfloat16*>(km_out), write_totals, lbq::device_status_ptr()};
   lbq::QuantVArgs va{static_cast<const __nv_bfloat16*>(v), sv_b, sv_l, sv_h, batch, heads, tok0, seg, seg_valid,
-                     seg_pad, vamax_total, vt_codes, v_scale, write_totals};
+                     seg_pad, vamax_total, vt_codes, v_scale, write_totals, lbq::device_status_ptr()};
   cudaError_t e = lbq::launch_quant_kv(ka, va, tile_begin, tile_end - tile_begin, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "quant_kv launch");
 }

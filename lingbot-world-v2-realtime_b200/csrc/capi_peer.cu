@@ -187,9 +187,9 @@ int lbq_share_quant_push(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h
   const int64_t tok0 = -int64_t(lo);   // segment token t is share token t - lo
   lbq::QuantKArgs ka{static_cast<const __nv_bfloat16*>(k), sk_b, sk_l, sk_h, batch, heads, tok0, seg, lo + share_valid,
                      seg_pad, kv_len_total, ksum_total, k_codes, k_scale, static_cast<__nv_bfloat16*>(km_out),
-                     write_totals};
+                     write_totals, lbq::device_status_ptr()};
   lbq::QuantVArgs va{static_cast<const __nv_bfloat16*>(v), sv_b, sv_l, sv_h, batch, heads, tok0, seg, lo + share_valid,
-                     seg_pad, vamax_total, vt_codes, v_scale, write_totals};
+                     seg_pad, vamax_total, vt_codes, v_scale, write_totals, lbq::device_status_ptr()};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = lbq::launch_quant_kv(ka, va, tile0, tile_end - tile0, st);
   if (e != cudaSuccess) return set_error(LBQ_ERR_CUDA, "share quant launch: %s", cudaGetErrorString(e));

@@ -19,6 +19,7 @@ struct KvBlockStatsArgs {
   int64_t max_blocks;         // rows of the stats tables
   double* ksum;               // [B][max_blocks][H][128]
   float* vamax;               // [B][max_blocks][H][128]
+  int* status;                // device status word (debug-build index checks)
 };
 
 struct KvWindowSumsArgs {
@@ -52,6 +53,7 @@ struct QuantKArgs {
   float* k_scale;             // [S][B][H][seg_pad/64]
   __nv_bfloat16* km_out;      // [B][H][128] or null
   int write_km;
+  int* status;                // device status word (debug-build index checks)
 };
 
 struct QuantVArgs {
@@ -64,6 +66,7 @@ struct QuantVArgs {
   uint8_t* vt_codes;          // [S][B][H][128][seg_pad]
   float* v_scale;             // [B][H][128]
   int write_scale;
+  int* status;                // device status word (debug-build index checks)
 };
 
 struct AttnArgs {

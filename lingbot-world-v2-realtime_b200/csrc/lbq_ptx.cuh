@@ -28,7 +28,25 @@ enum DeviceStatus : int {
   kDevTimeoutO = 0x105,      // O accumulator never completed
   kDevTimeoutPeerStats = 0x201,  // sequence split: a rank's share statistics never arrived
   kDevTimeoutPeerData = 0x202,   // sequence split: a rank's K/V share never arrived
+  kDevBadStatsRow = 0x301,       // debug build: block-statistics row outside the table
+  kDevBadSourceToken = 0x302,    // debug build: quantizer source token below 0
+  kDevBadTile = 0x303,           // debug build: key tile outside its code segment
+  kDevBadOwner = 0x304,          // debug build: key-range partial outside the owner's receive slot
 };
+
+// Debug builds (-DLBQ_DEBUG=1, liblbq_debug.so) check the index arithmetic at the places the kDevBad*
+// codes name: a failed check records its code in the status word (the first failure wins) and the
+// caller clamps or skips the access; nothing traps. Release builds compile every check to `true`
+// without evaluating its condition.
+#if defined(LBQ_DEBUG) && LBQ_DEBUG
+__device__ __forceinline__ bool lbq_check(bool ok, int* status, int code) {
+  if (!ok && status != nullptr) atomicCAS(status, 0, code);
+  return ok;
+}
+#define LBQ_CHECK(cond, status, code) ::lbq::lbq_check((cond), (status), (code))
+#else
+#define LBQ_CHECK(cond, status, code) true
+#endif
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -87,8 +87,10 @@ __global__ void __launch_bounds__(128) kv_block_stats_kernel(KvBlockStatsArgs a)
     vmax = fmaxf(vmax, sh_v[g][t & 7][t >> 3]);
   }
   const int64_t o = ((int64_t(b) * a.max_blocks + blk) * a.heads + h) * 128 + t;
-  a.ksum[o] = tot;
-  a.vamax[o] = vmax;
+  if (LBQ_CHECK(blk < a.max_blocks, a.status, kDevBadStatsRow)) {
+    a.ksum[o] = tot;
+    a.vamax[o] = vmax;
+  }
 }
 
 // ------------------------------------------------------------------ window sums
@@ -217,7 +219,7 @@ __device__ __forceinline__ void quant_k_tile(const QuantKArgs& a, QuantKvShared&
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int64_t tok = int64_t(blk) * 64 + rg + 8 * i;      // token index inside this segment
-    raw[i] = tok < a.seg_valid
+    raw[i] = tok < a.seg_valid && LBQ_CHECK(a.tok0 + tok >= 0, a.status, kDevBadSourceToken)
                  ? *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + (a.tok0 + tok) * a.sk_l + h * a.sk_h + c16 * 8)
                  : make_uint4(0u, 0u, 0u, 0u);
   }
@@ -276,7 +278,7 @@ __device__ __forceinline__ void quant_v_tile(const QuantVArgs& a, QuantKvShared&
     const int piece = t + 256 * i;                   // 2048 pieces of 16 bytes
     const int r = piece >> 4, c16 = piece & 15;
     const int64_t tok = int64_t(tile) * 128 + r;
-    const uint4 raw = tok < a.seg_valid
+    const uint4 raw = tok < a.seg_valid && LBQ_CHECK(a.tok0 + tok >= 0, a.status, kDevBadSourceToken)
                           ? *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + (a.tok0 + tok) * a.sv_l + h * a.sv_h + c16 * 8)
                           : make_uint4(0u, 0u, 0u, 0u);
     *reinterpret_cast<uint4*>(&sh.v[r * kVtPitch + c16 * 16]) = raw;

@@ -8,7 +8,8 @@ import os
 import threading
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_PKG, "liblbq.so")
+# LBQ_DEBUG_LIB=1: the debug build (device-side index checks recording 0x3xx status codes)
+LIB_PATH = os.path.join(_PKG, "liblbq_debug.so" if os.environ.get("LBQ_DEBUG_LIB") == "1" else "liblbq.so")
 
 _i32, _i64, _f32, _vp, _sz = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
 _u64 = ctypes.c_uint64
@@ -71,7 +72,8 @@ def load():
         if _lib is None:
             if not os.path.exists(LIB_PATH):
                 raise ImportError(f"{LIB_PATH} is missing: build it with `python -m lingbot_b200.build` "
-                                  "(nvcc, sm_100a); there is no fallback implementation")
+                                  "(add --debug for the debug library; nvcc, sm_100a); there is no fallback "
+                                  "implementation")
             lib = ctypes.CDLL(LIB_PATH)
             for name, (res, args) in SIGNATURES.items():
                 fn = getattr(lib, name)

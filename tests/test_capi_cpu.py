@@ -44,3 +44,13 @@ def test_argument_validation_without_a_gpu():
     assert rc == 2 and b"aligned" in lib.lbq_last_error()
     assert lib.lbq_abi_version() == 100
 
+
+
+def test_debug_library_exports_the_same_entry_points():
+    """liblbq_debug.so (device-side index checks, LBQ_DEBUG_LIB=1) exports every declared entry point."""
+    from lingbot_b200 import build as b
+    path = b.build(debug=True)
+    lib = ctypes.CDLL(path)
+    for name in declared():
+        assert hasattr(lib, name), name
+    assert lib.lbq_abi_version() == _lib.load().lbq_abi_version()
