@@ -23,3 +23,19 @@ def pytest_collection_modifyitems(config, items):
     for it in items:
         if "gpu" in it.keywords:
             it.add_marker(skip)
+
+
+@pytest.fixture(autouse=True)
+def _device_status_stays_clear(request):
+    """After every GPU test the device status word must be clear: no bounded wait ran out and, with the
+    debug library (LBQ_DEBUG_LIB=1), no index check failed."""
+    yield
+    if "gpu" not in request.keywords:
+        return
+    import torch
+    if not torch.cuda.is_available():
+        return
+    from lingbot_b200 import _lib
+    torch.cuda.synchronize()
+    status = _lib.device_status()
+    assert status == 0, f"device status {status:#x} after the test"
