@@ -510,6 +510,53 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if constexpr (kKeyRange) signal_after_last_cta(a.peers, a.nranks, a.rank, a.xchg_off, xchg::kDoneAttn);
 }
 
+// Key-range epilogue of the persistent kernel: as store_key_partial, but each warp stages its 32 rows
+// in its own rows of the tile's two P buffers only (chunks 0-7 of a row in its P row of buffer 0, chunks
+// 8-15 in buffer 1, 128-byte swizzle), so that a warp that has moved on to the next item and writes its
+// P rows cannot overwrite another warp's staged rows.
+__device__ __forceinline__ void store_key_partial_own_rows(const AttnArgs& a, uint32_t tO, uint8_t* ptile,
+                                                           int quarter, int lane, int qtile, int bh, int bhs,
+                                                           float m, float dsum) {
+  const float rd = __frcp_rn(dsum);
+  const int rl = quarter * 32 + lane;                    // row inside the tile (TMEM lane)
+  auto stage = [&](int row, int chunk) {                 // 16-byte chunk `chunk` of tile row `row`
+    return ptile + (chunk >> 3) * kTile + row * 128 + (((chunk & 7) ^ (row & 7)) << 4);
+  };
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t ov[32];
+    tmem_ld32(tO + 32 * c, ov);
+    tmem_ld_wait();
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      uint32_t hw[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const __half2 p = __floats2half2_rn(__fmul_rn(__uint_as_float(ov[8 * e + 2 * k]), rd),
+                                            __fmul_rn(__uint_as_float(ov[8 * e + 2 * k + 1]), rd));
+        hw[k] = *reinterpret_cast<const uint32_t*>(&p);
+      }
+      *reinterpret_cast<uint4*>(stage(rl, 4 * c + e)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    }
+  }
+  __syncwarp();
+  const int qrow0 = qtile * 128;
+  const int owner = qrow0 / a.part;                      // part % 128 == 0: one owner per Q tile
+  if (!LBQ_CHECK(owner < a.nranks && qrow0 - owner * a.part + 128 <= a.part, a.status, kDevBadOwner)) return;
+  const int64_t slot = (int64_t(a.rank) * bhs + bh) * a.part + (qrow0 - owner * a.part);
+  char* dst = reinterpret_cast<char*>(static_cast<uintptr_t>(a.peers[owner]));
+  uint8_t* dst_o = reinterpret_cast<uint8_t*>(dst + a.recv_o_off) + slot * 256;
+#pragma unroll 4
+  for (int i = 0; i < 16; ++i) {
+    const int r = quarter * 32 + 2 * i + (lane >> 4), ch = lane & 15;
+    if (qrow0 + r < a.q_len)
+      *reinterpret_cast<uint4*>(dst_o + r * 256 + ch * 16) = *reinterpret_cast<const uint4*>(stage(r, ch));
+  }
+  if (qrow0 + rl < a.q_len) reinterpret_cast<float2*>(dst + a.recv_ml_off)[slot + rl] = make_float2(m, dsum);
+  // the staged rows are read before this warp writes its next P rows over them
+  __syncwarp();
+}
+
 // ------------------------------------------------------------------ persistent variant
 // The same computation as attn_fwd_kernel with a grid of at most one CTA per SM, each looping over
 // work items (Q-tile pair, batch*head, KV split) = blockIdx.x, blockIdx.x + gridDim.x, ...: barrier
@@ -806,7 +853,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if constexpr (kKeyRange) {
         if (__all_sync(0xffffffffu, o_ready) && qtile * 128 < a.q_len) {
           tc_fence_after();
-          store_key_partial(a, tO, sP + 2 * t * kTile, quarter, lane, qtile, bh, bhs, m, dsum);
+          store_key_partial_own_rows(a, tO, sP + 2 * t * kTile, quarter, lane, qtile, bh, bhs, m, dsum);
         }
       } else if (o_ready) {
         tc_fence_after();
