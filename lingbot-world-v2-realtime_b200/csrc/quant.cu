@@ -20,6 +20,7 @@
 // attention kernel's masked keys are finite; key tiles past that are never read and not written.
 #include <cuda_bf16.h>
 #include <cstdint>
+#include <cstdlib>
 
 #include "lbq_ptx.cuh"
 #include "lbq_kernels.h"
@@ -48,6 +49,10 @@ __device__ __forceinline__ float warp_max(float x) {
 // ------------------------------------------------------------------ K/V block statistics
 // One CTA per (64-token block, head, batch). ksum: fp64 sum of K over the block's tokens that are
 // < kv_len; vamax: max |V|. 128 threads = 8 row groups x 16 chunks of 8 channels.
+// kLoadsFirst: all of a thread's 8 token loads are issued before the accumulation (one memory round
+// trip instead of eight dependent ones); the sums are accumulated in the same order, so both variants
+// give the same bits.
+template <bool kLoadsFirst>
 __global__ void __launch_bounds__(128) kv_block_stats_kernel(KvBlockStatsArgs a) {
   const int blk = a.blk_begin + blockIdx.x;
   const int h = blockIdx.y, b = blockIdx.z;
@@ -56,18 +61,43 @@ __global__ void __launch_bounds__(128) kv_block_stats_kernel(KvBlockStatsArgs a)
   float vm[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) { s[i] = 0.0; vm[i] = 0.f; }
-  for (int r = rg; r < 64; r += 8) {
-    const int64_t tok = int64_t(blk) * 64 + r;
-    if (tok >= a.kv_len) break;
-    const uint4 kr = *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + tok * a.sk_l + h * a.sk_h + c16 * 8);
-    const uint4 vr = *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + tok * a.sv_l + h * a.sv_h + c16 * 8);
-    float kf[8], vf[8];
-    bf16x8_to_f32(kr, kf);
-    bf16x8_to_f32(vr, vf);
+  if constexpr (kLoadsFirst) {
+    uint4 kr[8], vr[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      s[i] += double(kf[i]);
-      vm[i] = fmaxf(vm[i], fabsf(vf[i]));
+    for (int j = 0; j < 8; ++j) {
+      const int64_t tok = int64_t(blk) * 64 + rg + 8 * j;
+      const bool in = tok < a.kv_len;
+      kr[j] = in ? *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + tok * a.sk_l + h * a.sk_h + c16 * 8)
+                 : make_uint4(0u, 0u, 0u, 0u);
+      vr[j] = in ? *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + tok * a.sv_l + h * a.sv_h + c16 * 8)
+                 : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (int64_t(blk) * 64 + rg + 8 * j >= a.kv_len) break;
+      float kf[8], vf[8];
+      bf16x8_to_f32(kr[j], kf);
+      bf16x8_to_f32(vr[j], vf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        s[i] += double(kf[i]);
+        vm[i] = fmaxf(vm[i], fabsf(vf[i]));
+      }
+    }
+  } else {
+    for (int r = rg; r < 64; r += 8) {
+      const int64_t tok = int64_t(blk) * 64 + r;
+      if (tok >= a.kv_len) break;
+      const uint4 kr = *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + tok * a.sk_l + h * a.sk_h + c16 * 8);
+      const uint4 vr = *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + tok * a.sv_l + h * a.sv_h + c16 * 8);
+      float kf[8], vf[8];
+      bf16x8_to_f32(kr, kf);
+      bf16x8_to_f32(vr, vf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        s[i] += double(kf[i]);
+        vm[i] = fmaxf(vm[i], fabsf(vf[i]));
+      }
     }
   }
   // [row group][channel within chunk][chunk]: a warp's 16 chunks of one slot are consecutive words
@@ -322,8 +352,16 @@ __global__ void __launch_bounds__(256) quant_kv_kernel(QuantKArgs ka, QuantVArgs
 // ------------------------------------------------------------------ launchers
 cudaError_t launch_kv_block_stats(const KvBlockStatsArgs& a, cudaStream_t st) {
   dim3 grid(a.blk_end - a.blk_begin, a.heads, a.batch);
-  if (cudaError_t e0 = prefer_max_shared<kv_block_stats_kernel>(); e0 != cudaSuccess) return e0;
-  kv_block_stats_kernel<<<grid, 128, 0, st>>>(a);
+  // LBQ_STATS_LOADS_FIRST=1 selects the variant that issues every load before accumulating (an A/B
+  // switch, read at every launch)
+  const char* env = std::getenv("LBQ_STATS_LOADS_FIRST");
+  if (env != nullptr && env[0] == '1') {
+    if (cudaError_t e0 = prefer_max_shared<kv_block_stats_kernel<true>>(); e0 != cudaSuccess) return e0;
+    kv_block_stats_kernel<true><<<grid, 128, 0, st>>>(a);
+  } else {
+    if (cudaError_t e0 = prefer_max_shared<kv_block_stats_kernel<false>>(); e0 != cudaSuccess) return e0;
+    kv_block_stats_kernel<false><<<grid, 128, 0, st>>>(a);
+  }
   return cudaGetLastError();
 }
 cudaError_t launch_kv_window_sums(const KvWindowSumsArgs& a, cudaStream_t st) {
