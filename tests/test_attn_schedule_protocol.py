@@ -34,14 +34,28 @@ class Bar:
         return (self.phase & 1) != parity
 
 
+class Always(Bar):
+    """A wait that is always satisfied: a point where the scheduler may run other roles."""
+
+    def __init__(self):
+        super().__init__("yield", 1)
+
+    def ready(self, parity):
+        return True
+
+
 class Model:
     """One CTA: `n_tiles[k]` key tiles for its k-th work item. `early_q_release` and `local_p_parity`
-    break the protocol (for the sensitivity tests)."""
+    break the protocol, `shared_staging` stages the key-range epilogue in 8 KB per warp across the P
+    buffers (the single-item kernel's layout) instead of each warp's own P rows (for the sensitivity
+    tests)."""
 
-    def __init__(self, n_tiles, seed, early_q_release=False, local_p_parity=False):
+    def __init__(self, n_tiles, seed, early_q_release=False, local_p_parity=False, shared_staging=False):
         self.rng = random.Random(seed)
         self.n_tiles = n_tiles
         self.early_q_release, self.local_p_parity = early_q_release, local_p_parity
+        self.shared_staging = shared_staging
+        self.rows = {}                         # (tile t, P buffer, warp's 32-row block) -> last writer
         self.q_full, self.q_empty = Bar("q_full", 1), Bar("q_empty", 1)
         self.k_full = [Bar(f"k_full{s}", 1) for s in range(STAGES)]
         self.k_empty = [Bar(f"k_empty{s}", 1) for s in range(STAGES)]
@@ -107,7 +121,13 @@ class Model:
                     self.commit(self.k_empty[(g + 1) % STAGES])
                 g += 1
 
-    def softmax_warp(self, t):
+    def staging(self, t, w):
+        """The P-row blocks warp w stages its 32 rows of the partial in (16 KB P buffers of 4 blocks)."""
+        if self.shared_staging:                # bytes [8K*w, 8K*w + 8K) of the tile's two buffers
+            return [(t, w // 2, 2 * (w % 2)), (t, w // 2, 2 * (w % 2) + 1)]
+        return [(t, 0, w), (t, 1, w)]          # its own rows in both buffers
+
+    def softmax_warp(self, t, w):
         g = 0
         self.s_free[t].arrive()                 # S_t starts as the refill constant
         for k, n in enumerate(self.n_tiles):
@@ -117,6 +137,7 @@ class Model:
                 self.s_free[t].arrive()
                 if self.s_free[t].arrived == 0:      # every warp has refilled S_t
                     self.s[t] = "magic"
+                self.rows[(t, g & 1, w)] = ("P", g)
                 tile, warps = self.p[t][g & 1] or (None, 0)
                 self.p[t][g & 1] = (g, warps + 1 if tile == g else 1)
                 if i > 0:
@@ -126,6 +147,13 @@ class Model:
             yield self.o_done[t], (g - 1) & 1
             assert self.o[t] == (k, g - 1), f"epilogue {t}: O holds {self.o[t]}, item {k} expected"
             self.o_read[t] = k
+            for block in self.staging(t, w):       # key-range epilogue: stage, then copy out
+                self.rows[block] = ("stage", w, k)
+            for _ in range(16):                      # the copy's 16 store iterations
+                yield Always(), 0
+                for block in self.staging(t, w):
+                    assert self.rows[block] == ("stage", w, k), \
+                        f"epilogue {t}.{w}: staged rows {block} overwritten by {self.rows[block]}"
             self.o_free[t].arrive()
 
     # ---------------------------------------------------------------- asynchronous work
@@ -161,7 +189,7 @@ class Model:
 
     # ---------------------------------------------------------------- scheduler
     def run(self, max_steps=500_000):
-        roles = [self.producer(), self.issuer()] + [self.softmax_warp(t) for t in range(2) for _ in range(4)]
+        roles = [self.producer(), self.issuer()] + [self.softmax_warp(t, w) for t in range(2) for w in range(4)]
         wait = [None] * len(roles)
         done = [False] * len(roles)
         for _ in range(max_steps):
@@ -194,7 +222,7 @@ def test_random_schedules_complete_without_hazards():
         Model(n_tiles, seed=trial).run()
 
 
-@pytest.mark.parametrize("mutation", ["early_q_release", "local_p_parity"])
+@pytest.mark.parametrize("mutation", ["early_q_release", "local_p_parity", "shared_staging"])
 def test_the_model_catches_a_broken_protocol(mutation):
     caught = 0
     for n_tiles, trial in _schedules(100, 7):
