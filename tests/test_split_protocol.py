@@ -1,5 +1,6 @@
-"""The cross-rank protocol of the key-range split (lingbot_b200.split.KeySplitAttention over
-csrc/peer.cu and the key-range attention kernel), checked on a CPU model under random interleavings.
+"""The cross-rank protocols of the sequence splits, checked on a CPU model under random interleavings:
+the key-range split (lingbot_b200.split.KeySplitAttention over csrc/peer.cu and the key-range attention
+kernel) and, below, the query split (SplitAttention).
 
 Every rank runs the calls of a pass sequence on two streams (main and side) joined by events, exactly in
 the order KeySplitAttention.__call__ launches them:
@@ -155,6 +156,75 @@ def test_the_model_catches_a_broken_protocol(mutation):
         persist = [True, False, True, True]
         try:
             SplitModel(3, persist, seed=trial, **{mutation: True}).run()
+        except (AssertionError, RuntimeError):
+            caught += 1
+    assert caught >= 10, f"{mutation}: only {caught} of 40 schedules failed"
+
+
+class QuerySplitModel(SplitModel):
+    """The query split (lingbot_b200.split.SplitAttention) in its launch order:
+    - main stream: block stats, totals push, window totals, then the fork; the memory quantizer; join,
+      peer wait, attention;
+    - side stream, after the fork: this rank's share quantized into its own code buffer and pushed into
+      every other rank's, the bf16 share push for persisting calls, and the query quantizer.
+
+    `codes[s]` on a rank is the call whose chunk codes of rank s its buffer holds; the attention reads
+    all of them. `early_fork` forks the side stream before the window totals (a broken variant)."""
+
+    def __init__(self, n, persist, seed, early_fork=False, **kw):
+        super().__init__(n, persist, seed, **kw)
+        self.early_fork = early_fork
+        for x in self.ranks:
+            x.codes = [-1] * n
+
+    def main(self, r):
+        me = self.ranks[r]
+        for c, persist in enumerate(self.persist):
+            if self.early_fork:
+                me.events.add(("fork", c))
+            for p in range(self.n):
+                self.ranks[p].slots[c & 1][r] = (c + 1, c)
+                yield
+            par = me.calls & 1
+            yield from self.wait(lambda: all(w[0] == me.calls + 1 for w in me.slots[par]))
+            yield
+            assert all(w == (c + 1, c) for w in me.slots[par]), f"rank {r} call {c}: totals overwritten"
+            me.calls += 1
+            me.events.add(("fork", c))
+            yield                                    # the memory quantizer (local)
+            yield from self.wait(lambda: ("join", c) in me.events)
+            yield from self.peer_wait(r, 1 + int(persist))
+            assert all(v == c for v in me.codes), f"rank {r} call {c}: chunk codes {me.codes}"
+            yield
+            assert all(v == c for v in me.codes), f"rank {r} call {c}: chunk codes changed under attention"
+
+    def side(self, r):
+        me = self.ranks[r]
+        for c, persist in enumerate(self.persist):
+            yield from self.wait(lambda: ("fork", c) in me.events)
+            yield from self.push(r, lambda p: self.ranks[p].codes.__setitem__(r, c))
+            if persist:
+                yield from self.push(r, lambda p: self.ranks[p].cache.__setitem__(r, c))
+            me.events.add(("join", c))
+
+    def state(self):
+        return super().state() + tuple(tuple(x.codes) for x in self.ranks)
+
+
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_query_split_protocol_random_interleavings(n):
+    rng = random.Random(100 + n)
+    for trial in range(40 if n < 8 else 15):
+        persist = [rng.random() < 0.3 for _ in range(rng.randint(2, 6))]
+        QuerySplitModel(n, persist, seed=trial).run()
+
+
+@pytest.mark.parametrize("mutation", ["early_fork", "signal_before_write"])
+def test_the_query_split_model_catches_a_broken_protocol(mutation):
+    caught = 0
+    for trial in range(40):
+        try:
+            QuerySplitModel(3, [True, False, False, True], seed=trial, **{mutation: True}).run()
         except (AssertionError, RuntimeError):
             caught += 1
     assert caught >= 10, f"{mutation}: only {caught} of 40 schedules failed"
