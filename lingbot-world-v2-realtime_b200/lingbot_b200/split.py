@@ -330,6 +330,21 @@ def key_tiles(mem_len, world, rank):
     return rank * tiles // world, (rank + 1) * tiles // world
 
 
+def key_ranges(mem_len, n_tokens, world, rank):
+    """Rank `rank`'s keys under the key-range split, as (tile start, tiles, valid keys) per code segment
+    (memory, then chunk; chunk only without a memory part): its `key_tiles` of the memory part and the
+    128-token tiles of its own chunk share (none when the share is empty)."""
+    part = share_part(n_tokens, world)
+    lo = min(n_tokens, rank * part)
+    valid = min(n_tokens, lo + part) - lo
+    lo = lo if valid > 0 else 0
+    chunk = (lo // 128, -(-(lo + valid) // 128) - lo // 128 if valid else 0, n_tokens)
+    if mem_len == 0:
+        return [chunk]
+    m0, m1 = key_tiles(mem_len, world, rank)
+    return [(m0, m1 - m0, mem_len), chunk]
+
+
 class KeySplitAttention(SplitAttention):
     """One rank's self-attention for one layer of a chunk under the key-range split: the rank attends
     EVERY query row of the chunk, but only against its own keys — its slice of the memory part
@@ -389,12 +404,7 @@ class KeySplitAttention(SplitAttention):
 
     def ranges(self):
         """(tile start, tiles, valid keys) of each code segment this rank attends."""
-        chunk_t0 = self._lo // 128
-        chunk = (chunk_t0, -(-(self._lo + self.share_valid) // 128) - chunk_t0 if self.share_valid else 0, self.n)
-        if self.mem_len == 0:
-            return [chunk]
-        m0, m1 = self.mem_tiles
-        return [(m0, m1 - m0, self.mem_len), chunk]
+        return key_ranges(self.mem_len, self.n, self.world, self.rank)
 
     def __call__(self, q_rows, cache, k_part, v_part, out, sm_scale=None, num_splits=None, attn_events=None,
                  persist=True):

@@ -111,3 +111,42 @@ def test_key_ranges_restate_the_split_emulation():
     # a partial made of two pieces runs them under one running max: the same as one piece
     assert torch.equal(O.attn_from_codes(*codes, **kernel, key_ranges=[[(0, 256), (256, 700)]]),
                        O.attn_from_codes(*codes, **kernel))
+
+
+@pytest.mark.parametrize("mem,n", [(24128, 6032), (48256, 6032), (1280, 700), (0, 6032)])
+@pytest.mark.parametrize("world", range(1, 9))
+def test_every_rank_passes_the_abi_checks(mem, n, world):
+    """The arguments KeySplitAttention gives lbq_attn_fwd_keys and lbq_quant_kv_tiles pass the ABI's
+    validation for every rank (BASELINE config 4 and 5 windows among them): on a host without a GPU the
+    calls then stop at the tensor map or the launch (LBQ_ERR_CUDA), never at an argument check."""
+    if mem == 0 and n <= (world - 1) * split.share_part(n, world):
+        pytest.skip("the last ranks hold no keys (KeySplitAttention rejects this split)")
+    if mem and -(-mem // 128) < world:
+        pytest.skip("fewer memory tiles than ranks (KeySplitAttention rejects this split)")
+    lib = _lib.load()
+    fake = ctypes.c_void_p(0x10000)
+    part = split.share_part(n, world)
+    nseg = 2 if mem else 1
+    seg_len = mem if mem else n
+    covered = 0
+    for rank in range(world):
+        rg = split.key_ranges(mem, n, world, rank)
+        assert len(rg) == nseg and sum(t for _, t, _ in rg) >= 1
+        arr = ctypes.c_int * nseg
+        rc = lib.lbq_attn_fwd_keys(fake, fake, n, world * part, fake, fake, fake, nseg, seg_len, 1, 12, 0.0,
+                                   arr(*[x[0] for x in rg]), arr(*[x[1] for x in rg]), arr(*[x[2] for x in rg]),
+                                   fake, world, rank, 0, part, 1 << 20, 1 << 24, None)
+        assert rc == 3, (rank, rc, _err())                              # LBQ_ERR_CUDA: validation passed
+        act = (fake, 1536, 1536, 128)
+        for s, (t0, nt, valid) in enumerate(rg):
+            if nt == 0:
+                continue
+            chunk = s == nseg - 1
+            lo = t0 * 128 if chunk else 0
+            rc = lib.lbq_quant_kv_tiles(*act, *act, 1, 12, -lo if chunk else 0, s, nseg,
+                                        (min(n, lo + part) if chunk else valid), seg_len, mem + n,
+                                        fake, fake, fake, fake, fake, fake, fake, int(not chunk or mem == 0),
+                                        t0, t0 + nt, None)
+            assert rc == 3, (rank, s, rc, _err())
+            covered += min(valid, (t0 + nt) * 128) - t0 * 128
+    assert covered == mem + n                                            # every key of the window once
