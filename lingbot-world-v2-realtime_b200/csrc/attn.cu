@@ -29,7 +29,6 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
-#include <cstdlib>
 
 #include "lbq_kernels.h"
 #include "lbq_peer.cuh"
@@ -510,408 +509,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if constexpr (kKeyRange) signal_after_last_cta(a.peers, a.nranks, a.rank, a.xchg_off, xchg::kDoneAttn);
 }
 
-// Key-range epilogue of the persistent kernel: as store_key_partial, but each warp stages its 32 rows
-// in its own rows of the tile's two P buffers only (chunks 0-7 of a row in its P row of buffer 0, chunks
-// 8-15 in buffer 1, 128-byte swizzle), so that a warp that has moved on to the next item and writes its
-// P rows cannot overwrite another warp's staged rows.
-__device__ __forceinline__ void store_key_partial_own_rows(const AttnArgs& a, uint32_t tO, uint8_t* ptile,
-                                                           int quarter, int lane, int qtile, int bh, int bhs,
-                                                           float m, float dsum) {
-  const float rd = __frcp_rn(dsum);
-  const int rl = quarter * 32 + lane;                    // row inside the tile (TMEM lane)
-  auto stage = [&](int row, int chunk) {                 // 16-byte chunk `chunk` of tile row `row`
-    return ptile + (chunk >> 3) * kTile + row * 128 + (((chunk & 7) ^ (row & 7)) << 4);
-  };
-#pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
-    uint32_t ov[32];
-    tmem_ld32(tO + 32 * c, ov);
-    tmem_ld_wait();
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      uint32_t hw[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const __half2 p = __floats2half2_rn(__fmul_rn(__uint_as_float(ov[8 * e + 2 * k]), rd),
-                                            __fmul_rn(__uint_as_float(ov[8 * e + 2 * k + 1]), rd));
-        hw[k] = *reinterpret_cast<const uint32_t*>(&p);
-      }
-      *reinterpret_cast<uint4*>(stage(rl, 4 * c + e)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    }
-  }
-  __syncwarp();
-  const int qrow0 = qtile * 128;
-  const int owner = qrow0 / a.part;                      // part % 128 == 0: one owner per Q tile
-  if (!LBQ_CHECK(owner < a.nranks && qrow0 - owner * a.part + 128 <= a.part, a.status, kDevBadOwner)) return;
-  const int64_t slot = (int64_t(a.rank) * bhs + bh) * a.part + (qrow0 - owner * a.part);
-  char* dst = reinterpret_cast<char*>(static_cast<uintptr_t>(a.peers[owner]));
-  uint8_t* dst_o = reinterpret_cast<uint8_t*>(dst + a.recv_o_off) + slot * 256;
-#pragma unroll 4
-  for (int i = 0; i < 16; ++i) {
-    const int r = quarter * 32 + 2 * i + (lane >> 4), ch = lane & 15;
-    if (qrow0 + r < a.q_len)
-      *reinterpret_cast<uint4*>(dst_o + r * 256 + ch * 16) = *reinterpret_cast<const uint4*>(stage(r, ch));
-  }
-  if (qrow0 + rl < a.q_len) reinterpret_cast<float2*>(dst + a.recv_ml_off)[slot + rl] = make_float2(m, dsum);
-  // the staged rows are read before this warp writes its next P rows over them
-  __syncwarp();
-}
-
-// ------------------------------------------------------------------ persistent variant
-// The same computation as attn_fwd_kernel with a grid of at most one CTA per SM, each looping over
-// work items (Q-tile pair, batch*head, KV split) = blockIdx.x, blockIdx.x + gridDim.x, ...: barrier
-// setup, tensor-memory allocation and tensor-map prefetch are paid once per SM instead of once per
-// item, and the producer loads the next item's Q and first K/V tiles while the softmax warpgroups
-// finish the current item's epilogue. Every per-tile barrier keeps counting across items (g = the
-// CTA's running tile count), and two more barriers order the item hand-over:
-//   q_empty   the issuer's commit after an item's last Q.K^T; the producer waits before reloading Q;
-//   o_free[t] the softmax warpgroup's arrival after its epilogue has read O_t; the issuer waits before
-//             the next item's first P.V of that tile (which overwrites O_t).
-// Every item must hold at least one key tile (the host clamps the split count so that none is empty).
-struct AttnSharedP {
-  AttnShared base;
-  uint64_t q_empty;
-  uint64_t o_free[2];
-};
-constexpr size_t kAttnSmemBytesP = 1024 + kTile * (6 + 2 * kStages) + sizeof(AttnSharedP);
-
-struct AttnItem {
-  int qp, bh, split, t_begin, n;
-};
-__device__ __forceinline__ AttnItem attn_item(const AttnArgs& a, int it, int qpairs, int bhs) {
-  AttnItem w;
-  w.qp = it % qpairs;
-  const int r = it / qpairs;
-  w.bh = r % bhs;
-  w.split = r / bhs;
-  w.t_begin = w.split * a.tiles_per_split;
-  w.n = min(w.t_begin + a.tiles_per_split, a.total_tiles) - w.t_begin;
-  return w;
-}
-
-template <bool kKeyRange>
-__global__ void __launch_bounds__(kAttnThreads, 1)
-    attn_fwd_persistent_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                               const __grid_constant__ CUtensorMap tm_v, const AttnArgs a, int items) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sP = smem + 2 * kTile;
-  uint8_t* sK = smem + 6 * kTile;
-  uint8_t* sV = smem + kTile * (6 + kStages);
-  AttnSharedP* shp = reinterpret_cast<AttnSharedP*>(smem + kTile * (6 + 2 * kStages));
-  AttnShared* sh = &shp->base;
-  volatile int* abort_flag = &sh->abort;
-
-  const int qpairs = (a.q_pad / 128 + 1) / 2;
-  const int bhs = a.batch * a.heads;
-  const int tiles_per_seg = a.seg_pad / 128;
-  const int my_items = int(blockIdx.x) < items ? (items - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  if (threadIdx.x == 0) {
-    mbar_init(&sh->q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sh->k_full[s], 1);
-      mbar_init(&sh->k_empty[s], 1);
-      mbar_init(&sh->v_full[s], 1);
-      mbar_init(&sh->v_empty[s], 1);
-    }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(&sh->s_full[t], 1);
-      mbar_init(&sh->s_free[t], 128);
-      mbar_init(&sh->p_full[t], 128);
-      mbar_init(&sh->o_done[t], 1);
-      mbar_init(&shp->o_free[t], 128);
-    }
-    mbar_init(&shp->q_empty, 1);
-    mbar_init(&sh->drain, 1);
-    sh->abort = 0;
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(&sh->tmem_base, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = sh->tmem_base;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0 && my_items > 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      int g = 0, issued = 0, q_loads = 0;
-      bool ok = true;
-      for (int k = 0; ok && k < my_items; ++k) {
-        const AttnItem w = attn_item(a, int(blockIdx.x) + k * int(gridDim.x), qpairs, bhs);
-        // the previous item's last Q.K^T has read both Q tiles
-        if (k > 0 && !mbar_wait(&shp->q_empty, (k - 1) & 1, abort_flag, a.status, kDevTimeoutQ)) break;
-        mbar_arrive_expect_tx(&sh->q_full, 2 * kTile);
-        tma_load_3d(sQ, &tm_q, &sh->q_full, 0, (2 * w.qp) * 128, w.bh);
-        tma_load_3d(sQ + kTile, &tm_q, &sh->q_full, 0, (2 * w.qp + 1) * 128, w.bh);
-        ++q_loads;
-        for (int i = 0; i < w.n; ++i, ++g) {
-          int seg, lt;
-          tile_seg<kKeyRange>(a, w.t_begin + i, tiles_per_seg, seg, lt);
-          (void)LBQ_CHECK(seg < a.nseg && lt >= 0 && lt < tiles_per_seg, a.status, kDevBadTile);
-          const int s = g % kStages;
-          const uint32_t ph = (g / kStages) & 1;
-          if (!mbar_wait(&sh->k_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&sh->k_full[s], kTile);
-          tma_load_3d(sK + s * kTile, &tm_k, &sh->k_full[s], 0, lt * 128, seg * bhs + w.bh);
-          if (!mbar_wait(&sh->v_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) {
-            issued = g + 1;
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&sh->v_full[s], kTile);
-          tma_load_3d(sV + s * kTile, &tm_v, &sh->v_full[s], lt * 128, 0, seg * bhs + w.bh);
-          issued = g + 1;
-        }
-      }
-      if (*abort_flag) {
-        // Let copies already in flight land before the CTA's shared memory goes away.
-        if (q_loads > 0) mbar_drain_wait(&sh->q_full, (q_loads - 1) & 1);
-        for (int i = (issued > kStages ? issued - kStages : 0); i < issued; ++i) {
-          const int s = i % kStages;
-          const uint32_t ph = (i / kStages) & 1;
-          mbar_drain_wait(&sh->k_full[s], ph);
-          mbar_drain_wait(&sh->v_full[s], ph);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ tcgen05 issuer
-    if (lane == 0 && my_items > 0) {
-      const uint64_t qdesc[2] = {smem_desc_sw128(smem_u32(sQ)), smem_desc_sw128(smem_u32(sQ + kTile))};
-      auto issue_qk = [&](int t, int g) {
-        const uint64_t kdesc = smem_desc_sw128(smem_u32(sK + (g % kStages) * kTile));
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) mma_i8_ss(tmem + 128 * t, qdesc[t] + 2 * kk, kdesc + 2 * kk, kIdescQK, 1u);
-        tc_commit(&sh->s_full[t]);
-      };
-      auto issue_pv = [&](int t, int g, bool first) {
-        const uint64_t pdesc = smem_desc_sw128(smem_u32(sP + (2 * t + (g & 1)) * kTile));
-        const uint64_t vdesc = smem_desc_sw128(smem_u32(sV + (g % kStages) * kTile));
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_f8_ss(tmem + 256 + 128 * t, pdesc + 2 * kk, vdesc + 2 * kk, kIdescPV, (!first || kk > 0) ? 1u : 0u);
-        tc_commit(&sh->o_done[t]);
-      };
-      int g = 0;
-      bool ok = true;
-      for (int k = 0; ok && k < my_items; ++k) {
-        const AttnItem w = attn_item(a, int(blockIdx.x) + k * int(gridDim.x), qpairs, bhs);
-        ok = mbar_wait(&sh->q_full, k & 1, abort_flag, a.status, kDevTimeoutQ);
-        tc_fence_after();
-        if (ok && (ok = mbar_wait(&sh->k_full[g % kStages], (g / kStages) & 1, abort_flag, a.status,
-                                  kDevTimeoutKV))) {
-          for (int t = 0; ok && t < 2; ++t) {
-            // S_t initialised (first item) or read and refilled by the previous tile's softmax
-            ok = mbar_wait(&sh->s_free[t], g & 1, abort_flag, a.status, kDevTimeoutS);
-            tc_fence_after();
-            if (ok) issue_qk(t, g);
-          }
-          if (ok) tc_commit(&sh->k_empty[g % kStages]);
-        }
-        for (int j = 0; ok && j < w.n; ++j, ++g) {
-          const int s = g % kStages;
-          const bool more = j + 1 < w.n;
-          if (more && !(ok = mbar_wait(&sh->k_full[(g + 1) % kStages], ((g + 1) / kStages) & 1, abort_flag,
-                                       a.status, kDevTimeoutKV)))
-            break;
-          if (!(ok = mbar_wait(&sh->v_full[s], (g / kStages) & 1, abort_flag, a.status, kDevTimeoutKV))) break;
-          if (!more) tc_commit(&shp->q_empty);      // every Q.K^T of this item has been issued
-          for (int t = 0; ok && t < 2; ++t) {
-            if (more) {
-              if (!(ok = mbar_wait(&sh->s_free[t], (g + 1) & 1, abort_flag, a.status, kDevTimeoutS))) break;
-              tc_fence_after();
-              issue_qk(t, g + 1);
-            }
-            if (j == 0 && k > 0) {                 // O_t read by the previous item's epilogue
-              if (!(ok = mbar_wait(&shp->o_free[t], (k - 1) & 1, abort_flag, a.status, kDevTimeoutO))) break;
-              tc_fence_after();
-            }
-            if (!(ok = mbar_wait(&sh->p_full[t], g & 1, abort_flag, a.status, kDevTimeoutP))) break;
-            tc_fence_after();
-            issue_pv(t, g, j == 0);
-          }
-          if (!ok) break;
-          tc_commit(&sh->v_empty[s]);
-          if (more) tc_commit(&sh->k_empty[(g + 1) % kStages]);
-        }
-      }
-      // Drain: every MMA issued above has completed once `drain` flips.
-      tc_commit(&sh->drain);
-      mbar_drain_wait(&sh->drain, 0);
-    }
-  } else {
-    // ------------------------------------------------------------ softmax warpgroups
-    const int t = (warp - 2) >> 2;
-    const int quarter = warp & 3;
-    const uint32_t lane_off = uint32_t(quarter * 32) << 16;
-    const uint32_t tS = tmem + 128 * t + lane_off, tO = tmem + 256 + 128 * t + lane_off;
-    const int kspb = a.seg_pad / 64;
-    const int prow_off = (quarter * 32 + lane) * 128;
-    const int rsw = lane & 7;
-    bool ok = my_items > 0;
-    int g = 0;
-    if (ok) {
-#pragma unroll
-      for (int c = 0; c < 16; ++c) tmem_fill8(tS + 8 * c, 0x4B400000u);
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&sh->s_free[t]);
-    }
-    for (int k = 0; ok && k < my_items; ++k) {
-      const AttnItem w = attn_item(a, int(blockIdx.x) + k * int(gridDim.x), qpairs, bhs);
-      const int bh = w.bh, b = bh / a.heads, h = bh - (bh / a.heads) * a.heads;
-      const int qtile = 2 * w.qp + t;
-      const int row = qtile * 128 + quarter * 32 + lane;
-      const float qs = qtile * 128 < a.q_pad ? a.q_scale[int64_t(bh) * (a.q_pad / 32) + qtile * 4 + quarter] : 0.f;
-      auto kscale_ptr = [&](int i) {
-        int seg, lt;
-        tile_seg<kKeyRange>(a, w.t_begin + i, tiles_per_seg, seg, lt);
-        if (!LBQ_CHECK(seg < a.nseg && lt >= 0 && lt * 2 + 1 < kspb, a.status, kDevBadTile)) seg = lt = 0;
-        return a.k_scale + int64_t(seg * bhs + bh) * kspb + lt * 2;
-      };
-      float m = -INFINITY, dsum = 0.f;
-      float2 ks_next = *reinterpret_cast<const float2*>(kscale_ptr(0));
-      for (int i = 0; ok && i < w.n; ++i, ++g) {
-        int seg, lt;
-        tile_seg<kKeyRange>(a, w.t_begin + i, tiles_per_seg, seg, lt);
-        const int valid = min(128, seg_valid<kKeyRange>(a, seg) - lt * 128);
-        const float2 ks = ks_next;
-        if (i + 1 < w.n) ks_next = *reinterpret_cast<const float2*>(kscale_ptr(i + 1));
-        const float c1a = __fmul_rn(__fmul_rn(qs, ks.x), a.sm_log2);
-        const float c1b = __fmul_rn(__fmul_rn(qs, ks.y), a.sm_log2);
-        if (!mbar_wait(&sh->s_full[t], g & 1, abort_flag, a.status, kDevTimeoutS)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        uint32_t sv[4][32];
-        tmem_ld32(tS + 0, sv[0]);
-        tmem_ld32(tS + 32, sv[1]);
-        tmem_ld32(tS + 64, sv[2]);
-        tmem_ld32(tS + 96, sv[3]);
-        tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < 16; ++c) tmem_fill8(tS + 8 * c, 0x4B400000u);
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(&sh->s_free[t]);
-        // P_t[g & 1] was last read by the P.V of tile g - 2, complete since the o_done wait of tile
-        // g - 1 (in this item or at the end of the previous one)
-        uint8_t* prow = sP + (2 * t + (g & 1)) * kTile + prow_off;
-        const float alpha = valid == 128 ? softmax_tile<false>(sv, 128, c1a, c1b, m, dsum, prow, rsw)
-                                         : softmax_tile<true>(sv, valid, c1a, c1b, m, dsum, prow, rsw);
-        fence_proxy_async_smem();
-        if (i > 0) {
-          if (!mbar_wait(&sh->o_done[t], (g - 1) & 1, abort_flag, a.status, kDevTimeoutO)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          if (__any_sync(0xffffffffu, alpha != 1.f)) {
-            const uint64_t a2 = f2_pack(alpha, alpha);
-#pragma unroll 1
-            for (int c = 0; c < 4; c += 2) {
-              uint32_t ov[2][32];
-              tmem_ld32(tO + 32 * c, ov[0]);
-              tmem_ld32(tO + 32 * c + 32, ov[1]);
-              tmem_ld_wait();
-#pragma unroll
-              for (int h2 = 0; h2 < 2; ++h2) {
-#pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                  float lo, hi;
-                  f2_unpack(f2_mul(f2_pack(__uint_as_float(ov[h2][e]), __uint_as_float(ov[h2][e + 1])), a2), lo,
-                            hi);
-                  ov[h2][e] = __float_as_uint(lo);
-                  ov[h2][e + 1] = __float_as_uint(hi);
-                }
-              }
-              tmem_st32(tO + 32 * c, ov[0]);
-              tmem_st32(tO + 32 * c + 32, ov[1]);
-            }
-            tmem_st_wait();
-          }
-        }
-        tc_fence_before();
-        mbar_arrive(&sh->p_full[t]);
-      }
-      const bool o_ready = ok && mbar_wait(&sh->o_done[t], (g - 1) & 1, abort_flag, a.status, kDevTimeoutO);
-      if (!o_ready) ok = false;
-      if constexpr (kKeyRange) {
-        if (__all_sync(0xffffffffu, o_ready) && qtile * 128 < a.q_len) {
-          tc_fence_after();
-          store_key_partial_own_rows(a, tO, sP + 2 * t * kTile, quarter, lane, qtile, bh, bhs, m, dsum);
-        }
-      } else if (o_ready) {
-        tc_fence_after();
-        if (a.num_splits == 1) {
-          const float rd = __frcp_rn(dsum);
-          const float* vs = a.v_scale + int64_t(bh) * 128;
-          __nv_bfloat16* dst = a.out + b * a.so_b + int64_t(row) * a.so_l + h * a.so_h;
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t ov[32];
-            tmem_ld32(tO + 32 * c, ov);
-            tmem_ld_wait();
-            uint32_t packed[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float o0 = __fmul_rn(__fmul_rn(__uint_as_float(ov[2 * e]), rd), vs[32 * c + 2 * e]);
-              const float o1 = __fmul_rn(__fmul_rn(__uint_as_float(ov[2 * e + 1]), rd), vs[32 * c + 2 * e + 1]);
-              const __nv_bfloat162 pr = __floats2bfloat162_rn(o0, o1);
-              packed[e] = *reinterpret_cast<const uint32_t*>(&pr);
-            }
-            if (row < a.q_len) {
-#pragma unroll
-              for (int e = 0; e < 4; ++e)
-                reinterpret_cast<uint4*>(dst + 32 * c)[e] =
-                    make_uint4(packed[4 * e], packed[4 * e + 1], packed[4 * e + 2], packed[4 * e + 3]);
-            }
-          }
-        } else {
-          const int64_t prow = (int64_t(w.split) * bhs + bh) * a.q_pad + row;
-          float* dst = a.o_part + prow * 128;
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t ov[32];
-            tmem_ld32(tO + 32 * c, ov);
-            tmem_ld_wait();
-            if (row < a.q_len) {
-#pragma unroll
-              for (int e = 0; e < 8; ++e)
-                reinterpret_cast<uint4*>(dst + 32 * c)[e] =
-                    make_uint4(ov[4 * e], ov[4 * e + 1], ov[4 * e + 2], ov[4 * e + 3]);
-            }
-          }
-          if (row < a.q_len) a.ml_part[prow] = make_float2(m, dsum);
-        }
-      }
-      // O_t has been read (every tcgen05.ld above waited): the next item's first P.V may overwrite it
-      tc_fence_before();
-      mbar_arrive(&shp->o_free[t]);
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, 512);
-  if constexpr (kKeyRange) signal_after_last_cta(a.peers, a.nranks, a.rank, a.xchg_off, xchg::kDoneAttn);
-}
-
 // Flash-decoding merge of the per-split partials (splitkv/README.md:60-69): one warp per
 // (row, batch*head), 4 channels per lane.
 __global__ void __launch_bounds__(128) splitkv_combine_kernel(const CombineArgs a) {
@@ -1018,47 +615,12 @@ cudaError_t launch_attn_variant(const AttnArgs& a, const CUtensorMap& tm_q, cons
   return cudaGetLastError();
 }
 
-// Persistent schedule: min(items, SMs) CTAs looping over the items (attn_fwd_persistent_kernel).
-template <bool kKeyRange>
-cudaError_t launch_attn_persistent(const AttnArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
-                                   const CUtensorMap& tm_v, cudaStream_t st) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  static bool configured[64] = {};
-  static int sms[64] = {};
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!configured[dev]) {
-    e = cudaFuncSetAttribute(attn_fwd_persistent_kernel<kKeyRange>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             int(kAttnSmemBytesP));
-    if (e != cudaSuccess) return e;
-    e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return e;
-    configured[dev] = true;
-  }
-  const int64_t items = int64_t((a.q_pad / 128 + 1) / 2) * a.batch * a.heads * a.num_splits;
-  if (items <= 0 || items > (int64_t(1) << 31) - 1) return cudaErrorInvalidValue;
-  const int grid = int(items < sms[dev] ? items : sms[dev]);
-  if (cudaError_t e0 = prefer_max_shared<attn_fwd_persistent_kernel<kKeyRange>>(); e0 != cudaSuccess) return e0;
-  attn_fwd_persistent_kernel<kKeyRange><<<grid, kAttnThreads, kAttnSmemBytesP, st>>>(tm_q, tm_k, tm_v, a, int(items));
-  return cudaGetLastError();
-}
-
-// LBQ_ATTN_PERSISTENT=1 in the environment selects the persistent schedule (read at every launch, so a
-// process can compare the two; a captured CUDA graph keeps the schedule it was captured with).
-bool persistent_schedule() {
-  const char* e = std::getenv("LBQ_ATTN_PERSISTENT");
-  return e != nullptr && e[0] == '1';
-}
-
 cudaError_t launch_attn(const AttnArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                         cudaStream_t st) {
-  if (persistent_schedule()) return launch_attn_persistent<false>(a, tm_q, tm_k, tm_v, st);
   return launch_attn_variant<false>(a, tm_q, tm_k, tm_v, st);
 }
 cudaError_t launch_attn_keys(const AttnArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                              const CUtensorMap& tm_v, cudaStream_t st) {
-  if (persistent_schedule()) return launch_attn_persistent<true>(a, tm_q, tm_k, tm_v, st);
   return launch_attn_variant<true>(a, tm_q, tm_k, tm_v, st);
 }
 

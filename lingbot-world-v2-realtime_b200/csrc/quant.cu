@@ -20,7 +20,6 @@
 // attention kernel's masked keys are finite; key tiles past that are never read and not written.
 #include <cuda_bf16.h>
 #include <cstdint>
-#include <cstdlib>
 
 #include "lbq_ptx.cuh"
 #include "lbq_kernels.h"
@@ -49,10 +48,6 @@ __device__ __forceinline__ float warp_max(float x) {
 // ------------------------------------------------------------------ K/V block statistics
 // One CTA per (64-token block, head, batch). ksum: fp64 sum of K over the block's tokens that are
 // < kv_len; vamax: max |V|. 128 threads = 8 row groups x 16 chunks of 8 channels.
-// kLoadsFirst: all of a thread's 8 token loads are issued before the accumulation (one memory round
-// trip instead of eight dependent ones); the sums are accumulated in the same order, so both variants
-// give the same bits.
-template <bool kLoadsFirst>
 __global__ void __launch_bounds__(128) kv_block_stats_kernel(KvBlockStatsArgs a) {
   const int blk = a.blk_begin + blockIdx.x;
   const int h = blockIdx.y, b = blockIdx.z;
@@ -61,43 +56,18 @@ __global__ void __launch_bounds__(128) kv_block_stats_kernel(KvBlockStatsArgs a)
   float vm[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) { s[i] = 0.0; vm[i] = 0.f; }
-  if constexpr (kLoadsFirst) {
-    uint4 kr[8], vr[8];
+  for (int r = rg; r < 64; r += 8) {
+    const int64_t tok = int64_t(blk) * 64 + r;
+    if (tok >= a.kv_len) break;
+    const uint4 kr = *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + tok * a.sk_l + h * a.sk_h + c16 * 8);
+    const uint4 vr = *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + tok * a.sv_l + h * a.sv_h + c16 * 8);
+    float kf[8], vf[8];
+    bf16x8_to_f32(kr, kf);
+    bf16x8_to_f32(vr, vf);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int64_t tok = int64_t(blk) * 64 + rg + 8 * j;
-      const bool in = tok < a.kv_len;
-      kr[j] = in ? *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + tok * a.sk_l + h * a.sk_h + c16 * 8)
-                 : make_uint4(0u, 0u, 0u, 0u);
-      vr[j] = in ? *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + tok * a.sv_l + h * a.sv_h + c16 * 8)
-                 : make_uint4(0u, 0u, 0u, 0u);
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (int64_t(blk) * 64 + rg + 8 * j >= a.kv_len) break;
-      float kf[8], vf[8];
-      bf16x8_to_f32(kr[j], kf);
-      bf16x8_to_f32(vr[j], vf);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        s[i] += double(kf[i]);
-        vm[i] = fmaxf(vm[i], fabsf(vf[i]));
-      }
-    }
-  } else {
-    for (int r = rg; r < 64; r += 8) {
-      const int64_t tok = int64_t(blk) * 64 + r;
-      if (tok >= a.kv_len) break;
-      const uint4 kr = *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + tok * a.sk_l + h * a.sk_h + c16 * 8);
-      const uint4 vr = *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + tok * a.sv_l + h * a.sv_h + c16 * 8);
-      float kf[8], vf[8];
-      bf16x8_to_f32(kr, kf);
-      bf16x8_to_f32(vr, vf);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        s[i] += double(kf[i]);
-        vm[i] = fmaxf(vm[i], fabsf(vf[i]));
-      }
+    for (int i = 0; i < 8; ++i) {
+      s[i] += double(kf[i]);
+      vm[i] = fmaxf(vm[i], fabsf(vf[i]));
     }
   }
   // [row group][channel within chunk][chunk]: a warp's 16 chunks of one slot are consecutive words
@@ -349,192 +319,11 @@ __global__ void __launch_bounds__(256) quant_kv_kernel(QuantKArgs ka, QuantVArgs
   else quant_k_tile(ka, sh, tile, first, h, b);
 }
 
-// ------------------------------------------------------------------ K/V quantizer, pipelined
-// The same codes as quant_kv_kernel from a persistent grid (a few CTAs per SM): each CTA walks the work
-// items (K or V of a 128-token tile, head, batch) blockIdx.x, blockIdx.x + gridDim.x, ..., and while it
-// reduces and stores one item, the next item's bf16 tile already streams into its second shared buffer
-// (cp.async 16-byte pieces; rows past the segment are zero-filled without being read). Both tensors
-// are staged with the V path's 272-byte row pitch.
-constexpr int kPipeTileBytes = 128 * kVtPitch;
-
-struct QuantPipeShared {
-  float km[128];
-  float recp[128];
-  float red[8];
-};
-constexpr size_t kQuantPipeSmem = 2 * kPipeTileBytes + sizeof(QuantPipeShared);
-
-struct PipeItem {
-  bool is_v;
-  int tile, h, b;
-};
-__device__ __forceinline__ PipeItem pipe_item(int it, int tile0, int tiles, int heads) {
-  PipeItem w;
-  w.is_v = (it & 1) != 0;
-  const int rest = it >> 1;
-  w.tile = tile0 + rest % tiles;
-  const int r2 = rest / tiles;
-  w.h = r2 % heads;
-  w.b = r2 / heads;
-  return w;
-}
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
-               : "memory");
-}
-
-// Starts the copy of an item's 128 x 256-byte bf16 tile into `buf` (row r at r * kVtPitch).
-__device__ __forceinline__ void pipe_issue(const QuantKArgs& ka, const QuantVArgs& va, const PipeItem& w,
-                                           uint8_t* buf) {
-  const __nv_bfloat16* base = w.is_v ? va.v + w.b * va.sv_b + w.h * va.sv_h : ka.k + w.b * ka.sk_b + w.h * ka.sk_h;
-  const int64_t sl = w.is_v ? va.sv_l : ka.sk_l;
-  const int64_t tok0 = w.is_v ? va.tok0 : ka.tok0;
-  const int seg_valid = w.is_v ? va.seg_valid : ka.seg_valid;
-  [[maybe_unused]] int* status = w.is_v ? va.status : ka.status;    // debug-build index checks
-  const uint32_t sbuf = smem_u32(buf);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int piece = int(threadIdx.x) + 256 * i;    // 2048 pieces of 16 bytes
-    const int r = piece >> 4, c16 = piece & 15;
-    const int64_t tok = int64_t(w.tile) * 128 + r;
-    const bool valid = tok < seg_valid && LBQ_CHECK(tok0 + tok >= 0, status, kDevBadSourceToken);
-    const __nv_bfloat16* src = valid ? base + (tok0 + tok) * sl + c16 * 8 : base;
-    cp_async16(sbuf + uint32_t(r * kVtPitch + c16 * 16), src, valid);
-  }
-}
-
-// quant_k_tile with the tile read from `buf`.
-__device__ __forceinline__ void pipe_k(const QuantKArgs& a, QuantPipeShared& sh, const uint8_t* buf, const PipeItem& w,
-                                       bool first) {
-  const int half = threadIdx.x >> 7, t = threadIdx.x & 127, c16 = t & 15, rg = t >> 4;
-  const int blk = w.tile * 2 + half;
-  const int64_t bh = int64_t(w.b) * a.heads + w.h;
-  if (half == 0) {
-    const float km = window_mean_bf16(a.ksum_total, bh * 128 + t, a.kv_len_total);
-    sh.km[t] = km;
-    if (a.km_out != nullptr && first && a.write_km) a.km_out[bh * 128 + t] = __float2bfloat16_rn(km);
-  }
-  uint4 raw[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-    raw[i] = *reinterpret_cast<const uint4*>(buf + (half * 64 + rg + 8 * i) * kVtPitch + c16 * 16);
-  __syncthreads();
-  float km[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) km[j] = sh.km[c16 * 8 + j];
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int64_t tok = int64_t(blk) * 64 + rg + 8 * i;
-    if (tok < a.seg_valid) {
-      float x[8];
-      bf16x8_to_f32(raw[i], x);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(__fsub_rn(x[j], km[j])));
-    }
-  }
-  amax = warp_max(amax);
-  if ((t & 31) == 0) sh.red[half * 4 + (t >> 5)] = amax;
-  __syncthreads();
-  const float* red = sh.red + half * 4;
-  amax = fmaxf(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])), 1e-7f);
-  const float inv = __fmul_rn(__frcp_rn(amax), 127.f);
-  const int64_t seg_bh = (int64_t(a.seg) * a.batch + w.b) * a.heads + w.h;
-  const float scale = __fdiv_rn(amax, 127.f);
-  uint2 packed[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int r = rg + 8 * i;
-    const bool valid = int64_t(blk) * 64 + r < a.seg_valid;   // pad tokens encode 0
-    float x[8];
-    bf16x8_to_f32(raw[i], x);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) x[j] = valid ? __fmul_rn(__fsub_rn(x[j], km[j]), inv) : 0.f;
-    packed[i].x = pack_s8x4(cvt_rni_sat_s8(x[0]), cvt_rni_sat_s8(x[1]), cvt_rni_sat_s8(x[2]), cvt_rni_sat_s8(x[3]));
-    packed[i].y = pack_s8x4(cvt_rni_sat_s8(x[4]), cvt_rni_sat_s8(x[5]), cvt_rni_sat_s8(x[6]), cvt_rni_sat_s8(x[7]));
-  }
-  int8_t* dst = a.k_codes + (seg_bh * a.seg_pad + int64_t(blk) * 64) * 128;
-  if (t == 0) a.k_scale[seg_bh * (a.seg_pad / 64) + blk] = scale;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) *reinterpret_cast<uint2*>(dst + (rg + 8 * i) * 128 + c16 * 8) = packed[i];
-}
-
-// quant_v_tile with the tile already staged in `buf`.
-__device__ __forceinline__ void pipe_v(const QuantVArgs& a, QuantPipeShared& sh, const uint8_t* buf, const PipeItem& w,
-                                       bool first) {
-  const int t = threadIdx.x;
-  const int64_t bh = int64_t(w.b) * a.heads + w.h;
-  if (t < 128) {
-    const float amax = a.vamax_total[bh * 128 + t];
-    sh.recp[t] = __fmul_rn(__frcp_rn(amax), 2.25f);
-    if (first && a.write_scale) a.v_scale[bh * 128 + t] = __fdiv_rn(amax, 2.25f);
-  }
-  __syncthreads();
-  const int cp = t & 63, tq = t >> 6;
-  const float r0 = sh.recp[2 * cp], r1 = sh.recp[2 * cp + 1];
-  uint32_t w0[8], w1[8];                             // channel 2cp / 2cp+1: 32 key bytes each
-#pragma unroll
-  for (int k4 = 0; k4 < 8; ++k4) {
-    float lo[4], hi[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int r = tq * 32 + 4 * k4 + e;
-      const uint32_t pair = *reinterpret_cast<const uint32_t*>(buf + r * kVtPitch + cp * 4);
-      lo[e] = fminf(fmaxf(__fmul_rn(__uint_as_float(pair << 16), r0), -2.25f), 2.25f);
-      hi[e] = fminf(fmaxf(__fmul_rn(__uint_as_float(pair & 0xffff0000u), r1), -2.25f), 2.25f);
-    }
-    w0[k4] = pack_e4m3x2(lo[0], lo[1]) | (pack_e4m3x2(lo[2], lo[3]) << 16);
-    w1[k4] = pack_e4m3x2(hi[0], hi[1]) | (pack_e4m3x2(hi[2], hi[3]) << 16);
-  }
-  const int64_t seg_bh = (int64_t(a.seg) * a.batch + w.b) * a.heads + w.h;
-  uint8_t* dst = a.vt_codes + seg_bh * 128 * a.seg_pad + int64_t(w.tile) * 128 + tq * 32;
-  uint4* d0 = reinterpret_cast<uint4*>(dst + int64_t(2 * cp) * a.seg_pad);
-  uint4* d1 = reinterpret_cast<uint4*>(dst + int64_t(2 * cp + 1) * a.seg_pad);
-  d0[0] = make_uint4(w0[0], w0[1], w0[2], w0[3]);
-  d0[1] = make_uint4(w0[4], w0[5], w0[6], w0[7]);
-  d1[0] = make_uint4(w1[0], w1[1], w1[2], w1[3]);
-  d1[1] = make_uint4(w1[4], w1[5], w1[6], w1[7]);
-}
-
-// Three CTAs per SM (3 x 70 KB of shared memory): at most 85 registers a thread.
-__global__ void __launch_bounds__(256, 3) quant_kv_pipe_kernel(QuantKArgs ka, QuantVArgs va, int tile0, int tiles,
-                                                               int items) {
-  extern __shared__ __align__(16) uint8_t pipe_smem[];
-  QuantPipeShared& sh = *reinterpret_cast<QuantPipeShared*>(pipe_smem + 2 * kPipeTileBytes);
-  int it = blockIdx.x;
-  if (it >= items) return;
-  pipe_issue(ka, va, pipe_item(it, tile0, tiles, ka.heads), pipe_smem);
-  asm volatile("cp.async.commit_group;" ::: "memory");
-  for (int k = 0; it < items; ++k, it += gridDim.x) {
-    const int next = it + int(gridDim.x);
-    if (next < items)
-      pipe_issue(ka, va, pipe_item(next, tile0, tiles, ka.heads), pipe_smem + ((k + 1) & 1) * kPipeTileBytes);
-    asm volatile("cp.async.commit_group;" ::: "memory");   // possibly empty: one group per item
-    asm volatile("cp.async.wait_group 1;" ::: "memory");    // this thread's pieces of item k landed
-    __syncthreads();                                        // ... and every thread's
-    const PipeItem w = pipe_item(it, tile0, tiles, ka.heads);
-    const uint8_t* cur = pipe_smem + (k & 1) * kPipeTileBytes;
-    if (w.is_v) pipe_v(va, sh, cur, w, w.tile == tile0);
-    else pipe_k(ka, sh, cur, w, w.tile == tile0);
-    __syncthreads();                                        // buffer k & 1 and `sh` free again
-  }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-}
-
 // ------------------------------------------------------------------ launchers
 cudaError_t launch_kv_block_stats(const KvBlockStatsArgs& a, cudaStream_t st) {
   dim3 grid(a.blk_end - a.blk_begin, a.heads, a.batch);
-  // LBQ_STATS_LOADS_FIRST=1 selects the variant that issues every load before accumulating (an A/B
-  // switch, read at every launch)
-  const char* env = std::getenv("LBQ_STATS_LOADS_FIRST");
-  if (env != nullptr && env[0] == '1') {
-    if (cudaError_t e0 = prefer_max_shared<kv_block_stats_kernel<true>>(); e0 != cudaSuccess) return e0;
-    kv_block_stats_kernel<true><<<grid, 128, 0, st>>>(a);
-  } else {
-    if (cudaError_t e0 = prefer_max_shared<kv_block_stats_kernel<false>>(); e0 != cudaSuccess) return e0;
-    kv_block_stats_kernel<false><<<grid, 128, 0, st>>>(a);
-  }
+  if (cudaError_t e0 = prefer_max_shared<kv_block_stats_kernel>(); e0 != cudaSuccess) return e0;
+  kv_block_stats_kernel<<<grid, 128, 0, st>>>(a);
   return cudaGetLastError();
 }
 cudaError_t launch_kv_window_sums(const KvWindowSumsArgs& a, cudaStream_t st) {
@@ -553,29 +342,6 @@ cudaError_t launch_quant_q(const QuantQArgs& a, cudaStream_t st) {
 // segment does not pay for the padding of its seg_pad, which the attention never reads.
 cudaError_t launch_quant_kv(const QuantKArgs& ka, const QuantVArgs& va, int tile0, int tiles, cudaStream_t st) {
   if (tiles <= 0) return cudaSuccess;
-  // LBQ_QUANT_PIPELINED=1 selects the persistent, prefetching variant (an A/B switch, read at every launch)
-  const char* env = std::getenv("LBQ_QUANT_PIPELINED");
-  if (env != nullptr && env[0] == '1') {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    static bool configured[64] = {};
-    static int sms[64] = {};
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!configured[dev]) {
-      e = cudaFuncSetAttribute(quant_kv_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kQuantPipeSmem));
-      if (e != cudaSuccess) return e;
-      e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-      if (e != cudaSuccess) return e;
-      configured[dev] = true;
-    }
-    const int64_t items = int64_t(tiles) * 2 * ka.heads * ka.batch;
-    if (items > (int64_t(1) << 31) - 1) return cudaErrorInvalidValue;
-    const int64_t cap = int64_t(3) * sms[dev];               // three 70 KB CTAs per SM
-    const int grid = int(items < cap ? items : cap);
-    quant_kv_pipe_kernel<<<grid, 256, kQuantPipeSmem, st>>>(ka, va, tile0, tiles, int(items));
-    return cudaGetLastError();
-  }
   // no carveout preference: the driver's choice measured fastest for this kernel (5.0 TB/s on the
   // 30-layer re-quant, 3.9 TB/s with the largest shared-memory split)
   dim3 grid(tiles * 2, ka.heads, ka.batch);

@@ -124,29 +124,43 @@ def quantize_qkv(q, k, v):
 
 
 def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_scale=None,
-                    tile=BLK_K, pv_accum="fp16", rows=None, heads=None, splits=1, key_ranges=None,
+                    pv_accum="fp16", rows=None, heads=None, splits=1, key_ranges=None,
                     partial_fp16=False):
     """Torch emulation of Sage's `qk_int8_sv_f8_accum_f16_fuse_v_scale_attn_inst_buf` (the call at
-    sage_preq.py:126-127 / sage_kvq.py:107-110), non-causal, per-warp Q granularity.
+    sage_preq.py:126-127 / sage_kvq.py:107-110), non-causal, per-warp Q granularity, with the kernel's
+    own fp32 arithmetic order.
 
-    Semantics (splitkv/README.md:51-69, cfg_fixedmax.patch:90-93, sage_kvq.py:15-19):
-      s      = (q_i8 . k_i8) * q_scale[row/32] * k_scale[key/64]        (int32 product is exact)
-      per key tile of `tile` keys, in order: m = running row max of s;
-      P      = exp2((s - m) * sm_scale * log2e + 8.807)                  (fp32, <= 448)
-      d      = d * exp2((m_old - m) * sm_scale * log2e) + sum(P)         (fp32 P, before fp8)
-      O      = O * same factor + e4m3(P) @ e4m3(V)                       (fp16 inside a tile when
-                                                                           pv_accum == "fp16")
-      out    = O / d * v_scale
+    The loop runs over 64-key tiles (CTA_K = 64, sage_kvq.py:29) in order. For a row with Q scale
+    q_s (its 32-row group) and a tile with K scale k_s (its 64-token block), S = q_i8 . k_i8 (exact
+    int32), and with sm = fl(sm_scale * log2 e):
+      main tiles    c = fl(sm * fl(q_s * k_s))       the per-tile scale upstream passes to update_mdo
+                    m_t = fma(max_j S_j, c, -8.807)   (cfg_condrescale.patch:20, cfg_fusedsoftmax.patch:127)
+                    x_j = fma(S_j, c, -m)             (cfg_fusedsoftmax.patch:157)
+      last 2 tiles  r_j = fl(S_j * fl(q_s * k_s))    upstream's last two iterations call update_mdo with
+                    m_t = fma(max_j r_j, sm, -8.807)  `original_sm_scale` (cfg_fixedmax.patch:307,329), i.e.
+                    x_j = fma(r_j, sm, -m)            on scores that already carry the dequant scale
+      m     = max(m_prev, m_t)                        (m starts at -inf: upstream's -5e6 with d = 1 is
+      alpha = exp2(m_prev - m)                         cleared by the first alpha = 0)
+      P_j   = exp2(x_j)                               (fp32, <= 448: the row max lands on 2^8.807)
+      d     = d * alpha + sum_j P_j                   (fp32 P, before the e4m3 rounding)
+      O     = O * alpha + e4m3(P) @ e4m3(V)           (fp16 inside a tile in 32-key steps when
+                                                       pv_accum == "fp16", the "inst buf"; else fp32)
+      out   = O / d * v_scale                         (splitkv/README.md:51-69)
+    Each fma is evaluated exactly in float64 and rounded once to float32 (the products S * c fit in
+    45 bits). `m` is in the log2 domain and includes -8.807 and the dequant scale
+    (splitkv/README.md:58).
+
     Returns fp32 [B, Lq, H, D]. `rows` / `heads` restrict the computation to a subset (query rows
     are independent, so the subset equals the same rows of the full result).
-    `splits` > 1 emulates split-KV (splitkv/README.md:36-69): the key tiles are cut into `splits`
-    contiguous ranges (ceil division, empty ranges dropped), each runs the loop above from a fresh
-    running max, and the partials merge as out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) d_s.
+    `splits` > 1 emulates split-KV (splitkv/README.md:36-69) as the CUDA path cuts it: the 128-key
+    tiles are cut into `splits` contiguous ranges (ceil division, empty ranges dropped), each runs the
+    loop above from a fresh running max (its own last two tiles included), and the partials merge as
+    out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) d_s.
     `key_ranges` replaces the split ranges with the key-range sequence split: one partial per rank,
-    each a list of (lo, hi) key ranges that the rank's loop runs through in order with one running
-    max (its memory tiles, then its chunk share). With `partial_fp16` each partial travels as
-    fp16(O_s / d_s) with (m_s, d_s), and the merge is out = sum_s w_s fp16(O_s / d_s) / sum_s w_s with
-    w_s = 2^(m_s - M) d_s.
+    each a list of (lo, hi) key ranges (lo a multiple of 64) that the rank's loop runs through in
+    order with one running max (its memory tiles, then its chunk share). With `partial_fp16` each
+    partial travels as fp16(O_s / d_s) with (m_s, d_s), and the merge is
+    out = sum_s w_s fp16(O_s / d_s) / sum_s w_s with w_s = 2^(m_s - M) d_s.
     """
     b, lq, h, d = q_codes.shape
     lk = k_codes.shape[1]
@@ -157,10 +171,9 @@ def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_sca
     heads = range(h) if heads is None else heads
     out = torch.zeros(b, lq, h, d, dtype=torch.float32)
     vq_all = e4m3_to_float(v_codes)                                    # [B, Lk, H, D]
-    off = torch.tensor(S_FP8_OFFSET, dtype=torch.float32)
-    ntiles = (lk + tile - 1) // tile
-    per = (ntiles + splits - 1) // splits
-    partials = [[(s0 * tile, min(lk, (s0 + per) * tile))] for s0 in range(0, ntiles, per)]
+    n128 = (lk + 127) // 128
+    per = (n128 + splits - 1) // splits
+    partials = [[(s0 * 128, min(lk, (s0 + per) * 128))] for s0 in range(0, n128, per)]
     if key_ranges is not None:
         partials = [[(lo, hi_) for lo, hi_ in pieces if hi_ > lo] for pieces in key_ranges]
         partials = [p for p in partials if p]
@@ -172,16 +185,17 @@ def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_sca
             vf = vq_all[bi, :, hi]                                       # [Lk, D]
             parts = []
             for pieces in partials:
+                tiles = [(t0, min(t0 + BLK_K, hi_)) for lo, hi_ in pieces for t0 in range(lo, hi_, BLK_K)]
                 state = None
-                for lo, hi_ in pieces:
-                    state = _attn_range(qf, qs, kf, vf, k_scale[bi, hi], lo, hi_, tile, pv_accum, sm_log2, off,
-                                        state)
+                for i, (t0, t1) in enumerate(tiles):
+                    state = _attn_tile(qf, qs, kf, vf, k_scale[bi, hi][t0 // BLK_K], t0, t1, pv_accum, sm_log2,
+                                       state, tail=i >= len(tiles) - 2)
                 parts.append(state)
             mx = torch.stack([p[0] for p in parts]).max(dim=0).values
             acc = torch.zeros(qf.shape[0], d)
             dsum = torch.zeros(qf.shape[0])
             for m_s, d_s, o_s in parts:
-                w = torch.exp2((m_s - mx) * sm_log2)
+                w = torch.exp2(m_s - mx)
                 if partial_fp16:
                     o_s = (o_s / d_s[:, None]).half().float() * d_s[:, None]
                 acc += w[:, None] * o_s
@@ -191,9 +205,15 @@ def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_sca
     return out
 
 
-def _attn_range(qf, qs, kf, vf, ks_all, lo, hi, tile, pv_accum, sm_log2, off, state=None):
-    """The kernel loop over keys [lo, hi), continuing from `state` (running max m, row sum d,
-    unnormalized O) when given: returns the updated (m, d, O)."""
+def _fma32(a, b, c):
+    """fp32 fma(a, b, c) for float32 tensors: the exact value in float64 (a * b has at most 48
+    significant bits here), rounded once to float32."""
+    return (a.double() * b.double() + c.double()).float()
+
+
+def _attn_tile(qf, qs, kf, vf, ks, t0, t1, pv_accum, sm_log2, state, tail):
+    """One 64-key tile [t0, t1) of the kernel loop (one K scale `ks`), continuing from `state`
+    (running max m, row sum d, unnormalized O) when given: returns the updated (m, d, O)."""
     r, d = qf.shape[0], vf.shape[1]
     if state is None:
         m = torch.full((r,), -math.inf)
@@ -201,26 +221,30 @@ def _attn_range(qf, qs, kf, vf, ks_all, lo, hi, tile, pv_accum, sm_log2, off, st
         acc = torch.zeros(r, d)
     else:
         m, dsum, acc = state
-    for t0 in range(lo, hi, tile):
-        t1 = min(t0 + tile, hi)
-        s_int = qf @ kf[t0:t1].T                                 # exact integers
-        ks = ks_all[torch.arange(t0, t1) // BLK_K]               # [T]
-        s = s_int * (qs[:, None] * ks[None, :])                  # dequantized, fp32
-        m_new = torch.maximum(m, s.max(dim=1).values)
-        alpha = torch.exp2((m - m_new) * sm_log2)
-        p = torch.exp2((s - m_new[:, None]) * sm_log2 + off)
-        dsum = dsum * alpha + p.sum(dim=1)
-        pq = e4m3_to_float(e4m3_rn_satfinite(p))
-        if pv_accum == "fp16":
-            tile_acc = torch.zeros(r, d)
-            for c0 in range(0, t1 - t0, 32):                     # m16n8k32 steps
-                c1 = min(c0 + 32, t1 - t0)
-                tile_acc = (tile_acc + pq[:, c0:c1] @ vf[t0 + c0:t0 + c1]).half().float()
-        else:
-            tile_acc = pq @ vf[t0:t1]
-        acc = acc * alpha[:, None] + tile_acc
-        m = m_new
-    return m, dsum, acc
+    s_int = qf @ kf[t0:t1].T                                     # exact integers (|S| < 2^21)
+    dq = (qs * ks).float()                                        # fl(q_s * k_s) per row
+    neg_off = torch.tensor(-S_FP8_OFFSET, dtype=torch.float32)
+    if tail:
+        rs = (s_int.double() * dq.double()[:, None]).float()     # fl(S * dequant)
+        scale = sm_log2.expand(r)
+    else:
+        rs = s_int
+        scale = (sm_log2 * dq).float()                            # fl(sm * dequant)
+    m_t = _fma32(rs.max(dim=1).values, scale, neg_off.expand(r))
+    m_new = torch.maximum(m, m_t)
+    alpha = torch.exp2(m - m_new)
+    p = torch.exp2(_fma32(rs, scale[:, None], -m_new[:, None]))
+    dsum = dsum * alpha + p.sum(dim=1)
+    pq = e4m3_to_float(e4m3_rn_satfinite(p))
+    if pv_accum == "fp16":
+        tile_acc = torch.zeros(r, d)
+        for c0 in range(0, t1 - t0, 32):                         # m16n8k32 steps
+            c1 = min(c0 + 32, t1 - t0)
+            tile_acc = (tile_acc + pq[:, c0:c1] @ vf[t0 + c0:t0 + c1]).half().float()
+    else:
+        tile_acc = pq @ vf[t0:t1]
+    acc = acc * alpha[:, None] + tile_acc
+    return m_new, dsum, acc
 
 
 def sage_attention(q, k, v, sm_scale=None, **kw):

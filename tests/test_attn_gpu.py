@@ -22,7 +22,7 @@ def oracle_from_window(w, rows=None, heads=None, sm_scale=None, kernel_granulari
     qs = w.q_scale.cpu()
     nb = (w.kv_len + 63) // 64
     ks = w.k_scale[0][:, :, :nb].cpu()
-    kw = dict(tile=128, pv_accum="fp32", splits=splits) if kernel_granularity else {}
+    kw = dict(pv_accum="fp32", splits=splits) if kernel_granularity else dict(splits=splits)
     return O.attn_from_codes(q_codes_nhd(w), qs, k_codes_nhd(w), ks, v_codes_nhd(w), w.v_scale.cpu(),
                              sm_scale=sm_scale, rows=rows, heads=heads, **kw)
 

@@ -38,7 +38,7 @@ def test_key_range_merge_matches_whole_window(world, mem, n):
     """Merging every rank's key-range partials sent as fp16 O / row sum equals the same key ranges merged
     in fp32 up to fp16 rounding, stays within the Sage tolerance of the whole window (the P grid
     follows each range's running max, as with split-KV), and is as close to fp32 attention as the
-    whole-window result (128-key tiles and fp32 P.V, as the kernel)."""
+    whole-window result (fp32 P.V, as the kernel)."""
     g = torch.Generator().manual_seed(5 + world)
     lq, h = 160, 2
     q = torch.randn(1, lq, h, 128, generator=g).bfloat16()
@@ -46,7 +46,7 @@ def test_key_range_merge_matches_whole_window(world, mem, n):
     v = torch.randn(1, mem + n, h, 128, generator=g).bfloat16()
     qq = O.quantize_qkv(q, k, v)
     codes = (qq["q_codes"], qq["q_scale"], qq["k_codes"], qq["k_scale"], qq["v_codes"], qq["v_scale"])
-    kernel = dict(tile=128, pv_accum="fp32")
+    kernel = dict(pv_accum="fp32")
     ranges = [_rank_ranges(mem, n, world, rank) for rank in range(world)]     # one partial per rank
     covered = sorted(r for pieces in ranges for r in pieces if r[1] > r[0])
     assert covered[0][0] == 0 and covered[-1][1] == mem + n
@@ -101,7 +101,7 @@ def test_key_ranges_restate_the_split_emulation():
     v = torch.randn(1, 700, 2, 128, generator=g).bfloat16()
     qq = O.quantize_qkv(q, k, v)
     codes = (qq["q_codes"], qq["q_scale"], qq["k_codes"], qq["k_scale"], qq["v_codes"], qq["v_scale"])
-    kernel = dict(tile=128, pv_accum="fp32")
+    kernel = dict(pv_accum="fp32")
     assert torch.equal(O.attn_from_codes(*codes, **kernel, key_ranges=[[(0, 700)]]),
                        O.attn_from_codes(*codes, **kernel))
     per = 2 * 128                                  # 6 tiles in 3 splits

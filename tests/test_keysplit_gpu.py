@@ -160,7 +160,7 @@ def test_key_ranges_emulated_on_one_gpu(world, mem, n):
     got = out.float().cpu()
     nb = (w.kv_len + 63) // 64
     emu = O.attn_from_codes(q_codes_nhd(w), w.q_scale.cpu(), k_codes_nhd(w), w.k_scale[0][:, :, :nb].cpu(),
-                            v_codes_nhd(w), w.v_scale.cpu(), tile=128, pv_accum="fp32", key_ranges=window_ranges,
+                            v_codes_nhd(w), w.v_scale.cpu(), pv_accum="fp32", key_ranges=window_ranges,
                             partial_fp16=True)
     exact = O.compare(got, emu)
     assert exact["cos"] >= 0.99999 and exact["max_abs"] <= MAX_ABS, exact
