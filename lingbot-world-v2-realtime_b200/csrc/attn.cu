@@ -1,31 +1,38 @@
-// Quantized attention forward for sm_100a: INT8 Q.K^T and FP8 P.V on tcgen05, accumulators in
-// tensor memory, operands staged by TMA, warp-specialised, two Q tiles in ping-pong.
+// Quantized attention forward for sm_100a: INT8 Q.K^T and FP8 P.V on tcgen05, accumulators in tensor
+// memory, operands staged by TMA, warp-specialised, two Q tiles per CTA.
 //
-// Semantics are those of SageAttention-2's `qk_int8_sv_f8_accum_f16_fuse_v_scale_attn_inst_buf`
-// as the reference calls it (lingbot/layers/sage_preq.py:126-127 with qk_quant_gran=2, i.e. one
-// Q scale per 32 rows; documented in experiments/bench_attn/splitkv/README.md:51-69 and
-// h2_tiles/cfg_fixedmax.patch:90-93):
-//   s   = (q_i8 . k_i8) * q_scale * k_scale * sm_scale * log2(e)      (int32 dot product, exact)
-//   m   = running row max of s, updated once per 128-key tile
-//   P   = exp2(s - m + 8.807)  (<= 448), rounded to e4m3 for the P.V product
-//   d   = d * exp2(m_old - m) + sum(P)                                (fp32, before rounding)
-//   O   = O * exp2(m_old - m) + e4m3(P) . e4m3(V)                      (fp32 in tensor memory)
-//   out = O / d * v_scale  -> bf16
-// Differences from the sm89 kernel (covered by the tolerance tests): the running max is updated
-// per 128 keys instead of 64, P.V accumulates in fp32 rather than fp16 inside a tile, and exp2 is
-// the ex2.approx instruction for 3/4 of the keys and an FMA-pipe polynomial (relative error
-// < 7.5e-5) for the rest.
+// Semantics are those of SageAttention-2's `qk_int8_sv_f8_accum_f16_fuse_v_scale_attn_inst_buf` as
+// the reference calls it (lingbot/layers/sage_preq.py:126-127 with qk_quant_gran=2: one Q scale per
+// 32 rows; experiments/bench_attn/splitkv/README.md:51-69, h2_tiles/cfg_fusedsoftmax.patch:89-160),
+// with its tile size and fp32 arithmetic order. The keys run in 64-key tiles (Sage's CTA_K). For a
+// row with Q scale q_s and a tile with K scale k_s, S = q_i8 . k_i8 (exact int32), sm = fl(sm_scale
+// * log2 e), dq = fl(q_s * k_s):
+//   main tiles:        c = fl(sm * dq);  m_t = fma(max S, c, -8.807);  x = fma(S, c, -m)
+//   last two tiles:    r = fl(S * dq);   m_t = fma(max r, sm, -8.807); x = fma(r, sm, -m)
+//                      (upstream's last two iterations run on dequantized scores with
+//                      original_sm_scale, h2_tiles/cfg_fixedmax.patch:307,329)
+//   m = max(m_prev, m_t); alpha = exp2(m_prev - m); P = exp2(x) (<= 448) -> e4m3
+//   d = d * alpha + sum(P) (fp32, before rounding);  O = O * alpha + e4m3(P) . e4m3(V)
+//   out = O / d * v_scale -> bf16
+// exp2 is ex2.approx (upstream's ptx_exp2). The only difference from the sm89 kernel is that P.V
+// accumulates in fp32 in tensor memory where Sage sums each 64-key tile in fp16.
 //
-// CTA = two 128-row Q tiles (A, B) x one (batch, head) x one KV split. Warps: 0 = TMA producer,
-// 1 = tcgen05 issuer (one thread), 2..5 = softmax warpgroup A, 6..9 = softmax warpgroup B. Q row r
-// of a tile is TMEM lane r; one thread owns one row and all 128 keys of each key tile. While one
-// warpgroup computes its softmax the tensor core works for the other.
-// Tensor memory (512 columns): S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512) (fp32).
-// As soon as a warpgroup has read its scores it refills its S buffer with 0x4B400000, the bits of
-// the float 1.5*2^23, and the next Q.K^T accumulates onto it: the int32 accumulator then holds the
-// bits of the float 1.5*2^23 + S (|S| <= 128*127*127 < 2^22), so scores need no conversion. P is
-// written (e4m3, 128-byte-swizzled K-major rows) to a double-buffered shared-memory tile that the
-// P.V product reads as its A operand; the next Q.K^T therefore does not wait for P.V.
+// CTA = two 128-row Q tiles (A, B) x one (batch, head) x one KV split, 512 threads:
+//   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B: one thread per row (= TMEM lane);
+//   warps 8-11  correction: O_t *= alpha before each 64-key P.V, then the epilogue of both tiles;
+//   warp 12     TMA producer (both Q tiles once; K and V^T in 128-key stages through a ring);
+//   warp 13     tcgen05 issuer (one thread) and tensor-memory owner; warps 14-15 idle.
+// Q.K^T runs on 128 keys (one MMA of N = 128 per 32 channels); the softmax takes the two 64-key halves
+// of the score tile in turn, each against the running max after the previous half, and P.V runs per
+// half (K = 64), the correction warps rescaling O between the two products when the second half
+// raised a row's max. Tensor memory (512 columns): S_A [0,128), S_B [128,256) int32 scores, O_A
+// [256,384), O_B [384,512) fp32. After reading S_t a softmax warp refills it with 0x4B400000, the bits
+// of the float 1.5*2^23, and the next Q.K^T accumulates onto that: the int32 accumulator then holds the
+// bits of the float 1.5*2^23 + S (|S| <= 128*127*127 < 2^21), so S needs one exact subtraction and no
+// conversion. The refill completes during the first half's softmax, after which the Q.K^T of the next
+// key tile runs during the second half. P (e4m3) goes to a double-buffered shared-memory tile
+// (128-byte-swizzled K-major rows), the A operand of P.V; the issuer hands a P buffer back with its own
+// barrier, so Q.K^T may run ahead of the P.V products.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
@@ -37,16 +44,22 @@
 namespace lbq {
 
 constexpr int kStages = 3;
-constexpr int kTile = 128 * 128;         // bytes of one 128 x 128 8-bit tile
-constexpr int kAttnThreads = 64 + 256;   // producer, issuer, 2 softmax warpgroups
+constexpr int kTile = 128 * 128;         // bytes of a Q tile, a P tile and a 128-key K or V^T stage
+constexpr int kAttnThreads = 512;
 constexpr float kFp8Offset = 8.807f;     // splitkv/README.md:58 (S_FP8_OFFSET)
 constexpr float kMagic = 12582912.0f;    // 1.5 * 2^23
+constexpr uint32_t kMagicBits = 0x4B400000u;
+constexpr uint32_t kMaskedBits = 0x4B000000u;   // 1.5*2^23 - 2^22: below every real score
+constexpr uint32_t kColS = 0, kColO = 256;
+// Registers per thread after the split (launched with 128): softmax 160, correction 120, producer and
+// issuer warpgroup 72: 128 x (160 + 160 + 120 + 72) = 65536 = 512 x 128.
+constexpr uint32_t kRegSoftmax = 160, kRegCorrection = 120, kRegMisc = 72;
+static_assert(128 * (2 * kRegSoftmax + kRegCorrection + kRegMisc) <= kAttnThreads * 128, "register split");
 
 #ifndef LBQ_POLY_PAIRS
-#define LBQ_POLY_PAIRS 4
+#define LBQ_POLY_PAIRS 0
 #endif
-// Of every 16 key pairs, this many take the FMA-pipe polynomial exp2 and the rest MUFU ex2 (MUFU
-// issues one exp per 8 clocks per SM sub-partition; 4 of 16 measured best).
+// Of every 16 key pairs, this many take the FMA-pipe polynomial exp2 instead of MUFU ex2.
 constexpr int kPolyPairs = LBQ_POLY_PAIRS;
 
 struct AttnShared {
@@ -55,16 +68,24 @@ struct AttnShared {
   uint64_t k_empty[kStages];
   uint64_t v_full[kStages];
   uint64_t v_empty[kStages];
-  uint64_t s_full[2];                    // per Q tile
-  uint64_t s_free[2];
-  uint64_t p_full[2];
-  uint64_t o_done[2];
+  uint64_t s_full[2];                    // per Q tile: Q.K^T of the next 128-key tile complete
+  uint64_t s_free[2];                    // S read and refilled (128 softmax threads)
+  uint64_t p_full[2][2];                 // [tile][j & 1]: P of key tile j in shared memory, its alphas
+                                         // written (128 softmax threads); two per tile, since the softmax
+                                         // may run a key tile ahead of the correction
+  uint64_t p_free[2][2];                 // [tile][j & 1]: the P.V products of key tile j complete (commit):
+                                         // P buffer j & 1 and its alphas may be overwritten
+  uint64_t o_ready[2];                   // O_t rescaled for the next 64-key P.V (128 correction threads)
+  uint64_t o_done[2];                    // P.V complete
+  uint64_t ml_full[2];                   // final (m, d) of every row in `ml`
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
+  float alpha[2][2][2][128];             // [Q tile][j & 1][64-key half][row]
+  float2 ml[2][128];                     // [Q tile][row]
 };
 
-// smem: Q_A, Q_B | P_A[2], P_B[2] | K stages | V stages | barriers
+// smem: Q_A, Q_B | P_A[2], P_B[2] | K stages | V stages | AttnShared
 constexpr size_t kAttnSmemBytes = 1024 /*alignment slack*/ + kTile * (6 + 2 * kStages) + sizeof(AttnShared);
 
 __device__ int g_status;
@@ -75,102 +96,129 @@ __device__ __forceinline__ int seg_valid(const AttnArgs& a, int seg) {
   const int rest = a.kv_len - seg * a.seg_len;
   return rest < a.seg_len ? rest : a.seg_len;
 }
-// Key tile jt of the call's tile sequence -> (code segment, tile inside the segment).
-template <bool kKeyRange>
-__device__ __forceinline__ void tile_seg(const AttnArgs& a, int jt, int tiles_per_seg, int& seg, int& lt) {
-  if constexpr (kKeyRange) {
-    seg = jt >= a.range_tile0[1] ? 1 : 0;
-    lt = jt - a.range_tile0[seg] + a.range_lt0[seg];
-  } else {
-    seg = jt / tiles_per_seg;
-    lt = jt - seg * tiles_per_seg;
-  }
-}
 
-// Softmax of one 128-key tile for the calling thread's row. `sv` holds the scores as the bits of
-// 1.5*2^23 + S (see the tensor-memory note above). The e4m3 P is written to this row of the shared
-// P tile `prow` (128 bytes, 16-byte chunk c stored at chunk c ^ (row & 7): the 128-byte swizzle the
-// MMA descriptor expects) as it is produced; `m` and `dsum` are updated and the factor O must be
-// rescaled by, 2^(m_old - m_new), is returned. Keys 0..63 use K scale c1a, keys 64..127 use c1b.
-template <bool kMasked>
-__device__ __forceinline__ float softmax_tile(uint32_t (&sv)[4][32], int valid, float c1a, float c1b, float& m,
-                                              float& dsum, uint8_t* prow, int rsw) {
-  if (kMasked) {
-#pragma unroll
-    for (int c = 0; c < 128; ++c)
-      if (c >= valid) sv[c >> 5][c & 31] = 0x4B000000u;     // 1.5*2^23 - 2^22: below every real score
-  }
-  auto F = [&](int c) { return __uint_as_float(sv[c >> 5][c & 31]); };
-  float mh[2];
-#pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    const int b0 = half * 64;
-    float r0 = fmaxf(F(b0 + 0), F(b0 + 1)), r1 = fmaxf(F(b0 + 2), F(b0 + 3));
-    float r2 = fmaxf(F(b0 + 4), F(b0 + 5)), r3 = fmaxf(F(b0 + 6), F(b0 + 7));
-#pragma unroll
-    for (int c = b0 + 8; c < b0 + 64; c += 8) {
-      r0 = fmax3(r0, F(c + 0), F(c + 1));
-      r1 = fmax3(r1, F(c + 2), F(c + 3));
-      r2 = fmax3(r2, F(c + 4), F(c + 5));
-      r3 = fmax3(r3, F(c + 6), F(c + 7));
+// Walks the CTA's 128-key tiles in order, tracking (code segment, tile inside the segment) without a
+// division per step. Key-range mode: the tile sequence is the pieces of AttnArgs::range_*.
+template <bool kKeyRange>
+struct TileWalk {
+  int jt, seg, lt;
+  __device__ __forceinline__ TileWalk(const AttnArgs& a, int jt0, int tiles_per_seg) : jt(jt0) {
+    if constexpr (kKeyRange) {
+      seg = jt0 >= a.range_tile0[1] ? 1 : 0;
+      lt = jt0 - a.range_tile0[seg] + a.range_lt0[seg];
+    } else {
+      seg = jt0 / tiles_per_seg;
+      lt = jt0 - seg * tiles_per_seg;
     }
-    mh[half] = fmax3(r0, r1, fmaxf(r2, r3));
   }
-  // tile max in log2 units; (mh - magic) is the exact integer max. A half with no valid key is
-  // skipped (its block scale is the 1e-7 floor, so its stand-in score is not low enough).
-  float tmax = __fmul_rn(mh[0] - kMagic, c1a);
-  if (!kMasked || valid > 64) tmax = fmaxf(tmax, __fmul_rn(mh[1] - kMagic, c1b));
-  const float m_new = fmaxf(m, tmax);
+  __device__ __forceinline__ void next(const AttnArgs& a, int tiles_per_seg) {
+    ++jt;
+    if constexpr (kKeyRange) {
+      if (jt == a.range_tile0[1]) {
+        seg = 1;
+        lt = a.range_lt0[1];
+      } else {
+        ++lt;
+      }
+    } else if (++lt == tiles_per_seg) {
+      ++seg;
+      lt = 0;
+    }
+  }
+  // valid keys of this tile (1..128)
+  __device__ __forceinline__ int valid(const AttnArgs& a) const {
+    return min(128, seg_valid<kKeyRange>(a, seg) - lt * 128);
+  }
+};
+
+// Softmax of one 64-key tile for the calling thread's row. `sv` holds the scores as the bits of
+// 1.5*2^23 + S. Writes the e4m3 P of the 64 keys to `pw` (word w = keys 4w..4w+3, key 4w in the low
+// byte), updates `m` and `dsum`, returns alpha.
+template <bool kMasked, bool kTail>
+__device__ __forceinline__ float softmax_sub(uint32_t* sv, int valid, float c, float dq, float sm, float& m,
+                                             float& dsum, uint32_t (&pw)[16]) {
+  if constexpr (kMasked) {
+#pragma unroll
+    for (int j = 0; j < 64; ++j)
+      if (j >= valid) sv[j] = kMaskedBits;
+  }
+  auto F = [&](int j) { return __uint_as_float(sv[j]); };
+  float r0 = fmaxf(F(0), F(1)), r1 = fmaxf(F(2), F(3)), r2 = fmaxf(F(4), F(5)), r3 = fmaxf(F(6), F(7));
+#pragma unroll
+  for (int j = 8; j < 64; j += 8) {
+    r0 = fmax3(r0, F(j + 0), F(j + 1));
+    r1 = fmax3(r1, F(j + 2), F(j + 3));
+    r2 = fmax3(r2, F(j + 4), F(j + 5));
+    r3 = fmax3(r3, F(j + 6), F(j + 7));
+  }
+  const float smax = fmax3(r0, r1, fmaxf(r2, r3)) - kMagic;       // exact integer max score
+  const float m_t = kTail ? __fmaf_rn(__fmul_rn(smax, dq), sm, -kFp8Offset) : __fmaf_rn(smax, c, -kFp8Offset);
+  const float m_new = fmaxf(m, m_t);
   const float alpha = (m == m_new) ? 1.f : ex2_approx(m - m_new);
   m = m_new;
-  // x = (f - magic) * c1 + (8.807 - m) = f * c1 + c0, c0 = 8.807 - m - magic * c1 (one rounding; the
-  // argument is off by at most half an ulp of |c0|, about 6e-5 for typical scales)
-  const float c0a = fmaf(-kMagic, c1a, kFp8Offset - m_new);
-  const float c0b = fmaf(-kMagic, c1b, kFp8Offset - m_new);
-  const uint64_t c0ax2 = f2_pack(c0a, c0a), c0bx2 = f2_pack(c0b, c0b);
-  const uint64_t c1ax2 = f2_pack(c1a, c1a), c1bx2 = f2_pack(c1b, c1b);
+  const uint64_t negm2 = f2_pack(-m_new, -m_new), nk2 = f2_pack(-kMagic, -kMagic);
+  const uint64_t c2 = f2_pack(c, c), dq2 = f2_pack(dq, dq), sm2 = f2_pack(sm, sm);
   uint64_t acc0 = f2_pack(0.f, 0.f), acc1 = acc0;
-  uint32_t pw[4];
 #pragma unroll
-  for (int w = 0; w < 32; ++w) {
+  for (int w = 0; w < 16; ++w) {
     uint32_t half16[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      const int c = 4 * w + 2 * e;
-      const uint64_t x = f2_fma(f2_pack(F(c), F(c + 1)), c < 64 ? c1ax2 : c1bx2, c < 64 ? c0ax2 : c0bx2);
+      const int j = 4 * w + 2 * e;
+      const uint64_t s2 = f2_add(f2_pack(F(j), F(j + 1)), nk2);   // S, exact
+      const uint64_t x = kTail ? f2_fma(f2_mul(s2, dq2), sm2, negm2) : f2_fma(s2, c2, negm2);
       float x0, x1;
       f2_unpack(x, x0, x1);
       uint64_t p;
-      if (((c >> 1) & 15) >= 16 - kPolyPairs) {
+      if (((j >> 1) & 15) >= 16 - kPolyPairs) {
         p = exp2_poly_x2(x0, x1);
       } else {
         p = f2_pack(ex2_approx(x0), ex2_approx(x1));
       }
       float p0, p1;
       f2_unpack(p, p0, p1);
-      if (kMasked) {
-        if (c >= valid) p0 = 0.f;
-        if (c + 1 >= valid) p1 = 0.f;
+      if constexpr (kMasked) {
+        if (j >= valid) p0 = 0.f;
+        if (j + 1 >= valid) p1 = 0.f;
         p = f2_pack(p0, p1);
       }
       if (e == 0) acc0 = f2_add(acc0, p); else acc1 = f2_add(acc1, p);
       half16[e] = pack_e4m3x2(p0, p1);
     }
-    pw[w & 3] = half16[0] | (half16[1] << 16);
-    if ((w & 3) == 3)   // 16 keys done: one swizzled 16-byte chunk of the row
-      *reinterpret_cast<uint4*>(prow + (((w >> 2) ^ rsw) << 4)) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+    pw[w] = half16[0] | (half16[1] << 16);
   }
   float s0, s1, s2, s3;
   f2_unpack(acc0, s0, s1);
   f2_unpack(acc1, s2, s3);
-  dsum = __fmaf_rn(dsum, alpha, (s0 + s1) + (s2 + s3));
+  dsum = __fadd_rn(__fmul_rn(dsum, alpha), (s0 + s1) + (s2 + s3));
   return alpha;
 }
 
-// Key-range epilogue of one softmax warp: its 32 rows of O / row sum as fp16 (V-code units, |x| <= 448)
-// are staged in the tile's P buffers (free once O is complete; 16-byte chunks of a 256-byte row
-// XOR-swizzled by row) and stored to the owner rank's receive slot for this rank as whole rows, two
-// rows per warp instruction; the (max, sum) of each row follows. Rows past q_len are not stored.
+// One 64-key half of the softmax, dispatched on masking and upstream's tail arithmetic; the P words go
+// to chunks 4h..4h+3 of this row of the shared P tile (16-byte chunk c at c ^ (row & 7): the 128-byte
+// swizzle of the MMA operand).
+__device__ __forceinline__ float softmax_half(uint32_t* sv, int valid, bool tail, float c, float dq, float sm,
+                                              float& m, float& dsum, uint8_t* prow, int h, int rsw) {
+  uint32_t pw[16];
+  float alpha;
+  if (valid == 64) {
+    alpha = tail ? softmax_sub<false, true>(sv, 64, c, dq, sm, m, dsum, pw)
+                 : softmax_sub<false, false>(sv, 64, c, dq, sm, m, dsum, pw);
+  } else {
+    alpha = tail ? softmax_sub<true, true>(sv, valid, c, dq, sm, m, dsum, pw)
+                 : softmax_sub<true, false>(sv, valid, c, dq, sm, m, dsum, pw);
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    *reinterpret_cast<uint4*>(prow + (((4 * h + q) ^ rsw) << 4)) =
+        make_uint4(pw[4 * q], pw[4 * q + 1], pw[4 * q + 2], pw[4 * q + 3]);
+  return alpha;
+}
+
+// Key-range epilogue of one correction warp: its 32 rows of O / row sum as fp16 (V-code units, |x| <=
+// 448) are staged in `stage` (32 KB of free shared memory; 16-byte chunks of a 256-byte row XOR-swizzled
+// by row) and stored to the owner rank's receive slot for this rank as whole rows, two rows per warp
+// instruction; the (max, sum) of each row follows. Rows past q_len are not stored.
 __device__ __forceinline__ void store_key_partial(const AttnArgs& a, uint32_t tO, uint8_t* stage, int quarter,
                                                   int lane, int qtile, int bh, int bhs, float m, float dsum) {
   const float rd = __frcp_rn(dsum);
@@ -179,7 +227,7 @@ __device__ __forceinline__ void store_key_partial(const AttnArgs& a, uint32_t tO
   for (int c = 0; c < 4; ++c) {
     uint32_t ov[32];
     tmem_ld32(tO + 32 * c, ov);
-    tmem_ld_wait();
+    tmem_ld_wait(ov);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       uint32_t hw[4];
@@ -210,7 +258,32 @@ __device__ __forceinline__ void store_key_partial(const AttnArgs& a, uint32_t tO
   if (qrow0 + rl < a.q_len) reinterpret_cast<float2*>(dst + a.recv_ml_off)[slot + rl] = make_float2(m, dsum);
 }
 
-// 320 threads hold registers as 384 (whole warpgroups), so at one CTA per SM a thread gets <= 168.
+// O_t *= alpha for the calling warp's 32 TMEM lanes (two 64-column load/store round trips).
+__device__ __forceinline__ void rescale_o(uint32_t tO, float alpha) {
+  const uint64_t a2 = f2_pack(alpha, alpha);
+#pragma unroll 1
+  for (int c = 0; c < 4; c += 2) {
+    uint32_t ov[2][32];
+    tmem_ld32(tO + 32 * c, ov[0]);
+    tmem_ld32(tO + 32 * c + 32, ov[1]);
+    tmem_ld_wait(ov[0]);
+    reg_anchor(ov[1]);
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        float lo, hi;
+        f2_unpack(f2_mul(f2_pack(__uint_as_float(ov[h2][e]), __uint_as_float(ov[h2][e + 1])), a2), lo, hi);
+        ov[h2][e] = __float_as_uint(lo);
+        ov[h2][e + 1] = __float_as_uint(hi);
+      }
+    }
+    tmem_st32(tO + 32 * c, ov[0]);
+    tmem_st32(tO + 32 * c + 32, ov[1]);
+  }
+  tmem_st_wait();
+}
+
 // kKeyRange: the key-range split's variant (tile pieces of AttnArgs::range_*, partials to the query
 // tile's owner rank); false: the whole window in uniform segments.
 template <bool kKeyRange>
@@ -221,8 +294,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                              // [2][kTile]
   uint8_t* sP = smem + 2 * kTile;                  // [tile][buffer][kTile]
-  uint8_t* sK = smem + 6 * kTile;
-  uint8_t* sV = smem + kTile * (6 + kStages);
+  uint8_t* sK = smem + 6 * kTile;                  // [kStages][kTile]
+  uint8_t* sV = smem + kTile * (6 + kStages);      // [kStages][kTile]
   AttnShared* sh = reinterpret_cast<AttnShared*>(smem + kTile * (6 + 2 * kStages));
   volatile int* abort_flag = &sh->abort;
 
@@ -230,7 +303,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int b = bh / a.heads, h = bh - b * a.heads;
   const int t_begin = split * a.tiles_per_split;
   const int t_end = min(t_begin + a.tiles_per_split, a.total_tiles);
-  const int n = t_end - t_begin;
+  const int n = t_end - t_begin;                   // 128-key tiles of this CTA
   const int tiles_per_seg = a.seg_pad / 128;
   const int bhs = a.batch * a.heads;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -246,14 +319,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sh->s_full[t], 1);
       mbar_init(&sh->s_free[t], 128);
-      mbar_init(&sh->p_full[t], 128);
+      mbar_init(&sh->p_full[t][0], 128);
+      mbar_init(&sh->p_full[t][1], 128);
+      mbar_init(&sh->p_free[t][0], 1);
+      mbar_init(&sh->p_free[t][1], 1);
+      mbar_init(&sh->o_ready[t], 128);
       mbar_init(&sh->o_done[t], 1);
+      mbar_init(&sh->ml_full[t], 128);
     }
     mbar_init(&sh->drain, 1);
     sh->abort = 0;
     fence_mbar_init();
   }
-  if (warp == 1) {
+  if (warp == 13) {
     tmem_alloc(&sh->tmem_base, 512);
     tmem_relinquish();
   }
@@ -262,9 +340,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0 && n > 0) {
+  if (warp >= 12) {
+    reg_dealloc<kRegMisc>();
+    if (warp == 12 && lane == 0 && n > 0) {
+      // ---------------------------------------------------------- TMA producer
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
@@ -272,231 +351,281 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_arrive_expect_tx(&sh->q_full, 2 * kTile);
       tma_load_3d(sQ, &tm_q, &sh->q_full, 0, (2 * qp) * 128, bh);
       tma_load_3d(sQ + kTile, &tm_q, &sh->q_full, 0, (2 * qp + 1) * 128, bh);
-      int issued = 0;
-      for (int i = 0; i < n; ++i) {
-        const int jt = t_begin + i;
-        int seg, lt;
-        tile_seg<kKeyRange>(a, jt, tiles_per_seg, seg, lt);
-        (void)LBQ_CHECK(seg < a.nseg && lt >= 0 && lt < tiles_per_seg, a.status, kDevBadTile);
+      int k_issued = 0, v_issued = 0;
+      TileWalk<kKeyRange> tw(a, t_begin, tiles_per_seg);
+      for (int i = 0; i < n; ++i, tw.next(a, tiles_per_seg)) {
+        (void)LBQ_CHECK(tw.seg < a.nseg && tw.lt >= 0 && tw.lt < tiles_per_seg, a.status, kDevBadTile);
         const int s = i % kStages;
         const uint32_t ph = (i / kStages) & 1;
         if (!mbar_wait(&sh->k_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) break;
         mbar_arrive_expect_tx(&sh->k_full[s], kTile);
-        tma_load_3d(sK + s * kTile, &tm_k, &sh->k_full[s], 0, lt * 128, seg * bhs + bh);
-        if (!mbar_wait(&sh->v_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) {
-          issued = i + 1;
-          break;
-        }
+        tma_load_3d(sK + s * kTile, &tm_k, &sh->k_full[s], 0, tw.lt * 128, tw.seg * bhs + bh);
+        k_issued = i + 1;
+        if (!mbar_wait(&sh->v_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) break;
         mbar_arrive_expect_tx(&sh->v_full[s], kTile);
-        tma_load_3d(sV + s * kTile, &tm_v, &sh->v_full[s], lt * 128, 0, seg * bhs + bh);
-        issued = i + 1;
+        tma_load_3d(sV + s * kTile, &tm_v, &sh->v_full[s], tw.lt * 128, 0, tw.seg * bhs + bh);
+        v_issued = i + 1;
       }
       if (*abort_flag) {
         // Let copies already in flight land before the CTA's shared memory goes away.
         mbar_drain_wait(&sh->q_full, 0);
-        for (int i = (issued > kStages ? issued - kStages : 0); i < issued; ++i) {
-          const int s = i % kStages;
-          const uint32_t ph = (i / kStages) & 1;
-          mbar_drain_wait(&sh->k_full[s], ph);
-          mbar_drain_wait(&sh->v_full[s], ph);
-        }
+        for (int i = (k_issued > kStages ? k_issued - kStages : 0); i < k_issued; ++i)
+          mbar_drain_wait(&sh->k_full[i % kStages], (i / kStages) & 1);
+        for (int i = (v_issued > kStages ? v_issued - kStages : 0); i < v_issued; ++i)
+          mbar_drain_wait(&sh->v_full[i % kStages], (i / kStages) & 1);
       }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ tcgen05 issuer
-    if (lane == 0 && n > 0) {
+    } else if (warp == 13 && lane == 0 && n > 0) {
+      // ---------------------------------------------------------- tcgen05 issuer
       bool ok = mbar_wait(&sh->q_full, 0, abort_flag, a.status, kDevTimeoutQ);
       tc_fence_after();
       const uint64_t qdesc[2] = {smem_desc_sw128(smem_u32(sQ)), smem_desc_sw128(smem_u32(sQ + kTile))};
-      // S_t += Q_t . K(i)^T, onto the magic constant the softmax left in S_t
-      auto issue_qk = [&](int t, int i) {
-        const uint64_t kdesc = smem_desc_sw128(smem_u32(sK + (i % kStages) * kTile));
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) mma_i8_ss(tmem + 128 * t, qdesc[t] + 2 * kk, kdesc + 2 * kk, kIdescQK, 1u);
-        tc_commit(&sh->s_full[t]);
-      };
-      auto issue_pv = [&](int t, int j) {
-        const uint64_t pdesc = smem_desc_sw128(smem_u32(sP + (2 * t + (j & 1)) * kTile));
-        const uint64_t vdesc = smem_desc_sw128(smem_u32(sV + (j % kStages) * kTile));
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_f8_ss(tmem + 256 + 128 * t, pdesc + 2 * kk, vdesc + 2 * kk, kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&sh->o_done[t]);
-      };
-      if (ok && (ok = mbar_wait(&sh->k_full[0], 0, abort_flag, a.status, kDevTimeoutKV))) {
-        for (int t = 0; ok && t < 2; ++t) {
-          ok = mbar_wait(&sh->s_free[t], 0, abort_flag, a.status, kDevTimeoutS);   // S_t initialised
+      const uint64_t kdesc0 = smem_desc_sw128(smem_u32(sK)), vdesc0 = smem_desc_sw128(smem_u32(sV));
+      const uint64_t pdesc0 = smem_desc_sw128(smem_u32(sP));
+      constexpr uint64_t kTileDesc = kTile >> 4;        // one tile in descriptor address units
+      int ks = 0, kph = 0;                              // K stage of the next Q.K^T and its phase bit
+      // S_t += Q_t . K(next stage)^T for both tiles once S_t(k - 1) was read and refilled (k: the key
+      // tile, k - 1 < 0 meaning the initial fill), onto the magic constant the softmax left in S_t
+      auto issue_qk = [&](int k) {
+        if (!(ok = mbar_wait(&sh->k_full[ks], kph, abort_flag, a.status, kDevTimeoutKV))) return;
+        const uint64_t kdesc = kdesc0 + ks * kTileDesc;
+        for (int t = 0; t < 2; ++t) {
+          if (!(ok = mbar_wait(&sh->s_free[t], k & 1, abort_flag, a.status, kDevTimeoutS))) return;
           tc_fence_after();
-          if (ok) issue_qk(t, 0);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_i8_ss(tmem + kColS + 128 * t, qdesc[t] + 2 * kk, kdesc + 2 * kk, kIdescQK, 1u);
+          tc_commit(&sh->s_full[t]);
         }
-        if (ok) tc_commit(&sh->k_empty[0]);
-      }
+        tc_commit(&sh->k_empty[ks]);
+        if (++ks == kStages) {
+          ks = 0;
+          kph ^= 1;
+        }
+      };
+      // Order per key tile j: P.V of its first half, Q.K^T of tile j + 2 (S_t was read by the softmax of
+      // tile j + 1), P.V of its second half. The scores of tile j + 2 are then ready long before the
+      // softmax gets to them.
+      TileWalk<kKeyRange> tw(a, t_begin, tiles_per_seg);
+      int ns = tw.valid(a) > 64 ? 2 : 1;               // 64-key halves of tile j
+      int vs = 0, vph = 0;                              // V stage of tile j and its phase bit
+      int u = 0;                                        // P.V products issued per Q tile
+      for (int k = 0; ok && k < 2 && k < n; ++k) issue_qk(k);
       for (int j = 0; ok && j < n; ++j) {
-        const int s = j % kStages;
-        const bool more = j + 1 < n;
-        if (more && !mbar_wait(&sh->k_full[(j + 1) % kStages], ((j + 1) / kStages) & 1, abort_flag, a.status,
-                               kDevTimeoutKV))
-          break;
-        if (!mbar_wait(&sh->v_full[s], (j / kStages) & 1, abort_flag, a.status, kDevTimeoutKV)) break;
-        for (int t = 0; ok && t < 2; ++t) {
-          if (more) {            // S_t(j) read and refilled -> next scores
-            if (!(ok = mbar_wait(&sh->s_free[t], (j + 1) & 1, abort_flag, a.status, kDevTimeoutS))) break;
-            tc_fence_after();
-            issue_qk(t, j + 1);
+        if (!(ok = mbar_wait(&sh->v_full[vs], vph, abort_flag, a.status, kDevTimeoutKV))) break;
+        const uint64_t vdesc = vdesc0 + vs * kTileDesc;
+        for (int hh = 0; ok && hh < ns; ++hh, ++u) {
+          if (hh == 1 && j + 2 < n) {
+            issue_qk(j + 2);
+            if (!ok) break;
           }
-          if (!(ok = mbar_wait(&sh->p_full[t], j & 1, abort_flag, a.status, kDevTimeoutP))) break;
-          tc_fence_after();
-          issue_pv(t, j);
+          for (int t = 0; t < 2; ++t) {                 // P_t(j, hh) written, O_t rescaled -> O_t += P V
+            if (!(ok = mbar_wait(&sh->o_ready[t], u & 1, abort_flag, a.status, kDevTimeoutP))) break;
+            tc_fence_after();
+            const uint64_t pdesc = pdesc0 + (2 * t + (j & 1)) * kTileDesc + 4 * hh;
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk)
+              mma_f8_ss(tmem + kColO + 128 * t, pdesc + 2 * kk, vdesc + 4 * hh + 2 * kk, kIdescPV,
+                        (u > 0 || kk > 0) ? 1u : 0u);
+            tc_commit(&sh->o_done[t]);
+          }
         }
         if (!ok) break;
-        tc_commit(&sh->v_empty[s]);
-        if (more) tc_commit(&sh->k_empty[(j + 1) % kStages]);
+        if (ns == 1 && j + 2 < n) {                     // a one-half tile: Q.K^T of tile j + 2 after its P.V
+          issue_qk(j + 2);
+          if (!ok) break;
+        }
+        tc_commit(&sh->v_empty[vs]);
+        for (int t = 0; t < 2; ++t) tc_commit(&sh->p_free[t][j & 1]);
+        if (++vs == kStages) {
+          vs = 0;
+          vph ^= 1;
+        }
+        if (j + 1 < n) {
+          tw.next(a, tiles_per_seg);
+          ns = tw.valid(a) > 64 ? 2 : 1;
+        }
       }
       // Drain: every MMA issued above has completed once `drain` flips.
       tc_commit(&sh->drain);
       mbar_drain_wait(&sh->drain, 0);
     }
-  } else {
+  } else if (warp < 8) {
     // ------------------------------------------------------------ softmax warpgroups
-    const int t = (warp - 2) >> 2;                      // Q tile of this warpgroup
+    reg_alloc<kRegSoftmax>();
+    const int t = warp >> 2;                            // Q tile of this warpgroup
     const int quarter = warp & 3;                       // TMEM lanes [32*quarter, 32*quarter+32)
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
-    const uint32_t tS = tmem + 128 * t + lane_off, tO = tmem + 256 + 128 * t + lane_off;
+    const uint32_t tS = tmem + kColS + 128 * t + lane_off;
     const int qtile = 2 * qp + t;
-    const int row = qtile * 128 + quarter * 32 + lane;
+    const int rl = quarter * 32 + lane;
     const float qs = qtile * 128 < a.q_pad ? a.q_scale[int64_t(bh) * (a.q_pad / 32) + qtile * 4 + quarter] : 0.f;
+    const float sm = a.sm_log2;
     const int kspb = a.seg_pad / 64;
-    auto kscale_ptr = [&](int i) {
-      const int jt = t_begin + i;
-      int seg, lt;
-      tile_seg<kKeyRange>(a, jt, tiles_per_seg, seg, lt);
+    const int prow_off = rl * 128;
+    const int rsw = lane & 7;                           // row & 7 (rows of a warp start at 32k)
+    float m = -INFINITY, dsum = 0.f;
+    bool ok = n > 0;
+    TileWalk<kKeyRange> tw(a, t_begin, tiles_per_seg);
+    auto kscale_ptr = [&](const TileWalk<kKeyRange>& w) {
+      int seg = w.seg, lt = w.lt;
       if (!LBQ_CHECK(seg < a.nseg && lt >= 0 && lt * 2 + 1 < kspb, a.status, kDevBadTile)) seg = lt = 0;
       return a.k_scale + int64_t(seg * bhs + bh) * kspb + lt * 2;
     };
-    float m = -INFINITY, dsum = 0.f;
-    bool ok = n > 0;
-    const int prow_off = (quarter * 32 + lane) * 128;
-    const int rsw = lane & 7;                               // row & 7 (rows of a warp start at 32k)
+    // the last two 64-key tiles take upstream's tail arithmetic
+    int ns_last = 0;
+    if (ok) {
+      TileWalk<kKeyRange> tl(a, t_end - 1, tiles_per_seg);
+      ns_last = tl.valid(a) > 64 ? 2 : 1;
+    }
     // S_t starts as the magic constant (the first Q.K^T accumulates onto it)
 #pragma unroll
-    for (int c = 0; c < 16; ++c) tmem_fill8(tS + 8 * c, 0x4B400000u);
+    for (int c = 0; c < 16; ++c) tmem_fill8(tS + 8 * c, kMagicBits);
     tmem_st_wait();
     tc_fence_before();
     mbar_arrive(&sh->s_free[t]);
-    float2 ks_next = ok ? *reinterpret_cast<const float2*>(kscale_ptr(0)) : make_float2(0.f, 0.f);
-    for (int i = 0; ok && i < n; ++i) {
-      const int jt = t_begin + i;
-      int seg, lt;
-      tile_seg<kKeyRange>(a, jt, tiles_per_seg, seg, lt);
-      const int valid = min(128, seg_valid<kKeyRange>(a, seg) - lt * 128);
+    float2 ks_next = ok ? *reinterpret_cast<const float2*>(kscale_ptr(tw)) : make_float2(0.f, 0.f);
+    for (int j = 0; ok && j < n; ++j) {
+      const int tv = tw.valid(a);
       const float2 ks = ks_next;
-      if (i + 1 < n) ks_next = *reinterpret_cast<const float2*>(kscale_ptr(i + 1));   // prefetch
-      const float c1a = __fmul_rn(__fmul_rn(qs, ks.x), a.sm_log2);
-      const float c1b = __fmul_rn(__fmul_rn(qs, ks.y), a.sm_log2);
-      if (!mbar_wait(&sh->s_full[t], i & 1, abort_flag, a.status, kDevTimeoutS)) {
+      if (j + 1 < n) {                                  // prefetch the next tile's K scales
+        tw.next(a, tiles_per_seg);
+        ks_next = *reinterpret_cast<const float2*>(kscale_ptr(tw));
+      }
+      if (!mbar_wait(&sh->s_full[t], j & 1, abort_flag, a.status, kDevTimeoutS)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t sv[4][32];
-      tmem_ld32(tS + 0, sv[0]);
-      tmem_ld32(tS + 32, sv[1]);
-      tmem_ld32(tS + 64, sv[2]);
-      tmem_ld32(tS + 96, sv[3]);
-      tmem_ld_wait();
-      // refill S_t with the magic constant and let the next Q.K^T go
+      uint32_t sv[128];
+      auto& sv0 = *reinterpret_cast<uint32_t(*)[32]>(sv);
+      auto& sv1 = *reinterpret_cast<uint32_t(*)[32]>(sv + 32);
+      auto& sv2 = *reinterpret_cast<uint32_t(*)[32]>(sv + 64);
+      auto& sv3 = *reinterpret_cast<uint32_t(*)[32]>(sv + 96);
+      tmem_ld32(tS + 0, sv0);
+      tmem_ld32(tS + 32, sv1);
+      tmem_ld32(tS + 64, sv2);
+      tmem_ld32(tS + 96, sv3);
+      tmem_ld_wait(sv0);
+      reg_anchor(sv1);
+      reg_anchor(sv2);
+      reg_anchor(sv3);
+      // refill S_t with the magic constant; its stores complete during the first half's softmax
 #pragma unroll
-      for (int c = 0; c < 16; ++c) tmem_fill8(tS + 8 * c, 0x4B400000u);
+      for (int c = 0; c < 16; ++c) tmem_fill8(tS + 8 * c, kMagicBits);
+      // P_t[j & 1] and its alphas were last read for tile j - 2
+      if (j >= 2 && !mbar_wait(&sh->p_free[t][j & 1], ((j - 2) >> 1) & 1, abort_flag, a.status, kDevTimeoutO)) {
+        ok = false;
+        break;
+      }
+      uint8_t* prow = sP + (2 * t + (j & 1)) * kTile + prow_off;
+      const bool last1 = j == n - 1, prev1 = j == n - 2 && ns_last == 1;
+      {
+        const float dq = __fmul_rn(qs, ks.x);
+        const float alpha = softmax_half(sv, min(64, tv), last1 || (prev1 && tv <= 64), __fmul_rn(sm, dq), dq, sm,
+                                         m, dsum, prow, 0, rsw);
+        sh->alpha[t][j & 1][0][rl] = alpha;
+      }
+      // S_t refilled: the Q.K^T of tile j + 1 may go (it runs during the second half)
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&sh->s_free[t]);
-      // P_t[i & 1] was last read by P.V of tile i - 2, complete since the o_done wait of tile i - 1
-      uint8_t* prow = sP + (2 * t + (i & 1)) * kTile + prow_off;
-      const float alpha = valid == 128 ? softmax_tile<false>(sv, 128, c1a, c1b, m, dsum, prow, rsw)
-                                       : softmax_tile<true>(sv, valid, c1a, c1b, m, dsum, prow, rsw);
+      if (tv > 64) {
+        const float dq = __fmul_rn(qs, ks.y);
+        const float alpha = softmax_half(sv + 64, tv - 64, last1 || prev1, __fmul_rn(sm, dq), dq, sm, m, dsum, prow,
+                                         1, rsw);
+        sh->alpha[t][j & 1][1][rl] = alpha;
+      }
       fence_proxy_async_smem();
-      if (i > 0) {
-        if (!mbar_wait(&sh->o_done[t], (i - 1) & 1, abort_flag, a.status, kDevTimeoutO)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
-          const uint64_t a2 = f2_pack(alpha, alpha);
-#pragma unroll 1
-          for (int c = 0; c < 4; c += 2) {     // two 32-column chunks per load/store round trip
-            uint32_t ov[2][32];
-            tmem_ld32(tO + 32 * c, ov[0]);
-            tmem_ld32(tO + 32 * c + 32, ov[1]);
-            tmem_ld_wait();
-#pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2) {
-#pragma unroll
-              for (int e = 0; e < 32; e += 2) {
-                float lo, hi;
-                f2_unpack(f2_mul(f2_pack(__uint_as_float(ov[h2][e]), __uint_as_float(ov[h2][e + 1])), a2), lo, hi);
-                ov[h2][e] = __float_as_uint(lo);
-                ov[h2][e + 1] = __float_as_uint(hi);
-              }
-            }
-            tmem_st32(tO + 32 * c, ov[0]);
-            tmem_st32(tO + 32 * c + 32, ov[1]);
-          }
-          tmem_st_wait();
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&sh->p_full[t]);
+      mbar_arrive(&sh->p_full[t][j & 1]);
     }
-    const bool o_ready = ok && mbar_wait(&sh->o_done[t], (n - 1) & 1, abort_flag, a.status, kDevTimeoutO);
-    if constexpr (kKeyRange) {
-      // warp-uniform: tcgen05.ld is a whole-warp instruction
-      if (__all_sync(0xffffffffu, o_ready) && qtile * 128 < a.q_len) {
-        tc_fence_after();
-        store_key_partial(a, tO, sP + 2 * t * kTile, quarter, lane, qtile, bh, bhs, m, dsum);
+    if (ok) {
+      sh->ml[t][rl] = make_float2(m, dsum);
+      mbar_arrive(&sh->ml_full[t]);
+    }
+  } else {
+    // ------------------------------------------------------------ correction + epilogue
+    reg_dealloc<kRegCorrection>();
+    const int quarter = warp & 3;
+    const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+    const int rl = quarter * 32 + lane;
+    bool ok = n > 0;
+    int u = 0;
+    TileWalk<kKeyRange> tw(a, t_begin, tiles_per_seg);
+    for (int j = 0; ok && j < n; ++j, tw.next(a, tiles_per_seg)) {
+      const int ns = tw.valid(a) > 64 ? 2 : 1;
+      for (int hh = 0; ok && hh < ns; ++hh, ++u) {
+        for (int t = 0; t < 2; ++t) {
+          if (hh == 0 &&
+              !(ok = mbar_wait(&sh->p_full[t][j & 1], (j >> 1) & 1, abort_flag, a.status, kDevTimeoutP)))
+            break;
+          if (u > 0) {
+            if (!(ok = mbar_wait(&sh->o_done[t], (u - 1) & 1, abort_flag, a.status, kDevTimeoutO))) break;
+            tc_fence_after();
+            const float alpha = sh->alpha[t][j & 1][hh][rl];
+            if (__any_sync(0xffffffffu, alpha != 1.f)) rescale_o(tmem + kColO + 128 * t + lane_off, alpha);
+          }
+          tc_fence_before();
+          mbar_arrive(&sh->o_ready[t]);
+        }
       }
-    } else if (o_ready) {
-      tc_fence_after();
-      if (a.num_splits == 1) {
-        const float rd = __frcp_rn(dsum);
-        const float* vs = a.v_scale + int64_t(bh) * 128;
-        __nv_bfloat16* dst = a.out + b * a.so_b + int64_t(row) * a.so_l + h * a.so_h;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t ov[32];
-          tmem_ld32(tO + 32 * c, ov);
-          tmem_ld_wait();
-          uint32_t packed[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float o0 = __fmul_rn(__fmul_rn(__uint_as_float(ov[2 * e]), rd), vs[32 * c + 2 * e]);
-            const float o1 = __fmul_rn(__fmul_rn(__uint_as_float(ov[2 * e + 1]), rd), vs[32 * c + 2 * e + 1]);
-            const __nv_bfloat162 pr = __floats2bfloat162_rn(o0, o1);
-            packed[e] = *reinterpret_cast<const uint32_t*>(&pr);
-          }
-          if (row < a.q_len) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              reinterpret_cast<uint4*>(dst + 32 * c)[e] =
-                  make_uint4(packed[4 * e], packed[4 * e + 1], packed[4 * e + 2], packed[4 * e + 3]);
-          }
+    }
+    for (int t = 0; t < 2; ++t) {
+      const uint32_t tO = tmem + kColO + 128 * t + lane_off;
+      const int qtile = 2 * qp + t;
+      const int row = qtile * 128 + rl;
+      const bool o_ready = ok && mbar_wait(&sh->o_done[t], (u - 1) & 1, abort_flag, a.status, kDevTimeoutO) &&
+                           mbar_wait(&sh->ml_full[t], 0, abort_flag, a.status, kDevTimeoutO);
+      if (!o_ready) ok = false;
+      const float2 ml = o_ready ? sh->ml[t][rl] : make_float2(0.f, 1.f);
+      if constexpr (kKeyRange) {
+        // warp-uniform: tcgen05.ld is a whole-warp instruction
+        if (__all_sync(0xffffffffu, o_ready) && qtile * 128 < a.q_len) {
+          tc_fence_after();
+          store_key_partial(a, tO, sP + 2 * t * kTile, quarter, lane, qtile, bh, bhs, ml.x, ml.y);
         }
-      } else {
-        const int64_t prow = (int64_t(split) * bhs + bh) * a.q_pad + row;
-        float* dst = a.o_part + prow * 128;
+      } else if (__all_sync(0xffffffffu, o_ready)) {
+        tc_fence_after();
+        if (a.num_splits == 1) {
+          const float rd = __frcp_rn(ml.y);
+          const float* vs = a.v_scale + int64_t(bh) * 128;
+          __nv_bfloat16* dst = a.out + b * a.so_b + int64_t(row) * a.so_l + h * a.so_h;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t ov[32];
-          tmem_ld32(tO + 32 * c, ov);
-          tmem_ld_wait();
-          if (row < a.q_len) {
+          for (int c = 0; c < 4; ++c) {
+            uint32_t ov[32];
+            tmem_ld32(tO + 32 * c, ov);
+            tmem_ld_wait(ov);
+            uint32_t packed[16];
 #pragma unroll
-            for (int e = 0; e < 8; ++e)
-              reinterpret_cast<uint4*>(dst + 32 * c)[e] =
-                  make_uint4(ov[4 * e], ov[4 * e + 1], ov[4 * e + 2], ov[4 * e + 3]);
+            for (int e = 0; e < 16; ++e) {
+              const float o0 = __fmul_rn(__fmul_rn(__uint_as_float(ov[2 * e]), rd), vs[32 * c + 2 * e]);
+              const float o1 = __fmul_rn(__fmul_rn(__uint_as_float(ov[2 * e + 1]), rd), vs[32 * c + 2 * e + 1]);
+              const __nv_bfloat162 pr = __floats2bfloat162_rn(o0, o1);
+              packed[e] = *reinterpret_cast<const uint32_t*>(&pr);
+            }
+            if (row < a.q_len) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                reinterpret_cast<uint4*>(dst + 32 * c)[e] =
+                    make_uint4(packed[4 * e], packed[4 * e + 1], packed[4 * e + 2], packed[4 * e + 3]);
+            }
           }
+        } else {
+          const int64_t prow = (int64_t(split) * bhs + bh) * a.q_pad + row;
+          float* dst = a.o_part + prow * 128;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t ov[32];
+            tmem_ld32(tO + 32 * c, ov);
+            tmem_ld_wait(ov);
+            if (row < a.q_len) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e)
+                reinterpret_cast<uint4*>(dst + 32 * c)[e] =
+                    make_uint4(ov[4 * e], ov[4 * e + 1], ov[4 * e + 2], ov[4 * e + 3]);
+            }
+          }
+          if (row < a.q_len) a.ml_part[prow] = ml;
         }
-        if (row < a.q_len) a.ml_part[prow] = make_float2(m, dsum);
       }
     }
   }
@@ -504,7 +633,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, 512);
+  if (warp == 13) tmem_dealloc(tmem, 512);
   // the owners of the query tiles may read this rank's partials once every CTA has stored them
   if constexpr (kKeyRange) signal_after_last_cta(a.peers, a.nranks, a.rank, a.xchg_off, xchg::kDoneAttn);
 }

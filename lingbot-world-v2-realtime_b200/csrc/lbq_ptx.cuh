@@ -69,17 +69,30 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                "r"(bytes)
                : "memory");
 }
-// Waits (suspended, not spinning) until the phase with `parity` completes or the suspend-time hint
-// (1 ms) runs out; returns whether the phase completed.
+#ifndef LBQ_TRY_WAIT_HINT_NS
+#define LBQ_TRY_WAIT_HINT_NS 0
+#endif
+// Waits until the phase with `parity` completes or the instruction's own time limit runs out (with
+// LBQ_TRY_WAIT_HINT_NS > 0: a suspend-time hint of that many ns); returns whether the phase completed.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
+#if LBQ_TRY_WAIT_HINT_NS > 0
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(uint32_t(LBQ_TRY_WAIT_HINT_NS))
       : "memory");
+#else
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+#endif
   return ok != 0;
 }
 __device__ __forceinline__ uint64_t globaltimer_ns() {
@@ -158,7 +171,8 @@ __device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-// D[tmem] (+)= A[tmem] * B[smem]^T, e4m3 x e4m3 -> fp32.
+// D[tmem] (+)= A[tmem] * B[smem]^T, e4m3 x e4m3 -> fp32. A (M x K, K-major) is read from tensor
+// memory: row r in lane r, four consecutive K elements per 32-bit column, the lowest K in the low byte.
 __device__ __forceinline__ void mma_f8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                           uint32_t accumulate) {
   asm volatile(
@@ -196,14 +210,14 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
   return d;
 }
 
-// Instruction descriptors (M=128, N=128, both operands K-major, dense).
+// Instruction descriptors (M=128, both operands K-major, dense).
 //   [4,6) D format (1 = f32, 2 = s32), [7,10) A format, [10,13) B format,
 //   [17,23) N>>3, [24,29) M>>4.
-constexpr uint32_t idesc_m128_n128(uint32_t dfmt, uint32_t afmt, uint32_t bfmt) {
-  return (dfmt << 4) | (afmt << 7) | (bfmt << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t idesc_m128(uint32_t n, uint32_t dfmt, uint32_t afmt, uint32_t bfmt) {
+  return (dfmt << 4) | (afmt << 7) | (bfmt << 10) | ((n >> 3) << 17) | ((128u >> 4) << 24);
 }
-constexpr uint32_t kIdescQK = idesc_m128_n128(2, 1, 1);  // s32 <- s8 x s8
-constexpr uint32_t kIdescPV = idesc_m128_n128(1, 0, 0);  // f32 <- e4m3 x e4m3
+constexpr uint32_t kIdescQK = idesc_m128(128, 2, 1, 1);   // s32 <- s8 x s8, N = 128 keys
+constexpr uint32_t kIdescPV = idesc_m128(128, 1, 0, 0);   // f32 <- e4m3 x e4m3, N = 128 channels
 
 // Warp-collective TMEM load: thread i of the warp reads lane (lane_base + i), 32 consecutive
 // 32-bit columns starting at the column in `taddr`.
@@ -219,6 +233,29 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Waits for this thread's TMEM loads and ties the 32 destination registers to the wait, so that the
+// compiler cannot move a use of them above it.
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+        "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+        "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+        "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+      :
+      : "memory");
+}
+// No instruction: orders the 32 registers after the preceding volatile asm (a second tmem_ld_wait).
+__device__ __forceinline__ void reg_anchor(uint32_t (&r)[32]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
 
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
@@ -255,6 +292,19 @@ __device__ __forceinline__ void tmem_fill8(uint32_t taddr, uint32_t v) {
                : "memory");
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------- register reallocation
+// Every warp of a warpgroup executes the same setmaxnreg. The per-thread counts of all warpgroups of a
+// CTA must add up to at most what the CTA was launched with (threads x registers at launch), or an
+// increase waits forever.
+template <uint32_t N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
 
 // ---------------------------------------------------------------- numerics
 __device__ __forceinline__ float ex2_approx(float x) {

@@ -125,7 +125,7 @@ def quantize_qkv(q, k, v):
 
 def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_scale=None,
                     pv_accum="fp16", rows=None, heads=None, splits=1, key_ranges=None,
-                    partial_fp16=False):
+                    partial_fp16=False, ambiguous=None):
     """Torch emulation of Sage's `qk_int8_sv_f8_accum_f16_fuse_v_scale_attn_inst_buf` (the call at
     sage_preq.py:126-127 / sage_kvq.py:107-110), non-causal, per-warp Q granularity, with the kernel's
     own fp32 arithmetic order.
@@ -161,12 +161,17 @@ def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_sca
     order with one running max (its memory tiles, then its chunk share). With `partial_fp16` each
     partial travels as fp16(O_s / d_s) with (m_s, d_s), and the merge is
     out = sum_s w_s fp16(O_s / d_s) / sum_s w_s with w_s = 2^(m_s - M) d_s.
+    With `ambiguous` (a bool tensor [B, Lq, H], set in place), a row is marked when one of its P lies
+    within EXP2_REL_ERR (relative) of an e4m3 rounding midpoint and a one-step flip of that P could move
+    the row's output by more than AMBIGUOUS_IMPACT: the e4m3 value then depends on the last bits of the
+    exp2 implementation (ex2.approx on the GPU, a correctly rounded exp2 here).
     """
     b, lq, h, d = q_codes.shape
     lk = k_codes.shape[1]
     if sm_scale is None:
         sm_scale = d ** -0.5
-    sm_log2 = torch.tensor(sm_scale * LOG2E, dtype=torch.float32)
+    # fl(fl(sm_scale) * fl(log2 e)): the fp32 product the kernel forms from its float argument
+    sm_log2 = torch.tensor(sm_scale, dtype=torch.float32) * torch.tensor(LOG2E, dtype=torch.float32)
     rows = torch.arange(lq) if rows is None else torch.as_tensor(rows)
     heads = range(h) if heads is None else heads
     out = torch.zeros(b, lq, h, d, dtype=torch.float32)
@@ -187,9 +192,13 @@ def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_sca
             for pieces in partials:
                 tiles = [(t0, min(t0 + BLK_K, hi_)) for lo, hi_ in pieces for t0 in range(lo, hi_, BLK_K)]
                 state = None
+                amb = None if ambiguous is None else torch.zeros(qf.shape[0], dtype=torch.bool)
+                vmax = float(v_scale[bi, hi].max()) * V_SCALE_MAX          # largest |V| in output units
                 for i, (t0, t1) in enumerate(tiles):
                     state = _attn_tile(qf, qs, kf, vf, k_scale[bi, hi][t0 // BLK_K], t0, t1, pv_accum, sm_log2,
-                                       state, tail=i >= len(tiles) - 2)
+                                       state, tail=i >= len(tiles) - 2, amb=amb, vmax=vmax)
+                if amb is not None:
+                    ambiguous[bi, rows, hi] |= amb
                 parts.append(state)
             mx = torch.stack([p[0] for p in parts]).max(dim=0).values
             acc = torch.zeros(qf.shape[0], d)
@@ -211,7 +220,26 @@ def _fma32(a, b, c):
     return (a.double() * b.double() + c.double()).float()
 
 
-def _attn_tile(qf, qs, kf, vf, ks, t0, t1, pv_accum, sm_log2, state, tail):
+# ex2.approx.ftz.f32's relative error is about 2^-22 (2 ulp); a P within 2^-20 of an e4m3 rounding
+# midpoint (a margin of 4x) may round either way on the GPU. Such a P makes its row ambiguous when a
+# one-step flip of it could move an output by more than AMBIGUOUS_IMPACT.
+EXP2_REL_ERR = 2.0 ** -20
+AMBIGUOUS_IMPACT = 2e-3
+
+
+def _ambiguous_p(p: torch.Tensor, dsum: torch.Tensor, vmax: float) -> torch.Tensor:
+    """Per row: some P within EXP2_REL_ERR (relative) of a midpoint between two e4m3 values, whose e4m3
+    step times the largest |V| over the row sum (a bound on the output change a flip causes, since later
+    rescales shrink the numerator and the row sum alike) exceeds AMBIGUOUS_IMPACT."""
+    mant, ex = torch.frexp(p)                                    # p = mant * 2^ex, mant in [0.5, 1)
+    step_units = mant * 16.0                                     # p in units of the e4m3 step 2^(ex - 4)
+    dist = (step_units - step_units.floor() - 0.5).abs() / step_units
+    step = torch.ldexp(torch.ones_like(p), ex - 4)
+    impact = step * vmax / dsum[:, None]
+    return ((p > 0) & (dist < EXP2_REL_ERR) & (impact > AMBIGUOUS_IMPACT)).any(dim=1)
+
+
+def _attn_tile(qf, qs, kf, vf, ks, t0, t1, pv_accum, sm_log2, state, tail, amb=None, vmax=0.0):
     """One 64-key tile [t0, t1) of the kernel loop (one K scale `ks`), continuing from `state`
     (running max m, row sum d, unnormalized O) when given: returns the updated (m, d, O)."""
     r, d = qf.shape[0], vf.shape[1]
@@ -235,6 +263,8 @@ def _attn_tile(qf, qs, kf, vf, ks, t0, t1, pv_accum, sm_log2, state, tail):
     alpha = torch.exp2(m - m_new)
     p = torch.exp2(_fma32(rs, scale[:, None], -m_new[:, None]))
     dsum = dsum * alpha + p.sum(dim=1)
+    if amb is not None:
+        amb |= _ambiguous_p(p, dsum, vmax)
     pq = e4m3_to_float(e4m3_rn_satfinite(p))
     if pv_accum == "fp16":
         tile_acc = torch.zeros(r, d)
@@ -271,9 +301,13 @@ def sdpa_fp32(q, k, v, sm_scale=None, rows=None, heads=None):
     return out
 
 
-def compare(a: torch.Tensor, b: torch.Tensor) -> dict:
-    """Error metrics used throughout (splitkv/check.py:48-56)."""
+def compare(a: torch.Tensor, b: torch.Tensor, exclude: torch.Tensor | None = None) -> dict:
+    """Error metrics used throughout (splitkv/check.py:48-56). `exclude` ([B, Lq, H] bool, the
+    `ambiguous` rows of attn_from_codes) drops those rows from max_abs only; `excluded` counts them."""
+    keep = None if exclude is None else (~exclude)[..., None].expand_as(a).flatten()
     a, b = a.double().flatten(), b.double().flatten()
     dlt = (a - b).abs()
-    return dict(cos=F.cosine_similarity(a, b, dim=0).item(), max_abs=dlt.max().item(),
-                rel_l2=((a - b).norm() / b.norm()).item())
+    return dict(cos=F.cosine_similarity(a, b, dim=0).item(),
+                max_abs=(dlt if keep is None else dlt[keep]).max().item(),
+                rel_l2=((a - b).norm() / b.norm()).item(),
+                excluded=0 if exclude is None else int(exclude.sum()))

@@ -9,22 +9,41 @@ from tests._gpu import k_codes_nhd, make_qkv, q_codes_nhd, v_codes_nhd
 pytestmark = pytest.mark.gpu
 
 COS_MIN, MAX_ABS = 0.9995, 2e-2
+# Rows whose result hinges on the last bits of exp2 (oracle.attn_from_codes' `ambiguous` rows) are left
+# out of the max-abs bound; at most this fraction of rows.
+AMBIGUOUS_MAX = 0.01
 
 
-def oracle_from_window(w, rows=None, heads=None, sm_scale=None, kernel_granularity=False, splits=1):
+def oracle_from_window(w, rows=None, heads=None, sm_scale=None, fp32_pv=False, splits=1, ambiguous=None):
     """Run the oracle kernel emulation on the GPU path's own codes (isolates the attention kernel).
 
-    Default: Sage's semantics (running max per 64 keys, fp16 P.V inside a tile). With
-    `kernel_granularity`, the emulation uses this kernel's own choices (running max per 128 keys,
-    fp32 P.V) and must then agree to bf16 rounding; the two emulations differ by up to ~2e-2 max-abs
-    on windows of a few dozen keys, where outputs are O(1) (the P rounding grid follows the running
-    max), and by far less on long windows."""
+    Default: Sage's semantics (64-key tiles, upstream's fp32 order, fp16 P.V inside a tile). With
+    `fp32_pv` the tile's P.V sum is fp32, the kernel's one deviation (it accumulates in tensor memory)."""
     qs = w.q_scale.cpu()
     nb = (w.kv_len + 63) // 64
     ks = w.k_scale[0][:, :, :nb].cpu()
-    kw = dict(pv_accum="fp32", splits=splits) if kernel_granularity else dict(splits=splits)
+    kw = dict(pv_accum="fp32") if fp32_pv else {}
     return O.attn_from_codes(q_codes_nhd(w), qs, k_codes_nhd(w), ks, v_codes_nhd(w), w.v_scale.cpu(),
-                             sm_scale=sm_scale, rows=rows, heads=heads, **kw)
+                             sm_scale=sm_scale, rows=rows, heads=heads, splits=splits, ambiguous=ambiguous, **kw)
+
+
+def check_parity(got, w, rows=None, heads=None, splits=1, sm_scale=None):
+    """cos >= 0.9995 and max-abs <= 2e-2 against the Sage emulation, and cos >= 0.99999 and max-abs <=
+    2e-2 against its fp32-P.V variant (ambiguous rows excluded from max-abs only). Returns both."""
+    amb = torch.zeros(got.shape[0], got.shape[1], got.shape[2], dtype=torch.bool)
+    kw = dict(rows=rows, heads=heads, splits=splits, sm_scale=sm_scale)
+    sage_ref = oracle_from_window(w, ambiguous=amb, **kw)
+    exact_ref = oracle_from_window(w, fp32_pv=True, **kw)
+
+    def sub(x):
+        x = x if rows is None else x[:, rows]
+        return x if heads is None else x[:, :, heads]
+    g, s_, e_, a_ = sub(got), sub(sage_ref), sub(exact_ref), sub(amb)
+    exact, sage = O.compare(g, e_, exclude=a_), O.compare(g, s_, exclude=a_)
+    assert exact["excluded"] <= AMBIGUOUS_MAX * a_.numel(), exact
+    assert exact["cos"] >= 0.99999 and exact["max_abs"] <= MAX_ABS, exact
+    assert sage["cos"] >= COS_MIN and sage["max_abs"] <= MAX_ABS, sage
+    return exact, sage
 
 
 SHAPES = [  # (b, h, lq, lk) — edge shapes from the reference's split-KV check (splitkv/check.py:58-63)
@@ -36,6 +55,8 @@ SHAPES = [  # (b, h, lq, lk) — edge shapes from the reference's split-KV check
 @pytest.mark.parametrize("shape", SHAPES, ids=[f"b{b}h{h}q{q}k{k}" for b, h, q, k in SHAPES])
 @pytest.mark.parametrize("splits", [1, 3])
 def test_attention_matches_oracle(shape, splits):
+    """Against the Sage emulation (fp16 P.V inside a tile) and against the same emulation with fp32
+    P.V, beside fp32 SDPA."""
     from lingbot_b200 import _lib, ops
     b, h, lq, lk = shape
     q, k, v = make_qkv(11, b, h, lq, lk)
@@ -44,12 +65,9 @@ def test_attention_matches_oracle(shape, splits):
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
     got = out.float().cpu()
-    exact = O.compare(got, oracle_from_window(w, kernel_granularity=True, splits=splits))
-    assert exact["cos"] >= 0.99999 and exact["max_abs"] <= MAX_ABS, exact
-    sage = O.compare(got, oracle_from_window(w))
-    assert sage["cos"] >= COS_MIN, sage
+    check_parity(got, w, splits=splits)
     fp32 = O.sdpa_fp32(q.cpu(), k.cpu(), v.cpu())
-    m32 = O.compare(out.float().cpu(), fp32)
+    m32 = O.compare(got, fp32)
     assert m32["cos"] > 0.995, m32
 
 
@@ -58,12 +76,8 @@ def test_attention_with_outlier_channels():
     very peaked rows), at a size the CPU oracle finishes quickly (q 384 x kv 6000, 2 heads).
 
     Here the Sage semantics themselves are far from fp32 (the emulation: cos ~0.9954, max-abs ~0.42),
-    and two fp32 evaluations of them that associate s - m differently (the kernel: S*c1 - m with c1
-    including log2(e); the emulation: (s - m)*sm*log2(e)) round a dominant key's P to neighbouring e4m3
-    values in a few rows, so elementwise agreement is limited (measured max-abs 0.049, identical with
-    exact argument arithmetic, degree-4/5 exp2 polynomials or MUFU for every key). What must hold is
-    that the kernel is as accurate as the semantics: its error against fp32 SDPA within 1e-4 cosine of
-    the emulation's, and a cosine >= 0.9999 against both emulations."""
+    because a dominant key's P lands on a coarse e4m3 grid; the kernel must follow the emulation to the
+    north star's tolerance all the same, and be as accurate against fp32."""
     from lingbot_b200 import _lib, ops
     q, k, v = make_qkv(13, 1, 2, 384, 6000, outlier="four")
     w = ops.quantize_qkv(q, k, v)
@@ -71,15 +85,10 @@ def test_attention_with_outlier_channels():
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
     got = out.float().cpu()
+    check_parity(got, w)
     fp32 = O.sdpa_fp32(q.cpu(), k.cpu(), v.cpu())
-    emu = oracle_from_window(w)
-    exact = O.compare(got, oracle_from_window(w, kernel_granularity=True))
-    sage = O.compare(got, emu)
-    m32, emu32 = O.compare(got, fp32), O.compare(emu, fp32)
-    assert exact["cos"] >= 0.9999 and sage["cos"] >= 0.9999, (exact, sage)
-    assert exact["max_abs"] <= 0.1 and sage["max_abs"] <= 0.1, (exact, sage)
+    m32, emu32 = O.compare(got, fp32), O.compare(oracle_from_window(w), fp32)
     assert m32["cos"] >= emu32["cos"] - 1e-4, (m32, emu32)
-    assert m32["max_abs"] <= 1.1 * emu32["max_abs"], (m32, emu32)
 
 
 def test_attention_config1_rows_subset():
@@ -92,27 +101,22 @@ def test_attention_config1_rows_subset():
     assert _lib.device_status() == 0
     rows = torch.cat([torch.arange(0, 128), torch.arange(2944, 3072), torch.arange(5904, 6032)])
     heads = [0, 5, 11]
-    ref = oracle_from_window(w, rows=rows, heads=heads)
+    check_parity(out.float().cpu(), w, rows=rows, heads=heads)
     got = out.float().cpu()[:, rows][:, :, heads]
-    m = O.compare(got, ref[:, rows][:, :, heads])
-    assert m["cos"] >= COS_MIN and m["max_abs"] <= MAX_ABS, m
     fp32 = O.sdpa_fp32(q.cpu(), k.cpu(), v.cpu(), rows=rows, heads=heads)[:, rows][:, :, heads]
     assert O.compare(got, fp32)["cos"] > 0.995
 
 
 @pytest.mark.parametrize("splits", [2, 4, 7])
 def test_splits_match_split_emulation(splits):
-    """Split-KV restarts the running max per split, so P lands on a different e4m3 grid: the result
-    is checked against the oracle's split emulation (strict) and against Sage semantics (cosine)."""
+    """Split-KV restarts the running max per split (splitkv/README.md:93-102), so P lands on a
+    different e4m3 grid than one pass: the result is checked against the oracle's split emulation."""
     from lingbot_b200 import ops
     q, k, v = make_qkv(5, 1, 4, 700, 5000)
     w = ops.quantize_qkv(q, k, v)
     os_ = ops.attn_from_codes(w, num_splits=splits)
     torch.cuda.synchronize()
-    got = os_.float().cpu()
-    exact = O.compare(got, oracle_from_window(w, kernel_granularity=True, splits=splits))
-    assert exact["cos"] >= 0.99999 and exact["max_abs"] <= MAX_ABS, exact
-    assert O.compare(got, oracle_from_window(w))["cos"] >= COS_MIN
+    check_parity(os_.float().cpu(), w, splits=splits)
 
 
 def test_drop_in_attention_signature():
