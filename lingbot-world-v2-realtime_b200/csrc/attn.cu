@@ -342,15 +342,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   if (warp >= 12) {
     reg_dealloc<kRegMisc>();
-    if (warp == 12 && lane == 0 && n > 0) {
-      // ---------------------------------------------------------- TMA producer
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      // Both Q tiles; a tile past q_pad reads the map's out-of-bounds zero fill.
-      mbar_arrive_expect_tx(&sh->q_full, 2 * kTile);
-      tma_load_3d(sQ, &tm_q, &sh->q_full, 0, (2 * qp) * 128, bh);
-      tma_load_3d(sQ + kTile, &tm_q, &sh->q_full, 0, (2 * qp + 1) * 128, bh);
+    if (warp == 12 && n > 0) {
+      // ---------------------------------------------------------- TMA producer (whole warp, one lane issues)
+      if (elect_one()) {
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_k);
+        tma_prefetch_desc(&tm_v);
+        // Both Q tiles; a tile past q_pad reads the map's out-of-bounds zero fill.
+        mbar_arrive_expect_tx(&sh->q_full, 2 * kTile);
+        tma_load_3d(sQ, &tm_q, &sh->q_full, 0, (2 * qp) * 128, bh);
+        tma_load_3d(sQ + kTile, &tm_q, &sh->q_full, 0, (2 * qp + 1) * 128, bh);
+      }
       int k_issued = 0, v_issued = 0;
       TileWalk<kKeyRange> tw(a, t_begin, tiles_per_seg);
       for (int i = 0; i < n; ++i, tw.next(a, tiles_per_seg)) {
@@ -358,14 +360,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int s = i % kStages;
         const uint32_t ph = (i / kStages) & 1;
         if (!mbar_wait(&sh->k_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) break;
-        mbar_arrive_expect_tx(&sh->k_full[s], kTile);
-        tma_load_3d(sK + s * kTile, &tm_k, &sh->k_full[s], 0, tw.lt * 128, tw.seg * bhs + bh);
+        if (elect_one()) {
+          mbar_arrive_expect_tx(&sh->k_full[s], kTile);
+          tma_load_3d(sK + s * kTile, &tm_k, &sh->k_full[s], 0, tw.lt * 128, tw.seg * bhs + bh);
+        }
         k_issued = i + 1;
         if (!mbar_wait(&sh->v_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) break;
-        mbar_arrive_expect_tx(&sh->v_full[s], kTile);
-        tma_load_3d(sV + s * kTile, &tm_v, &sh->v_full[s], tw.lt * 128, 0, tw.seg * bhs + bh);
+        if (elect_one()) {
+          mbar_arrive_expect_tx(&sh->v_full[s], kTile);
+          tma_load_3d(sV + s * kTile, &tm_v, &sh->v_full[s], tw.lt * 128, 0, tw.seg * bhs + bh);
+        }
         v_issued = i + 1;
       }
+      __syncwarp();
       if (*abort_flag) {
         // Let copies already in flight land before the CTA's shared memory goes away.
         mbar_drain_wait(&sh->q_full, 0);
@@ -374,8 +381,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int i = (v_issued > kStages ? v_issued - kStages : 0); i < v_issued; ++i)
           mbar_drain_wait(&sh->v_full[i % kStages], (i / kStages) & 1);
       }
-    } else if (warp == 13 && lane == 0 && n > 0) {
-      // ---------------------------------------------------------- tcgen05 issuer
+    } else if (warp == 13 && n > 0) {
+      // ---------------------------------------------------------- tcgen05 issuer (whole warp, one lane issues)
       bool ok = mbar_wait(&sh->q_full, 0, abort_flag, a.status, kDevTimeoutQ);
       tc_fence_after();
       const uint64_t qdesc[2] = {smem_desc_sw128(smem_u32(sQ)), smem_desc_sw128(smem_u32(sQ + kTile))};
@@ -391,12 +398,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int t = 0; t < 2; ++t) {
           if (!(ok = mbar_wait(&sh->s_free[t], k & 1, abort_flag, a.status, kDevTimeoutS))) return;
           tc_fence_after();
+          if (elect_one()) {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_i8_ss(tmem + kColS + 128 * t, qdesc[t] + 2 * kk, kdesc + 2 * kk, kIdescQK, 1u);
-          tc_commit(&sh->s_full[t]);
+            for (int kk = 0; kk < 4; ++kk)
+              mma_i8_ss(tmem + kColS + 128 * t, qdesc[t] + 2 * kk, kdesc + 2 * kk, kIdescQK, 1u);
+            tc_commit(&sh->s_full[t]);
+          }
+          __syncwarp();
         }
-        tc_commit(&sh->k_empty[ks]);
+        if (elect_one()) tc_commit(&sh->k_empty[ks]);
+        __syncwarp();
         if (++ks == kStages) {
           ks = 0;
           kph ^= 1;
@@ -422,11 +433,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             if (!(ok = mbar_wait(&sh->o_ready[t], u & 1, abort_flag, a.status, kDevTimeoutP))) break;
             tc_fence_after();
             const uint64_t pdesc = pdesc0 + (2 * t + (j & 1)) * kTileDesc + 4 * hh;
+            if (elect_one()) {
 #pragma unroll
-            for (int kk = 0; kk < 2; ++kk)
-              mma_f8_ss(tmem + kColO + 128 * t, pdesc + 2 * kk, vdesc + 4 * hh + 2 * kk, kIdescPV,
-                        (u > 0 || kk > 0) ? 1u : 0u);
-            tc_commit(&sh->o_done[t]);
+              for (int kk = 0; kk < 2; ++kk)
+                mma_f8_ss(tmem + kColO + 128 * t, pdesc + 2 * kk, vdesc + 4 * hh + 2 * kk, kIdescPV,
+                          (u > 0 || kk > 0) ? 1u : 0u);
+              tc_commit(&sh->o_done[t]);
+            }
+            __syncwarp();
           }
         }
         if (!ok) break;
@@ -434,8 +448,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           issue_qk(j + 2);
           if (!ok) break;
         }
-        tc_commit(&sh->v_empty[vs]);
-        for (int t = 0; t < 2; ++t) tc_commit(&sh->p_free[t][j & 1]);
+        if (elect_one()) {
+          tc_commit(&sh->v_empty[vs]);
+          for (int t = 0; t < 2; ++t) tc_commit(&sh->p_free[t][j & 1]);
+        }
+        __syncwarp();
         if (++vs == kStages) {
           vs = 0;
           vph ^= 1;
@@ -446,7 +463,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       }
       // Drain: every MMA issued above has completed once `drain` flips.
-      tc_commit(&sh->drain);
+      if (elect_one()) tc_commit(&sh->drain);
+      __syncwarp();
       mbar_drain_wait(&sh->drain, 0);
     }
   } else if (warp < 8) {

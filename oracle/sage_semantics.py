@@ -188,18 +188,16 @@ def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_sca
             qs = q_scale[bi, hi][rows // WARP_Q]                         # [R]
             kf = k_codes[bi, :, hi].float()                             # [Lk, D]
             vf = vq_all[bi, :, hi]                                       # [Lk, D]
-            parts = []
+            parts, ambs = [], []
             for pieces in partials:
                 tiles = [(t0, min(t0 + BLK_K, hi_)) for lo, hi_ in pieces for t0 in range(lo, hi_, BLK_K)]
                 state = None
-                amb = None if ambiguous is None else torch.zeros(qf.shape[0], dtype=torch.bool)
-                vmax = float(v_scale[bi, hi].max()) * V_SCALE_MAX          # largest |V| in output units
+                amb = None if ambiguous is None else torch.full((qf.shape[0],), -math.inf)
                 for i, (t0, t1) in enumerate(tiles):
                     state = _attn_tile(qf, qs, kf, vf, k_scale[bi, hi][t0 // BLK_K], t0, t1, pv_accum, sm_log2,
-                                       state, tail=i >= len(tiles) - 2, amb=amb, vmax=vmax)
-                if amb is not None:
-                    ambiguous[bi, rows, hi] |= amb
+                                       state, tail=i >= len(tiles) - 2, amb=amb)
                 parts.append(state)
+                ambs.append(amb)
             mx = torch.stack([p[0] for p in parts]).max(dim=0).values
             acc = torch.zeros(qf.shape[0], d)
             dsum = torch.zeros(qf.shape[0])
@@ -211,6 +209,12 @@ def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_sca
                 dsum += w * d_s
             o = acc * (1.0 / dsum)[:, None] * v_scale[bi, hi][None, :]
             out[bi, rows, hi] = o
+            if ambiguous is not None:
+                # a flip of one e4m3 step 2^a (in units where the row max is 2^m_s... see _attn_tile)
+                # moves the output by at most 2^(a - M) * max|V| / D
+                vmax = float(v_scale[bi, hi].max()) * V_SCALE_MAX
+                for a_log in ambs:
+                    ambiguous[bi, rows, hi] |= torch.exp2(a_log - mx) * vmax / dsum > AMBIGUOUS_IMPACT
     return out
 
 
@@ -227,19 +231,19 @@ EXP2_REL_ERR = 2.0 ** -20
 AMBIGUOUS_IMPACT = 2e-3
 
 
-def _ambiguous_p(p: torch.Tensor, dsum: torch.Tensor, vmax: float) -> torch.Tensor:
-    """Per row: some P within EXP2_REL_ERR (relative) of a midpoint between two e4m3 values, whose e4m3
-    step times the largest |V| over the row sum (a bound on the output change a flip causes, since later
-    rescales shrink the numerator and the row sum alike) exceeds AMBIGUOUS_IMPACT."""
+def _ambiguous_step_log2(p: torch.Tensor, m: torch.Tensor) -> torch.Tensor:
+    """Per row: the largest e4m3 step, as log2(step) + m (m: the running max P was taken against, so
+    that 2^(. - M) is the step relative to a final max M), of the P that lie within EXP2_REL_ERR
+    (relative) of a midpoint between two e4m3 values; -inf where none does."""
     mant, ex = torch.frexp(p)                                    # p = mant * 2^ex, mant in [0.5, 1)
     step_units = mant * 16.0                                     # p in units of the e4m3 step 2^(ex - 4)
     dist = (step_units - step_units.floor() - 0.5).abs() / step_units
-    step = torch.ldexp(torch.ones_like(p), ex - 4)
-    impact = step * vmax / dsum[:, None]
-    return ((p > 0) & (dist < EXP2_REL_ERR) & (impact > AMBIGUOUS_IMPACT)).any(dim=1)
+    near = (p > 0) & (dist < EXP2_REL_ERR)
+    lg = torch.where(near, (ex - 4).float() + m[:, None], torch.full_like(p, -math.inf))
+    return lg.max(dim=1).values
 
 
-def _attn_tile(qf, qs, kf, vf, ks, t0, t1, pv_accum, sm_log2, state, tail, amb=None, vmax=0.0):
+def _attn_tile(qf, qs, kf, vf, ks, t0, t1, pv_accum, sm_log2, state, tail, amb=None):
     """One 64-key tile [t0, t1) of the kernel loop (one K scale `ks`), continuing from `state`
     (running max m, row sum d, unnormalized O) when given: returns the updated (m, d, O)."""
     r, d = qf.shape[0], vf.shape[1]
@@ -264,7 +268,7 @@ def _attn_tile(qf, qs, kf, vf, ks, t0, t1, pv_accum, sm_log2, state, tail, amb=N
     p = torch.exp2(_fma32(rs, scale[:, None], -m_new[:, None]))
     dsum = dsum * alpha + p.sum(dim=1)
     if amb is not None:
-        amb |= _ambiguous_p(p, dsum, vmax)
+        torch.maximum(amb, _ambiguous_step_log2(p, m_new), out=amb)
     pq = e4m3_to_float(e4m3_rn_satfinite(p))
     if pv_accum == "fp16":
         tile_acc = torch.zeros(r, d)
