@@ -215,6 +215,72 @@ __device__ __forceinline__ float softmax_half(uint32_t* sv, int valid, bool tail
   return alpha;
 }
 
+// Softmax of a whole 128-key tile (two 64-key tiles, neither masked nor in upstream's tail) for the
+// calling thread's row, in two steps: tile128_max takes the maxima of both halves, tile128_exp every
+// exp2, so that the second half's max does not wait for the first half's exponentials. The arithmetic is
+// softmax_sub's on each half in turn (the second against the running max after the first). P goes to
+// chunks 0..7 of this row of the shared P tile; tile128_exp returns the two alphas.
+__device__ __forceinline__ float2 tile128_max(const uint32_t* sv) {
+  auto F = [&](int j) { return __uint_as_float(sv[j]); };
+  float r[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) r[q] = fmaxf(F(8 * (q >> 2) * 8 + 2 * (q & 3)), F(8 * (q >> 2) * 8 + 2 * (q & 3) + 1));
+#pragma unroll
+  for (int j = 8; j < 64; j += 8) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      r[q] = fmax3(r[q], F(j + 2 * q), F(j + 2 * q + 1));
+      r[4 + q] = fmax3(r[4 + q], F(64 + j + 2 * q), F(64 + j + 2 * q + 1));
+    }
+  }
+  return make_float2(fmax3(r[0], r[1], fmaxf(r[2], r[3])) - kMagic, fmax3(r[4], r[5], fmaxf(r[6], r[7])) - kMagic);
+}
+__device__ __forceinline__ float2 tile128_exp(const uint32_t* sv, float2 smax, float c0, float c1, float& m,
+                                              float& dsum, uint8_t* prow, int rsw) {
+  auto F = [&](int j) { return __uint_as_float(sv[j]); };
+  const float m1 = fmaxf(m, __fmaf_rn(smax.x, c0, -kFp8Offset));
+  const float m2 = fmaxf(m1, __fmaf_rn(smax.y, c1, -kFp8Offset));
+  const float alpha1 = (m == m1) ? 1.f : ex2_approx(m - m1);
+  const float alpha2 = (m1 == m2) ? 1.f : ex2_approx(m1 - m2);
+  m = m2;
+  const uint64_t nk2 = f2_pack(-kMagic, -kMagic);
+  uint64_t acc[4] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+  uint32_t pw[4];
+#pragma unroll
+  for (int w = 0; w < 32; ++w) {
+    const int hh = w >> 4;
+    const uint64_t c2 = hh ? f2_pack(c1, c1) : f2_pack(c0, c0);
+    const uint64_t negm2 = hh ? f2_pack(-m2, -m2) : f2_pack(-m1, -m1);
+    uint32_t half16[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int j = 4 * w + 2 * e;
+      const uint64_t x = f2_fma(f2_add(f2_pack(F(j), F(j + 1)), nk2), c2, negm2);
+      float x0, x1;
+      f2_unpack(x, x0, x1);
+      uint64_t p;
+      if (((j >> 1) & 15) >= 16 - kPolyPairs) {
+        p = exp2_poly_x2(x0, x1);
+      } else {
+        p = f2_pack(ex2_approx(x0), ex2_approx(x1));
+      }
+      float p0, p1;
+      f2_unpack(p, p0, p1);
+      acc[2 * hh + e] = f2_add(acc[2 * hh + e], p);
+      half16[e] = pack_e4m3x2(p0, p1);
+    }
+    pw[w & 3] = half16[0] | (half16[1] << 16);
+    if ((w & 3) == 3)   // 16 keys done: one swizzled 16-byte chunk of the row
+      *reinterpret_cast<uint4*>(prow + (((w >> 2) ^ rsw) << 4)) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+  }
+  float s[8];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) f2_unpack(acc[q], s[2 * q], s[2 * q + 1]);
+  dsum = __fadd_rn(__fmul_rn(dsum, alpha1), (s[0] + s[1]) + (s[2] + s[3]));
+  dsum = __fadd_rn(__fmul_rn(dsum, alpha2), (s[4] + s[5]) + (s[6] + s[7]));
+  return make_float2(alpha1, alpha2);
+}
+
 // Key-range epilogue of one correction warp: its 32 rows of O / row sum as fp16 (V-code units, |x| <=
 // 448) are staged in `stage` (32 KB of free shared memory; 16-byte chunks of a 256-byte row XOR-swizzled
 // by row) and stored to the owner rank's receive slot for this rank as whole rows, two rows per warp
@@ -413,9 +479,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           kph ^= 1;
         }
       };
-      // Order per key tile j: P.V of its first half, Q.K^T of tile j + 2 (S_t was read by the softmax of
-      // tile j + 1), P.V of its second half. The scores of tile j + 2 are then ready long before the
-      // softmax gets to them.
+      // Order per key tile j: the P.V products of its halves, then Q.K^T of tile j + 2 (S_t is read by the
+      // softmax of tile j + 1 in its first half). The scores of tile j + 2 are ready long before the
+      // softmax gets to them, and P buffer j & 1 is handed back as early as possible.
       TileWalk<kKeyRange> tw(a, t_begin, tiles_per_seg);
       int ns = tw.valid(a) > 64 ? 2 : 1;               // 64-key halves of tile j
       int vs = 0, vph = 0;                              // V stage of tile j and its phase bit
@@ -425,10 +491,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (!(ok = mbar_wait(&sh->v_full[vs], vph, abort_flag, a.status, kDevTimeoutKV))) break;
         const uint64_t vdesc = vdesc0 + vs * kTileDesc;
         for (int hh = 0; ok && hh < ns; ++hh, ++u) {
-          if (hh == 1 && j + 2 < n) {
-            issue_qk(j + 2);
-            if (!ok) break;
-          }
           for (int t = 0; t < 2; ++t) {                 // P_t(j, hh) written, O_t rescaled -> O_t += P V
             if (!(ok = mbar_wait(&sh->o_ready[t], u & 1, abort_flag, a.status, kDevTimeoutP))) break;
             tc_fence_after();
@@ -444,15 +506,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
         if (!ok) break;
-        if (ns == 1 && j + 2 < n) {                     // a one-half tile: Q.K^T of tile j + 2 after its P.V
-          issue_qk(j + 2);
-          if (!ok) break;
-        }
         if (elect_one()) {
           tc_commit(&sh->v_empty[vs]);
           for (int t = 0; t < 2; ++t) tc_commit(&sh->p_free[t][j & 1]);
         }
         __syncwarp();
+        if (j + 2 < n) {
+          issue_qk(j + 2);
+          if (!ok) break;
+        }
         if (++vs == kStages) {
           vs = 0;
           vph ^= 1;
@@ -537,6 +599,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       uint8_t* prow = sP + (2 * t + (j & 1)) * kTile + prow_off;
       const bool last1 = j == n - 1, prev1 = j == n - 2 && ns_last == 1;
+      if (tv == 128 && !last1 && !prev1) {              // the bulk: both halves in one pass
+        const float2 smax = tile128_max(sv);
+        tmem_st_wait();                                 // the S refill has landed: the next Q.K^T may go
+        tc_fence_before();
+        mbar_arrive(&sh->s_free[t]);
+        const float2 al = tile128_exp(sv, smax, __fmul_rn(sm, __fmul_rn(qs, ks.x)), __fmul_rn(sm, __fmul_rn(qs, ks.y)),
+                                      m, dsum, prow, rsw);
+        sh->alpha[t][j & 1][0][rl] = al.x;
+        sh->alpha[t][j & 1][1][rl] = al.y;
+        fence_proxy_async_smem();
+        mbar_arrive(&sh->p_full[t][j & 1]);
+        continue;
+      }
       {
         const float dq = __fmul_rn(qs, ks.x);
         const float alpha = softmax_half(sv, min(64, tv), last1 || (prev1 && tv <= 64), __fmul_rn(sm, dq), dq, sm,
