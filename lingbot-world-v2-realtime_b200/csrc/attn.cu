@@ -20,8 +20,11 @@
 // CTA = two 128-row Q tiles (A, B) x one (batch, head) x one KV split, 512 threads:
 //   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B: one thread per row (= TMEM lane);
 //   warps 8-11  correction: O_t *= alpha before each 64-key P.V, then the epilogue of both tiles;
-//   warp 12     TMA producer (both Q tiles once; K and V^T in 128-key stages through a ring);
-//   warp 13     tcgen05 issuer (one thread) and tensor-memory owner; warps 14-15 idle.
+//   warp 12     TMA producer of both Q tiles (once) and of K in 128-key stages through a ring;
+//   warp 15     TMA producer of V^T (its own ring, so K can run ahead of V);
+//   warp 13     Q.K^T issuer and tensor-memory owner, warp 14 P.V issuer: two issuing warps, so that the
+//               scores of the next key tile never wait behind the P.V chain (each issues under
+//               elect.sync; they touch disjoint tensor memory and hand buffers back by barrier).
 // Q.K^T runs on 128 keys (one MMA of N = 128 per 32 channels); the softmax takes the two 64-key halves
 // of the score tile in turn, each against the running max after the previous half, and P.V runs per
 // half (K = 64), the correction warps rescaling O between the two products when the second half
@@ -31,8 +34,8 @@
 // bits of the float 1.5*2^23 + S (|S| <= 128*127*127 < 2^21), so S needs one exact subtraction and no
 // conversion. The refill completes during the first half's softmax, after which the Q.K^T of the next
 // key tile runs during the second half. P (e4m3) goes to a double-buffered shared-memory tile
-// (128-byte-swizzled K-major rows), the A operand of P.V; the issuer hands a P buffer back with its own
-// barrier, so Q.K^T may run ahead of the P.V products.
+// (128-byte-swizzled K-major rows), the A operand of P.V; the P.V issuer hands a P buffer back with its
+// own barrier, so Q.K^T may run ahead of the P.V products.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
@@ -78,7 +81,7 @@ struct AttnShared {
   uint64_t o_ready[2];                   // O_t rescaled for the next 64-key P.V (128 correction threads)
   uint64_t o_done[2];                    // P.V complete
   uint64_t ml_full[2];                   // final (m, d) of every row in `ml`
-  uint64_t drain;
+  uint64_t drain_qk, drain_pv;           // each issuer's MMAs complete
   uint32_t tmem_base;
   int abort;
   float alpha[2][2][2][128];             // [Q tile][j & 1][64-key half][row]
@@ -393,7 +396,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&sh->o_done[t], 1);
       mbar_init(&sh->ml_full[t], 128);
     }
-    mbar_init(&sh->drain, 1);
+    mbar_init(&sh->drain_qk, 1);
+    mbar_init(&sh->drain_pv, 1);
     sh->abort = 0;
     fence_mbar_init();
   }
@@ -409,60 +413,68 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (warp >= 12) {
     reg_dealloc<kRegMisc>();
     if (warp == 12 && n > 0) {
-      // ---------------------------------------------------------- TMA producer (whole warp, one lane issues)
+      // ---------------------------------------------------------- TMA producer of Q and K (one lane issues)
       if (elect_one()) {
         tma_prefetch_desc(&tm_q);
         tma_prefetch_desc(&tm_k);
-        tma_prefetch_desc(&tm_v);
         // Both Q tiles; a tile past q_pad reads the map's out-of-bounds zero fill.
         mbar_arrive_expect_tx(&sh->q_full, 2 * kTile);
         tma_load_3d(sQ, &tm_q, &sh->q_full, 0, (2 * qp) * 128, bh);
         tma_load_3d(sQ + kTile, &tm_q, &sh->q_full, 0, (2 * qp + 1) * 128, bh);
       }
-      int k_issued = 0, v_issued = 0;
+      int issued = 0;
       TileWalk<kKeyRange> tw(a, t_begin, tiles_per_seg);
       for (int i = 0; i < n; ++i, tw.next(a, tiles_per_seg)) {
         (void)LBQ_CHECK(tw.seg < a.nseg && tw.lt >= 0 && tw.lt < tiles_per_seg, a.status, kDevBadTile);
         const int s = i % kStages;
-        const uint32_t ph = (i / kStages) & 1;
-        if (!mbar_wait(&sh->k_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) break;
+        if (!mbar_wait(&sh->k_empty[s], ((i / kStages) & 1) ^ 1, abort_flag, a.status, kDevTimeoutKV)) break;
         if (elect_one()) {
           mbar_arrive_expect_tx(&sh->k_full[s], kTile);
           tma_load_3d(sK + s * kTile, &tm_k, &sh->k_full[s], 0, tw.lt * 128, tw.seg * bhs + bh);
         }
-        k_issued = i + 1;
-        if (!mbar_wait(&sh->v_empty[s], ph ^ 1, abort_flag, a.status, kDevTimeoutKV)) break;
+        __syncwarp();
+        issued = i + 1;
+      }
+      if (*abort_flag) {
+        // Let copies already in flight land before the CTA's shared memory goes away.
+        mbar_drain_wait(&sh->q_full, 0);
+        for (int i = (issued > kStages ? issued - kStages : 0); i < issued; ++i)
+          mbar_drain_wait(&sh->k_full[i % kStages], (i / kStages) & 1);
+      }
+    } else if (warp == 15 && n > 0) {
+      // ---------------------------------------------------------- TMA producer of V^T (one lane issues)
+      if (elect_one()) tma_prefetch_desc(&tm_v);
+      int issued = 0;
+      TileWalk<kKeyRange> tw(a, t_begin, tiles_per_seg);
+      for (int i = 0; i < n; ++i, tw.next(a, tiles_per_seg)) {
+        const int s = i % kStages;
+        if (!mbar_wait(&sh->v_empty[s], ((i / kStages) & 1) ^ 1, abort_flag, a.status, kDevTimeoutKV)) break;
         if (elect_one()) {
           mbar_arrive_expect_tx(&sh->v_full[s], kTile);
           tma_load_3d(sV + s * kTile, &tm_v, &sh->v_full[s], tw.lt * 128, 0, tw.seg * bhs + bh);
         }
-        v_issued = i + 1;
+        __syncwarp();
+        issued = i + 1;
       }
-      __syncwarp();
       if (*abort_flag) {
-        // Let copies already in flight land before the CTA's shared memory goes away.
-        mbar_drain_wait(&sh->q_full, 0);
-        for (int i = (k_issued > kStages ? k_issued - kStages : 0); i < k_issued; ++i)
-          mbar_drain_wait(&sh->k_full[i % kStages], (i / kStages) & 1);
-        for (int i = (v_issued > kStages ? v_issued - kStages : 0); i < v_issued; ++i)
+        for (int i = (issued > kStages ? issued - kStages : 0); i < issued; ++i)
           mbar_drain_wait(&sh->v_full[i % kStages], (i / kStages) & 1);
       }
     } else if (warp == 13 && n > 0) {
-      // ---------------------------------------------------------- tcgen05 issuer (whole warp, one lane issues)
+      // ---------------------------------------------------------- Q.K^T issuer (one lane issues)
+      // S_t(k) = Q_t . K(k)^T for both tiles once S_t(k - 1) was read and refilled (k = 0: the initial
+      // fill), onto the magic constant the softmax left in S_t. Runs ahead of the P.V products.
       bool ok = mbar_wait(&sh->q_full, 0, abort_flag, a.status, kDevTimeoutQ);
       tc_fence_after();
       const uint64_t qdesc[2] = {smem_desc_sw128(smem_u32(sQ)), smem_desc_sw128(smem_u32(sQ + kTile))};
-      const uint64_t kdesc0 = smem_desc_sw128(smem_u32(sK)), vdesc0 = smem_desc_sw128(smem_u32(sV));
-      const uint64_t pdesc0 = smem_desc_sw128(smem_u32(sP));
+      const uint64_t kdesc0 = smem_desc_sw128(smem_u32(sK));
       constexpr uint64_t kTileDesc = kTile >> 4;        // one tile in descriptor address units
-      int ks = 0, kph = 0;                              // K stage of the next Q.K^T and its phase bit
-      // S_t += Q_t . K(next stage)^T for both tiles once S_t(k - 1) was read and refilled (k: the key
-      // tile, k - 1 < 0 meaning the initial fill), onto the magic constant the softmax left in S_t
-      auto issue_qk = [&](int k) {
-        if (!(ok = mbar_wait(&sh->k_full[ks], kph, abort_flag, a.status, kDevTimeoutKV))) return;
-        const uint64_t kdesc = kdesc0 + ks * kTileDesc;
-        for (int t = 0; t < 2; ++t) {
-          if (!(ok = mbar_wait(&sh->s_free[t], k & 1, abort_flag, a.status, kDevTimeoutS))) return;
+      for (int k = 0; ok && k < n; ++k) {
+        const int s = k % kStages;
+        if (!(ok = mbar_wait(&sh->k_full[s], (k / kStages) & 1, abort_flag, a.status, kDevTimeoutKV))) break;
+        const uint64_t kdesc = kdesc0 + s * kTileDesc;
+        for (int t = 0; ok && t < 2; ++t) {
+          if (!(ok = mbar_wait(&sh->s_free[t], k & 1, abort_flag, a.status, kDevTimeoutS))) break;
           tc_fence_after();
           if (elect_one()) {
 #pragma unroll
@@ -472,26 +484,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
           __syncwarp();
         }
-        if (elect_one()) tc_commit(&sh->k_empty[ks]);
+        if (!ok) break;
+        if (elect_one()) tc_commit(&sh->k_empty[s]);
         __syncwarp();
-        if (++ks == kStages) {
-          ks = 0;
-          kph ^= 1;
-        }
-      };
-      // Order per key tile j: the P.V products of its halves, then Q.K^T of tile j + 2 (S_t is read by the
-      // softmax of tile j + 1 in its first half). The scores of tile j + 2 are ready long before the
-      // softmax gets to them, and P buffer j & 1 is handed back as early as possible.
+      }
+      // Drain: every MMA this warp issued has completed once `drain_qk` flips.
+      if (elect_one()) tc_commit(&sh->drain_qk);
+      __syncwarp();
+      mbar_drain_wait(&sh->drain_qk, 0);
+    } else if (warp == 14 && n > 0) {
+      // ---------------------------------------------------------- P.V issuer (one lane issues)
+      // O_t (+)= P_t(j, hh) . V(j, hh) per 64-key half once the softmax wrote P and the correction
+      // rescaled O_t; P buffer j & 1 and V stage j are handed back after the tile's last product.
+      const uint64_t vdesc0 = smem_desc_sw128(smem_u32(sV)), pdesc0 = smem_desc_sw128(smem_u32(sP));
+      constexpr uint64_t kTileDesc = kTile >> 4;
+      bool ok = true;
       TileWalk<kKeyRange> tw(a, t_begin, tiles_per_seg);
-      int ns = tw.valid(a) > 64 ? 2 : 1;               // 64-key halves of tile j
-      int vs = 0, vph = 0;                              // V stage of tile j and its phase bit
       int u = 0;                                        // P.V products issued per Q tile
-      for (int k = 0; ok && k < 2 && k < n; ++k) issue_qk(k);
-      for (int j = 0; ok && j < n; ++j) {
-        if (!(ok = mbar_wait(&sh->v_full[vs], vph, abort_flag, a.status, kDevTimeoutKV))) break;
-        const uint64_t vdesc = vdesc0 + vs * kTileDesc;
+      for (int j = 0; ok && j < n; ++j, tw.next(a, tiles_per_seg)) {
+        const int ns = tw.valid(a) > 64 ? 2 : 1;       // 64-key halves of tile j
+        const int s = j % kStages;
+        if (!(ok = mbar_wait(&sh->v_full[s], (j / kStages) & 1, abort_flag, a.status, kDevTimeoutKV))) break;
+        const uint64_t vdesc = vdesc0 + s * kTileDesc;
         for (int hh = 0; ok && hh < ns; ++hh, ++u) {
-          for (int t = 0; t < 2; ++t) {                 // P_t(j, hh) written, O_t rescaled -> O_t += P V
+          for (int t = 0; t < 2; ++t) {
             if (!(ok = mbar_wait(&sh->o_ready[t], u & 1, abort_flag, a.status, kDevTimeoutP))) break;
             tc_fence_after();
             const uint64_t pdesc = pdesc0 + (2 * t + (j & 1)) * kTileDesc + 4 * hh;
@@ -507,27 +523,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         if (!ok) break;
         if (elect_one()) {
-          tc_commit(&sh->v_empty[vs]);
+          tc_commit(&sh->v_empty[s]);
           for (int t = 0; t < 2; ++t) tc_commit(&sh->p_free[t][j & 1]);
         }
         __syncwarp();
-        if (j + 2 < n) {
-          issue_qk(j + 2);
-          if (!ok) break;
-        }
-        if (++vs == kStages) {
-          vs = 0;
-          vph ^= 1;
-        }
-        if (j + 1 < n) {
-          tw.next(a, tiles_per_seg);
-          ns = tw.valid(a) > 64 ? 2 : 1;
-        }
       }
-      // Drain: every MMA issued above has completed once `drain` flips.
-      if (elect_one()) tc_commit(&sh->drain);
+      // Drain: every MMA this warp issued has completed once `drain_pv` flips.
+      if (elect_one()) tc_commit(&sh->drain_pv);
       __syncwarp();
-      mbar_drain_wait(&sh->drain, 0);
+      mbar_drain_wait(&sh->drain_pv, 0);
     }
   } else if (warp < 8) {
     // ------------------------------------------------------------ softmax warpgroups
