@@ -46,7 +46,10 @@
 
 namespace lbq {
 
-constexpr int kStages = 3;
+constexpr int kStages = 2;               // K and V^T stages (128 keys each)
+constexpr int kPBufs = 3;                // P buffers per Q tile: the P.V of a tile may finish two tiles late
+__device__ __forceinline__ int pbuf(int j) { return j % kPBufs; }
+__device__ __forceinline__ uint32_t pphase(int j) { return (j / kPBufs) & 1; }
 constexpr int kTile = 128 * 128;         // bytes of a Q tile, a P tile and a 128-key K or V^T stage
 constexpr int kAttnThreads = 512;
 constexpr float kFp8Offset = 8.807f;     // splitkv/README.md:58 (S_FP8_OFFSET)
@@ -72,24 +75,26 @@ struct AttnShared {
   uint64_t v_full[kStages];
   uint64_t v_empty[kStages];
   uint64_t s_full[2];                    // per Q tile: Q.K^T of the next 128-key tile complete
-  uint64_t s_free[2];                    // S read and refilled (128 softmax threads)
-  uint64_t p_full[2][2];                 // [tile][j & 1]: P of key tile j in shared memory, its alphas
-                                         // written (128 softmax threads); two per tile, since the softmax
-                                         // may run a key tile ahead of the correction
-  uint64_t p_free[2][2];                 // [tile][j & 1]: the P.V products of key tile j complete (commit):
-                                         // P buffer j & 1 and its alphas may be overwritten
+  uint64_t s_read[2];                    // S read (128 softmax threads): the correction warps refill it
+  uint64_t s_free[2];                    // S refilled with the magic constant (128 correction threads)
+  uint64_t p_full[2][kPBufs];            // [tile][pbuf(j)]: P of key tile j in shared memory, its alphas
+                                         // written (128 softmax threads); one per buffer, since the softmax
+                                         // may run key tiles ahead of the correction
+  uint64_t p_free[2][kPBufs];            // [tile][pbuf(j)]: the P.V products of key tile j complete (commit):
+                                         // that P buffer and its alphas may be overwritten
   uint64_t o_ready[2];                   // O_t rescaled for the next 64-key P.V (128 correction threads)
   uint64_t o_done[2];                    // P.V complete
   uint64_t ml_full[2];                   // final (m, d) of every row in `ml`
   uint64_t drain_qk, drain_pv;           // each issuer's MMAs complete
   uint32_t tmem_base;
   int abort;
-  float alpha[2][2][2][128];             // [Q tile][j & 1][64-key half][row]
+  float alpha[2][kPBufs][2][128];        // [Q tile][pbuf(j)][64-key half][row]
   float2 ml[2][128];                     // [Q tile][row]
 };
 
-// smem: Q_A, Q_B | P_A[2], P_B[2] | K stages | V stages | AttnShared
-constexpr size_t kAttnSmemBytes = 1024 /*alignment slack*/ + kTile * (6 + 2 * kStages) + sizeof(AttnShared);
+// smem: Q_A, Q_B | P_A[kPBufs], P_B[kPBufs] | K stages | V stages | AttnShared
+constexpr int kSmemTiles = 2 + 2 * kPBufs + 2 * kStages;
+constexpr size_t kAttnSmemBytes = 1024 /*alignment slack*/ + kTile * kSmemTiles + sizeof(AttnShared);
 
 __device__ int g_status;
 
@@ -363,9 +368,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                              // [2][kTile]
   uint8_t* sP = smem + 2 * kTile;                  // [tile][buffer][kTile]
-  uint8_t* sK = smem + 6 * kTile;                  // [kStages][kTile]
-  uint8_t* sV = smem + kTile * (6 + kStages);      // [kStages][kTile]
-  AttnShared* sh = reinterpret_cast<AttnShared*>(smem + kTile * (6 + 2 * kStages));
+  uint8_t* sK = smem + kTile * (2 + 2 * kPBufs);   // [kStages][kTile]
+  uint8_t* sV = sK + kTile * kStages;              // [kStages][kTile]
+  AttnShared* sh = reinterpret_cast<AttnShared*>(smem + kTile * kSmemTiles);
   volatile int* abort_flag = &sh->abort;
 
   const int qp = blockIdx.x, bh = blockIdx.y, split = blockIdx.z;   // qp: pair of 128-row Q tiles
@@ -387,11 +392,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sh->s_full[t], 1);
+      mbar_init(&sh->s_read[t], 128);
       mbar_init(&sh->s_free[t], 128);
-      mbar_init(&sh->p_full[t][0], 128);
-      mbar_init(&sh->p_full[t][1], 128);
-      mbar_init(&sh->p_free[t][0], 1);
-      mbar_init(&sh->p_free[t][1], 1);
+      for (int pb = 0; pb < kPBufs; ++pb) {
+        mbar_init(&sh->p_full[t][pb], 128);
+        mbar_init(&sh->p_free[t][pb], 1);
+      }
       mbar_init(&sh->o_ready[t], 128);
       mbar_init(&sh->o_done[t], 1);
       mbar_init(&sh->ml_full[t], 128);
@@ -427,7 +433,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int i = 0; i < n; ++i, tw.next(a, tiles_per_seg)) {
         (void)LBQ_CHECK(tw.seg < a.nseg && tw.lt >= 0 && tw.lt < tiles_per_seg, a.status, kDevBadTile);
         const int s = i % kStages;
-        if (!mbar_wait(&sh->k_empty[s], ((i / kStages) & 1) ^ 1, abort_flag, a.status, kDevTimeoutKV)) break;
+        if (!mbar_wait_role(&sh->k_empty[s], ((i / kStages) & 1) ^ 1, abort_flag, a.status, kDevTimeoutKV)) break;
         if (elect_one()) {
           mbar_arrive_expect_tx(&sh->k_full[s], kTile);
           tma_load_3d(sK + s * kTile, &tm_k, &sh->k_full[s], 0, tw.lt * 128, tw.seg * bhs + bh);
@@ -448,7 +454,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       TileWalk<kKeyRange> tw(a, t_begin, tiles_per_seg);
       for (int i = 0; i < n; ++i, tw.next(a, tiles_per_seg)) {
         const int s = i % kStages;
-        if (!mbar_wait(&sh->v_empty[s], ((i / kStages) & 1) ^ 1, abort_flag, a.status, kDevTimeoutKV)) break;
+        if (!mbar_wait_role(&sh->v_empty[s], ((i / kStages) & 1) ^ 1, abort_flag, a.status, kDevTimeoutKV)) break;
         if (elect_one()) {
           mbar_arrive_expect_tx(&sh->v_full[s], kTile);
           tma_load_3d(sV + s * kTile, &tm_v, &sh->v_full[s], tw.lt * 128, 0, tw.seg * bhs + bh);
@@ -464,17 +470,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // ---------------------------------------------------------- Q.K^T issuer (one lane issues)
       // S_t(k) = Q_t . K(k)^T for both tiles once S_t(k - 1) was read and refilled (k = 0: the initial
       // fill), onto the magic constant the softmax left in S_t. Runs ahead of the P.V products.
-      bool ok = mbar_wait(&sh->q_full, 0, abort_flag, a.status, kDevTimeoutQ);
+      bool ok = mbar_wait_role(&sh->q_full, 0, abort_flag, a.status, kDevTimeoutQ);
       tc_fence_after();
       const uint64_t qdesc[2] = {smem_desc_sw128(smem_u32(sQ)), smem_desc_sw128(smem_u32(sQ + kTile))};
       const uint64_t kdesc0 = smem_desc_sw128(smem_u32(sK));
       constexpr uint64_t kTileDesc = kTile >> 4;        // one tile in descriptor address units
       for (int k = 0; ok && k < n; ++k) {
         const int s = k % kStages;
-        if (!(ok = mbar_wait(&sh->k_full[s], (k / kStages) & 1, abort_flag, a.status, kDevTimeoutKV))) break;
+        if (!(ok = mbar_wait_role(&sh->k_full[s], (k / kStages) & 1, abort_flag, a.status, kDevTimeoutKV))) break;
         const uint64_t kdesc = kdesc0 + s * kTileDesc;
         for (int t = 0; ok && t < 2; ++t) {
-          if (!(ok = mbar_wait(&sh->s_free[t], k & 1, abort_flag, a.status, kDevTimeoutS))) break;
+          if (!(ok = mbar_wait_role(&sh->s_free[t], k & 1, abort_flag, a.status, kDevTimeoutS))) break;
           tc_fence_after();
           if (elect_one()) {
 #pragma unroll
@@ -495,7 +501,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     } else if (warp == 14 && n > 0) {
       // ---------------------------------------------------------- P.V issuer (one lane issues)
       // O_t (+)= P_t(j, hh) . V(j, hh) per 64-key half once the softmax wrote P and the correction
-      // rescaled O_t; P buffer j & 1 and V stage j are handed back after the tile's last product.
+      // rescaled O_t; P buffer pbuf(j) and V stage j are handed back after the tile's last product.
       const uint64_t vdesc0 = smem_desc_sw128(smem_u32(sV)), pdesc0 = smem_desc_sw128(smem_u32(sP));
       constexpr uint64_t kTileDesc = kTile >> 4;
       bool ok = true;
@@ -504,13 +510,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int j = 0; ok && j < n; ++j, tw.next(a, tiles_per_seg)) {
         const int ns = tw.valid(a) > 64 ? 2 : 1;       // 64-key halves of tile j
         const int s = j % kStages;
-        if (!(ok = mbar_wait(&sh->v_full[s], (j / kStages) & 1, abort_flag, a.status, kDevTimeoutKV))) break;
+        if (!(ok = mbar_wait_role(&sh->v_full[s], (j / kStages) & 1, abort_flag, a.status, kDevTimeoutKV))) break;
         const uint64_t vdesc = vdesc0 + s * kTileDesc;
         for (int hh = 0; ok && hh < ns; ++hh, ++u) {
           for (int t = 0; t < 2; ++t) {
-            if (!(ok = mbar_wait(&sh->o_ready[t], u & 1, abort_flag, a.status, kDevTimeoutP))) break;
+            if (!(ok = mbar_wait_role(&sh->o_ready[t], u & 1, abort_flag, a.status, kDevTimeoutP))) break;
             tc_fence_after();
-            const uint64_t pdesc = pdesc0 + (2 * t + (j & 1)) * kTileDesc + 4 * hh;
+            const uint64_t pdesc = pdesc0 + (kPBufs * t + pbuf(j)) * kTileDesc + 4 * hh;
             if (elect_one()) {
 #pragma unroll
               for (int kk = 0; kk < 2; ++kk)
@@ -524,7 +530,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (!ok) break;
         if (elect_one()) {
           tc_commit(&sh->v_empty[s]);
-          for (int t = 0; t < 2; ++t) tc_commit(&sh->p_free[t][j & 1]);
+          for (int t = 0; t < 2; ++t) tc_commit(&sh->p_free[t][pbuf(j)]);
         }
         __syncwarp();
       }
@@ -561,12 +567,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       TileWalk<kKeyRange> tl(a, t_end - 1, tiles_per_seg);
       ns_last = tl.valid(a) > 64 ? 2 : 1;
     }
-    // S_t starts as the magic constant (the first Q.K^T accumulates onto it)
-#pragma unroll
-    for (int c = 0; c < 16; ++c) tmem_fill8(tS + 8 * c, kMagicBits);
-    tmem_st_wait();
-    tc_fence_before();
-    mbar_arrive(&sh->s_free[t]);
     float2 ks_next = ok ? *reinterpret_cast<const float2*>(kscale_ptr(tw)) : make_float2(0.f, 0.f);
     for (int j = 0; ok && j < n; ++j) {
       const int tv = tw.valid(a);
@@ -593,47 +593,40 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       reg_anchor(sv1);
       reg_anchor(sv2);
       reg_anchor(sv3);
-      // refill S_t with the magic constant; its stores complete during the first half's softmax
-#pragma unroll
-      for (int c = 0; c < 16; ++c) tmem_fill8(tS + 8 * c, kMagicBits);
-      // P_t[j & 1] and its alphas were last read for tile j - 2
-      if (j >= 2 && !mbar_wait(&sh->p_free[t][j & 1], ((j - 2) >> 1) & 1, abort_flag, a.status, kDevTimeoutO)) {
+      tc_fence_before();
+      mbar_arrive(&sh->s_read[t]);                     // S_t read: the correction warps refill it
+      // P buffer pbuf(j) of this tile and its alphas were last read for tile j - kPBufs
+      const int pb = pbuf(j);
+      if (j >= kPBufs && !mbar_wait(&sh->p_free[t][pb], pphase(j - kPBufs), abort_flag, a.status, kDevTimeoutO)) {
         ok = false;
         break;
       }
-      uint8_t* prow = sP + (2 * t + (j & 1)) * kTile + prow_off;
+      uint8_t* prow = sP + (kPBufs * t + pb) * kTile + prow_off;
       const bool last1 = j == n - 1, prev1 = j == n - 2 && ns_last == 1;
       if (tv == 128 && !last1 && !prev1) {              // the bulk: both halves in one pass
         const float2 smax = tile128_max(sv);
-        tmem_st_wait();                                 // the S refill has landed: the next Q.K^T may go
-        tc_fence_before();
-        mbar_arrive(&sh->s_free[t]);
         const float2 al = tile128_exp(sv, smax, __fmul_rn(sm, __fmul_rn(qs, ks.x)), __fmul_rn(sm, __fmul_rn(qs, ks.y)),
                                       m, dsum, prow, rsw);
-        sh->alpha[t][j & 1][0][rl] = al.x;
-        sh->alpha[t][j & 1][1][rl] = al.y;
+        sh->alpha[t][pb][0][rl] = al.x;
+        sh->alpha[t][pb][1][rl] = al.y;
         fence_proxy_async_smem();
-        mbar_arrive(&sh->p_full[t][j & 1]);
+        mbar_arrive(&sh->p_full[t][pb]);
         continue;
       }
       {
         const float dq = __fmul_rn(qs, ks.x);
         const float alpha = softmax_half(sv, min(64, tv), last1 || (prev1 && tv <= 64), __fmul_rn(sm, dq), dq, sm,
                                          m, dsum, prow, 0, rsw);
-        sh->alpha[t][j & 1][0][rl] = alpha;
+        sh->alpha[t][pb][0][rl] = alpha;
       }
-      // S_t refilled: the Q.K^T of tile j + 1 may go (it runs during the second half)
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&sh->s_free[t]);
       if (tv > 64) {
         const float dq = __fmul_rn(qs, ks.y);
         const float alpha = softmax_half(sv + 64, tv - 64, last1 || prev1, __fmul_rn(sm, dq), dq, sm, m, dsum, prow,
                                          1, rsw);
-        sh->alpha[t][j & 1][1][rl] = alpha;
+        sh->alpha[t][pb][1][rl] = alpha;
       }
       fence_proxy_async_smem();
-      mbar_arrive(&sh->p_full[t][j & 1]);
+      mbar_arrive(&sh->p_full[t][pb]);
     }
     if (ok) {
       sh->ml[t][rl] = make_float2(m, dsum);
@@ -647,18 +640,42 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int rl = quarter * 32 + lane;
     bool ok = n > 0;
     int u = 0;
+    // S_t = magic for the Q.K^T to accumulate onto: once at the start, then each time the softmax has
+    // read the scores (16 registers hold the constant, so a refill is eight 16-column stores)
+    uint32_t mg[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) mg[c] = kMagicBits;
+    auto refill = [&](int t) {
+      const uint32_t tS = tmem + kColS + 128 * t + lane_off;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) tmem_st16(tS + 16 * c, mg);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&sh->s_free[t]);
+    };
+    if (ok) {
+      refill(0);
+      refill(1);
+    }
     TileWalk<kKeyRange> tw(a, t_begin, tiles_per_seg);
     for (int j = 0; ok && j < n; ++j, tw.next(a, tiles_per_seg)) {
       const int ns = tw.valid(a) > 64 ? 2 : 1;
+      if (j + 1 < n) {                                  // S_t(j) read -> refill for the Q.K^T of tile j + 1
+        for (int t = 0; ok && t < 2; ++t) {
+          if (!(ok = mbar_wait(&sh->s_read[t], j & 1, abort_flag, a.status, kDevTimeoutS))) break;
+          tc_fence_after();
+          refill(t);
+        }
+      }
       for (int hh = 0; ok && hh < ns; ++hh, ++u) {
         for (int t = 0; t < 2; ++t) {
           if (hh == 0 &&
-              !(ok = mbar_wait(&sh->p_full[t][j & 1], (j >> 1) & 1, abort_flag, a.status, kDevTimeoutP)))
+              !(ok = mbar_wait(&sh->p_full[t][pbuf(j)], pphase(j), abort_flag, a.status, kDevTimeoutP)))
             break;
           if (u > 0) {
             if (!(ok = mbar_wait(&sh->o_done[t], (u - 1) & 1, abort_flag, a.status, kDevTimeoutO))) break;
             tc_fence_after();
-            const float alpha = sh->alpha[t][j & 1][hh][rl];
+            const float alpha = sh->alpha[t][pbuf(j)][hh][rl];
             if (__any_sync(0xffffffffu, alpha != 1.f)) rescale_o(tmem + kColO + 128 * t + lane_off, alpha);
           }
           tc_fence_before();
@@ -678,7 +695,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         // warp-uniform: tcgen05.ld is a whole-warp instruction
         if (__all_sync(0xffffffffu, o_ready) && qtile * 128 < a.q_len) {
           tc_fence_after();
-          store_key_partial(a, tO, sP + 2 * t * kTile, quarter, lane, qtile, bh, bhs, ml.x, ml.y);
+          store_key_partial(a, tO, sP + kPBufs * t * kTile, quarter, lane, qtile, bh, bhs, ml.x, ml.y);
         }
       } else if (__all_sync(0xffffffffu, o_ready)) {
         tc_fence_after();

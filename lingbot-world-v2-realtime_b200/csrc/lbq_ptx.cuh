@@ -129,6 +129,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (status) atomicCAS(status, 0, code);
   return false;
 }
+#ifndef LBQ_ROLE_SLEEP_NS
+#define LBQ_ROLE_SLEEP_NS 64
+#endif
+// mbar_wait for the producer and issuer warps, which share their SM sub-partition with softmax warps:
+// between polls the warp sleeps LBQ_ROLE_SLEEP_NS, so that its polling does not take their issue slots.
+__device__ __forceinline__ bool mbar_wait_role(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                               int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1; i < LBQ_SPIN_LIMIT; ++i) {
+#if LBQ_ROLE_SLEEP_NS > 0
+    __nanosleep(LBQ_ROLE_SLEEP_NS);
+#endif
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if ((i & 255) == 0 && globaltimer_ns() - t0 > LBQ_WAIT_LIMIT_NS) break;
+  }
+  *abort_flag = 1;
+  if (status) atomicCAS(status, 0, code);
+  return false;
+}
 // Bounded wait used while draining after an abort (ignores the abort flag).
 __device__ __forceinline__ void mbar_drain_wait(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
