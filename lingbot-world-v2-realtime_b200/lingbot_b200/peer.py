@@ -23,6 +23,19 @@ def _round_up(x, m):
     return (x + m - 1) // m * m
 
 
+def exchange_records(record, group=None):
+    """Every rank's (IPC handle bytes, offset, heap bytes) in rank order, through one all_gather_object of
+    the process group (the only collective of the split's set-up). All ranks must pass the same heap
+    size; a rank that never joins makes the call fail with the process group's timeout, not hang."""
+    world = dist.get_world_size(group)
+    everyone = [None] * world
+    dist.all_gather_object(everyone, record, group=group)
+    for p, (_, _, n) in enumerate(everyone):
+        if n != record[2]:
+            raise ValueError(f"rank {p} allocated a {n}-byte heap, this rank {record[2]}")
+    return everyone
+
+
 class PeerHeap:
     """`nbytes` of device memory on this rank, mapped by every rank of `group` (all ranks pass the same
     size and carve identically). With one rank (or no process group) nothing is exported."""
@@ -42,11 +55,8 @@ class PeerHeap:
             handle = (ctypes.c_char * 64)()
             off = ctypes.c_uint64(0)
             _lib.call("lbq_peer_export", ctypes.c_void_p(self.buf.data_ptr()), handle, ctypes.byref(off))
-            everyone = [None] * self.world
-            dist.all_gather_object(everyone, (bytes(handle), off.value, self.nbytes), group=group)
+            everyone = exchange_records((bytes(handle), off.value, self.nbytes), group)
             for p, (h, o, n) in enumerate(everyone):
-                if n != self.nbytes:
-                    raise ValueError(f"rank {p} allocated a {n}-byte heap, this rank {self.nbytes}")
                 if p == self.rank:
                     continue
                 base = ctypes.c_void_p()

@@ -1,12 +1,19 @@
 """Sequence split of the DiT's self-attention across GPUs — replaces the head/token split of
 lingbot/parallel/split_dit.py:366-445 and the head-divisibility rule of lingbot/parallel/config.py:13-17.
 
-The reference splits attention heads across cards (Ulysses), so its degree must divide the 12 heads,
-which 8 GPUs do not. Here every rank keeps all heads and a 128-row slice of the chunk's queries: query
-rows are independent given the full key window. Projections are token-sharded, so each rank holds a
-contiguous share of the current chunk's K/V; `gather_tokens` all-gathers it (NCCL over NVLink on the
-GPU, gloo on the CPU) into the rank's replica of the cache. The memory part of the window is already
-replicated on every rank: it was gathered when it was the current chunk.
+The reference splits attention heads across cards, so its degree must divide the 12 heads, which 8 GPUs
+do not. Here every rank keeps all heads. Projections are token-sharded in whole 128-token tiles
+(`share_part`), so each rank holds a contiguous share of the current chunk's q/k/v.
+
+* `SplitAttention` (query split): rank r attends its own query rows against the whole window. The
+  memory part of the window is replicated on every rank (it was replicated when it was the current
+  chunk); the chunk's per-channel statistics and quantized codes cross NVLink as peer-memory stores
+  into the other ranks' buffers (`peer.PeerHeap`, csrc/peer.cu), with no collective on the data path.
+* `KeySplitAttention` (key-range split): rank r quantizes and attends only its tiles of the window for
+  every query row, and the partial outputs go to the owners of the rows, which merge them.
+
+The process group serves only the set-up (the exchange of the peer heaps' IPC handles, `peer.PeerHeap`)
+and barriers between calls.
 """
 from __future__ import annotations
 
@@ -52,28 +59,6 @@ def token_part(n, world):
     return -(-n // world)
 
 
-def token_shard(n, world, rank):
-    """Rank `rank`'s contiguous token share [lo, hi) of a chunk of n tokens."""
-    part = token_part(n, world)
-    lo = min(n, rank * part)
-    return lo, min(n, lo + part)
-
-
-def gather_tokens(x_part, n, group=None, out=None):
-    """All-gather token shares [B, part, H, D] (zero-padded to `token_part(n, world)`) into the whole
-    chunk [B, n, H, D], in token order (rank-major == token order)."""
-    world = dist.get_world_size(group)
-    b, part, h, d = x_part.shape
-    if part != token_part(n, world):
-        raise ValueError(f"share of {part} tokens, expected {token_part(n, world)} for n={n}, world={world}")
-    buf = out if out is not None else torch.empty(world, b, part, h, d, dtype=x_part.dtype, device=x_part.device)
-    if dist.get_backend(group) == "nccl":
-        dist.all_gather_into_tensor(buf, x_part.contiguous(), group=group)
-    else:
-        dist.all_gather(list(buf.unbind(0)), x_part.contiguous(), group=group)
-    return buf.permute(1, 0, 2, 3, 4).reshape(b, world * part, h, d)[:, :n]
-
-
 def pad_share(x_full, world, rank, part=None):
     """This rank's zero-padded share [B, part, H, D] of a chunk [B, n, H, D] (test and bench helper);
     shares are `token_part` tokens unless `part` is given (e.g. `share_part`)."""
@@ -84,22 +69,6 @@ def pad_share(x_full, world, rank, part=None):
     share = torch.zeros(b, part, h, d, dtype=x_full.dtype, device=x_full.device)
     share[:, :hi - lo] = x_full[:, lo:hi]
     return share
-
-
-def attend_split(q_rows, cache, k_part, v_part, current_start, sink_tokens, local_attn_size,
-                 max_attention_size, n_tokens, group=None, sm_scale=None):
-    """One rank's self-attention for a chunk: gather the chunk's K/V shares, write them into this rank's
-    cache replica (kv_cache.write, which refreshes the block statistics), quantize the window and attend
-    this rank's query rows `q_rows` [B, r1-r0, H, 128]. Returns (out_rows, local_end, current_end);
-    the caller commits (kv_cache.commit) after the chunk's forward, as the reference does."""
-    from . import kv_cache
-    k = gather_tokens(k_part, n_tokens, group)
-    v = gather_tokens(v_part, n_tokens, group)
-    end, cur_end = kv_cache.write(cache, k, v, current_start, sink_tokens, local_attn_size)
-    if end > max_attention_size:
-        raise NotImplementedError("the window must start at token 0 of the cache (kv_size <= max_attention_size)")
-    out = kv_cache.attend(q_rows, cache, end - n_tokens, end, sm_scale=sm_scale)
-    return out, end, cur_end
 
 
 def share_part(n, world, align=Q_ALIGN):
