@@ -401,10 +401,46 @@ def run_ours(args, world, rank, local):
                 "kernel": "attn_fwd_kernel", "peak_source": f"2 x bf16_tflops_sustained ({peak_src}); the "
                 "INT8/FP8 dense tensor rate of B200 is twice its bf16 rate",
                 "frac_of_nominal_4500": round(achieved / 4500.0, 4), "attn_ms_per_call": round(attn_ms, 4)}
+    check = verify_output(chunk, world)
     if args.timeline:
         write_timeline(chunk, args.timeline, world, rank)
     e2e = None if args.no_e2e else run_e2e(chunk, args, world)
-    return dict(tops=tops, ms=ms, roofline=roofline, clocks=clk.summary(), launches=launches, e2e=e2e)
+    return dict(tops=tops, ms=ms, roofline=roofline, clocks=clk.summary(), launches=launches, e2e=e2e, check=check)
+
+
+def verify_output(chunk, world, heads=(0, 11), min_cos=0.998):
+    """After the timed region: one persisting call of layer 0 (its graph when captured), then this rank's
+    output rows of two heads against fp32 attention computed by torch on the GPU from the same bf16
+    q and window. A wrong kernel stops the bench here (RuntimeError) instead of printing a number.
+    Sage's own cosine against fp32 on these inputs is ~0.9992 (the reference's record)."""
+    torch.cuda.synchronize()
+    barrier(world)
+    if chunk.graphs is not None:
+        chunk.graphs[(0, 0, True)][0].replay()
+    else:
+        chunk.call(0, persist=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    c = chunk.caches[0]
+    q = chunk.q[0]
+    res = {}
+    for h in heads:
+        k = c["k"][0, :LK, h].float()
+        v = c["v"][0, :LK, h].float()
+        num = den = dot = 0.0
+        for r0 in range(0, q.shape[1], 1024):
+            s_ = (q[0, r0:r0 + 1024, h].float() @ k.T) * (D ** -0.5)
+            ref = torch.softmax(s_, dim=-1) @ v
+            got = chunk.out[0, r0:r0 + 1024, h].float()
+            dot += float((ref * got).sum())
+            num += float((got * got).sum())
+            den += float((ref * ref).sum())
+        res[h] = dot / (num * den) ** 0.5
+    worst = min(res.values())
+    if not worst >= min_cos:
+        raise RuntimeError(f"output check failed after the timed region: cosine {res} against fp32 attention")
+    barrier(world)
+    return {"vs_fp32_attention_cos_min": round(worst, 6), "heads": list(heads), "rows": q.shape[1]}
 
 
 def write_timeline(chunk, out_dir, world, rank):
@@ -939,6 +975,8 @@ def main():
                     else res["config"],
                     "roofline": res["roofline"], "clocks": res["clocks"], "gpu_launches": res["launches"],
                     "e2e": res["e2e"], "cpu_baseline": cpu}
+            if res.get("check") is not None:
+                line["output_check"] = res["check"]
             print(json.dumps(line), flush=True)
     finally:
         if world > 1:
