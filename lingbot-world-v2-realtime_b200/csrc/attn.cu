@@ -139,17 +139,15 @@ struct TileWalk {
   }
 };
 
-// Softmax of one 64-key tile for the calling thread's row. `sv` holds the scores as the bits of
-// 1.5*2^23 + S. Writes the e4m3 P of the 64 keys to `pw` (word w = keys 4w..4w+3, key 4w in the low
-// byte), updates `m` and `dsum`, returns alpha.
-template <bool kMasked, bool kTail>
-__device__ __forceinline__ float softmax_sub(uint32_t* sv, int valid, float c, float dq, float sm, float& m,
-                                             float& dsum, uint32_t (&pw)[16]) {
-  if constexpr (kMasked) {
+// Softmax of one 64-key tile for the calling thread's row, for the tiles the fused 128-key pass does not
+// take: a masked tile (keys >= `valid` are not in the window) or one of upstream's last two (`tail`).
+// `sv` holds the scores as the bits of 1.5*2^23 + S. Writes the e4m3 P of the 64 keys to `pw` (word w =
+// keys 4w..4w+3, key 4w in the low byte), updates `m` and `dsum`, returns alpha.
+__device__ __forceinline__ float softmax_sub(uint32_t* sv, int valid, bool tail, float c, float dq, float sm,
+                                             float& m, float& dsum, uint32_t (&pw)[16]) {
 #pragma unroll
-    for (int j = 0; j < 64; ++j)
-      if (j >= valid) sv[j] = kMaskedBits;
-  }
+  for (int j = 0; j < 64; ++j)
+    if (j >= valid) sv[j] = kMaskedBits;
   auto F = [&](int j) { return __uint_as_float(sv[j]); };
   float r0 = fmaxf(F(0), F(1)), r1 = fmaxf(F(2), F(3)), r2 = fmaxf(F(4), F(5)), r3 = fmaxf(F(6), F(7));
 #pragma unroll
@@ -160,12 +158,14 @@ __device__ __forceinline__ float softmax_sub(uint32_t* sv, int valid, float c, f
     r3 = fmax3(r3, F(j + 6), F(j + 7));
   }
   const float smax = fmax3(r0, r1, fmaxf(r2, r3)) - kMagic;       // exact integer max score
-  const float m_t = kTail ? __fmaf_rn(__fmul_rn(smax, dq), sm, -kFp8Offset) : __fmaf_rn(smax, c, -kFp8Offset);
+  // main tiles: x = fma(S, c, -m); the last two: x = fma(fl(S * dq), sm, -m). Both as S * mul, then fma.
+  const float mul = tail ? dq : 1.f, scl = tail ? sm : c;
+  const float m_t = __fmaf_rn(__fmul_rn(smax, mul), scl, -kFp8Offset);
   const float m_new = fmaxf(m, m_t);
   const float alpha = (m == m_new) ? 1.f : ex2_approx(m - m_new);
   m = m_new;
   const uint64_t negm2 = f2_pack(-m_new, -m_new), nk2 = f2_pack(-kMagic, -kMagic);
-  const uint64_t c2 = f2_pack(c, c), dq2 = f2_pack(dq, dq), sm2 = f2_pack(sm, sm);
+  const uint64_t mul2 = f2_pack(mul, mul), scl2 = f2_pack(scl, scl);
   uint64_t acc0 = f2_pack(0.f, 0.f), acc1 = acc0;
 #pragma unroll
   for (int w = 0; w < 16; ++w) {
@@ -174,22 +174,13 @@ __device__ __forceinline__ float softmax_sub(uint32_t* sv, int valid, float c, f
     for (int e = 0; e < 2; ++e) {
       const int j = 4 * w + 2 * e;
       const uint64_t s2 = f2_add(f2_pack(F(j), F(j + 1)), nk2);   // S, exact
-      const uint64_t x = kTail ? f2_fma(f2_mul(s2, dq2), sm2, negm2) : f2_fma(s2, c2, negm2);
+      const uint64_t x = f2_fma(f2_mul(s2, mul2), scl2, negm2);    // S * 1 is exact
       float x0, x1;
       f2_unpack(x, x0, x1);
-      uint64_t p;
-      if (((j >> 1) & 15) >= 16 - kPolyPairs) {
-        p = exp2_poly_x2(x0, x1);
-      } else {
-        p = f2_pack(ex2_approx(x0), ex2_approx(x1));
-      }
-      float p0, p1;
-      f2_unpack(p, p0, p1);
-      if constexpr (kMasked) {
-        if (j >= valid) p0 = 0.f;
-        if (j + 1 >= valid) p1 = 0.f;
-        p = f2_pack(p0, p1);
-      }
+      float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+      if (j >= valid) p0 = 0.f;
+      if (j + 1 >= valid) p1 = 0.f;
+      const uint64_t p = f2_pack(p0, p1);
       if (e == 0) acc0 = f2_add(acc0, p); else acc1 = f2_add(acc1, p);
       half16[e] = pack_e4m3x2(p0, p1);
     }
@@ -202,20 +193,12 @@ __device__ __forceinline__ float softmax_sub(uint32_t* sv, int valid, float c, f
   return alpha;
 }
 
-// One 64-key half of the softmax, dispatched on masking and upstream's tail arithmetic; the P words go
-// to chunks 4h..4h+3 of this row of the shared P tile (16-byte chunk c at c ^ (row & 7): the 128-byte
-// swizzle of the MMA operand).
+// One 64-key half of the softmax on the masked / tail path; the P words go to chunks 4h..4h+3 of this row
+// of the shared P tile (16-byte chunk c at c ^ (row & 7): the 128-byte swizzle of the MMA operand).
 __device__ __forceinline__ float softmax_half(uint32_t* sv, int valid, bool tail, float c, float dq, float sm,
                                               float& m, float& dsum, uint8_t* prow, int h, int rsw) {
   uint32_t pw[16];
-  float alpha;
-  if (valid == 64) {
-    alpha = tail ? softmax_sub<false, true>(sv, 64, c, dq, sm, m, dsum, pw)
-                 : softmax_sub<false, false>(sv, 64, c, dq, sm, m, dsum, pw);
-  } else {
-    alpha = tail ? softmax_sub<true, true>(sv, valid, c, dq, sm, m, dsum, pw)
-                 : softmax_sub<true, false>(sv, valid, c, dq, sm, m, dsum, pw);
-  }
+  const float alpha = softmax_sub(sv, valid, tail, c, dq, sm, m, dsum, pw);
 #pragma unroll
   for (int q = 0; q < 4; ++q)
     *reinterpret_cast<uint4*>(prow + (((4 * h + q) ^ rsw) << 4)) =
