@@ -14,8 +14,12 @@
 //   m = max(m_prev, m_t); alpha = exp2(m_prev - m); P = exp2(x) (<= 448) -> e4m3
 //   d = d * alpha + sum(P) (fp32, before rounding);  O = O * alpha + e4m3(P) . e4m3(V)
 //   out = O / d * v_scale -> bf16
-// exp2 is ex2.approx (upstream's ptx_exp2). The only difference from the sm89 kernel is that P.V
-// accumulates in fp32 in tensor memory where Sage sums each 64-key tile in fp16.
+// exp2 is ex2.approx (upstream's ptx_exp2). Differences from the sm89 kernel: P.V accumulates in fp32 in
+// tensor memory where Sage sums each 64-key tile in fp16; and in the bulk tiles (full 128-key tiles
+// other than the last two 64-key tiles) x is fma(1.5*2^23 + S, c, fl(-1.5*2^23 * c - m)) where
+// 1.5*2^23 * c < 4096 (within 2^-13 of upstream's x), and 2 of every 16 key pairs take a degree-3
+// polynomial exp2 (relative error 7.5e-5). Both can move a P across an e4m3 rounding midpoint only when it lies
+// that close to one; the masked and last two tiles, where few keys carry the row, are exact.
 //
 // CTA = two 128-row Q tiles (A, B) x one (batch, head) x one KV split, 512 threads:
 //   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B: one thread per row (= TMEM lane);
@@ -62,11 +66,9 @@ constexpr uint32_t kColS = 0, kColO = 256;
 constexpr uint32_t kRegSoftmax = 160, kRegCorrection = 120, kRegMisc = 72;
 static_assert(128 * (2 * kRegSoftmax + kRegCorrection + kRegMisc) <= kAttnThreads * 128, "register split");
 
-#ifndef LBQ_POLY_PAIRS
-#define LBQ_POLY_PAIRS 0
-#endif
-// Of every 16 key pairs, this many take the FMA-pipe polynomial exp2 instead of MUFU ex2.
-constexpr int kPolyPairs = LBQ_POLY_PAIRS;
+// In the bulk tiles, of every 16 key pairs this many take the FMA-pipe polynomial exp2 (relative error
+// 7.5e-5) instead of MUFU ex2, which is the busiest unit (measured: 2 of 16 is the fastest split).
+constexpr int kPolyPairs = 2;
 
 struct AttnShared {
   uint64_t q_full;
@@ -209,7 +211,8 @@ __device__ __forceinline__ float softmax_half(uint32_t* sv, int valid, bool tail
 // Softmax of a whole 128-key tile (two 64-key tiles, neither masked nor in upstream's tail) for the
 // calling thread's row, in two steps: tile128_max takes the maxima of both halves, tile128_exp every
 // exp2, so that the second half's max does not wait for the first half's exponentials. The arithmetic is
-// softmax_sub's on each half in turn (the second against the running max after the first). P goes to
+// softmax_sub's on each half in turn (the second against the running max after the first), with the
+// folded exp2 argument and the polynomial pairs described at the top of this file. P goes to
 // chunks 0..7 of this row of the shared P tile; tile128_exp returns the two alphas.
 __device__ __forceinline__ float2 tile128_max(const uint32_t* sv) {
   auto F = [&](int j) { return __uint_as_float(sv[j]); };
@@ -226,6 +229,15 @@ __device__ __forceinline__ float2 tile128_max(const uint32_t* sv) {
   }
   return make_float2(fmax3(r[0], r[1], fmaxf(r[2], r[3])) - kMagic, fmax3(r[4], r[5], fmaxf(r[6], r[7])) - kMagic);
 }
+// The fold (below) is taken where its argument error is small: 1.5*2^23 * c < kFoldMax bounds |b| near
+// 4096, so x is within 2^-13 of upstream's. c is uniform over a warp (one Q scale per 32 rows, one K
+// scale per 64 keys), so the choice is too.
+constexpr float kFoldMax = 4096.f;
+
+// kFold: x = fma(f, c, b) with f = 1.5*2^23 + S and b = fl(-1.5*2^23 * c - m), the exact subtraction of
+// the magic bias folded into the exp2 argument (one FFMA2 per key pair; x is within half an ulp of |b|
+// of upstream's fma(S, c, -m)). Otherwise S = f - 1.5*2^23 exactly, then x = fma(S, c, -m) as upstream.
+template <bool kFold>
 __device__ __forceinline__ float2 tile128_exp(const uint32_t* sv, float2 smax, float c0, float c1, float& m,
                                               float& dsum, uint8_t* prow, int rsw) {
   auto F = [&](int j) { return __uint_as_float(sv[j]); };
@@ -234,6 +246,7 @@ __device__ __forceinline__ float2 tile128_exp(const uint32_t* sv, float2 smax, f
   const float alpha1 = (m == m1) ? 1.f : ex2_approx(m - m1);
   const float alpha2 = (m1 == m2) ? 1.f : ex2_approx(m1 - m2);
   m = m2;
+  const float b1 = kFold ? __fmaf_rn(-kMagic, c0, -m1) : -m1, b2 = kFold ? __fmaf_rn(-kMagic, c1, -m2) : -m2;
   const uint64_t nk2 = f2_pack(-kMagic, -kMagic);
   uint64_t acc[4] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
   uint32_t pw[4];
@@ -241,12 +254,13 @@ __device__ __forceinline__ float2 tile128_exp(const uint32_t* sv, float2 smax, f
   for (int w = 0; w < 32; ++w) {
     const int hh = w >> 4;
     const uint64_t c2 = hh ? f2_pack(c1, c1) : f2_pack(c0, c0);
-    const uint64_t negm2 = hh ? f2_pack(-m2, -m2) : f2_pack(-m1, -m1);
+    const uint64_t b2x = hh ? f2_pack(b2, b2) : f2_pack(b1, b1);
     uint32_t half16[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int j = 4 * w + 2 * e;
-      const uint64_t x = f2_fma(f2_add(f2_pack(F(j), F(j + 1)), nk2), c2, negm2);
+      const uint64_t f = f2_pack(F(j), F(j + 1));
+      const uint64_t x = kFold ? f2_fma(f, c2, b2x) : f2_fma(f2_add(f, nk2), c2, b2x);
       float x0, x1;
       f2_unpack(x, x0, x1);
       uint64_t p;
@@ -588,8 +602,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const bool last1 = j == n - 1, prev1 = j == n - 2 && ns_last == 1;
       if (tv == 128 && !last1 && !prev1) {              // the bulk: both halves in one pass
         const float2 smax = tile128_max(sv);
-        const float2 al = tile128_exp(sv, smax, __fmul_rn(sm, __fmul_rn(qs, ks.x)), __fmul_rn(sm, __fmul_rn(qs, ks.y)),
-                                      m, dsum, prow, rsw);
+        const float c0 = __fmul_rn(sm, __fmul_rn(qs, ks.x)), c1 = __fmul_rn(sm, __fmul_rn(qs, ks.y));
+        const float2 al = kMagic * fmaxf(c0, c1) < kFoldMax ? tile128_exp<true>(sv, smax, c0, c1, m, dsum, prow, rsw)
+                                                            : tile128_exp<false>(sv, smax, c0, c1, m, dsum, prow, rsw);
         sh->alpha[t][pb][0][rl] = al.x;
         sh->alpha[t][pb][1][rl] = al.y;
         fence_proxy_async_smem();

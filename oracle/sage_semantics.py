@@ -161,10 +161,12 @@ def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_sca
     order with one running max (its memory tiles, then its chunk share). With `partial_fp16` each
     partial travels as fp16(O_s / d_s) with (m_s, d_s), and the merge is
     out = sum_s w_s fp16(O_s / d_s) / sum_s w_s with w_s = 2^(m_s - M) d_s.
-    With `ambiguous` (a bool tensor [B, Lq, H], set in place), a row is marked when one of its P lies
-    within EXP2_REL_ERR (relative) of an e4m3 rounding midpoint and a one-step flip of that P could move
-    the row's output by more than AMBIGUOUS_IMPACT: the e4m3 value then depends on the last bits of the
-    exp2 implementation (ex2.approx on the GPU, a correctly rounded exp2 here).
+    With `ambiguous` (a bool tensor [B, Lq, H], set in place), a row is marked when the P of the row
+    that lie within the GPU kernel's own error of an e4m3 rounding midpoint could, all flipping one e4m3
+    step the same way, move the row's output by more than AMBIGUOUS_IMPACT: their e4m3 values depend on
+    the last bits of the exp2 implementation (ex2.approx on the GPU, a correctly rounded exp2 here), and
+    outside the last two tiles also on the kernel's folded exp2 argument and polynomial exp2
+    (bulk_rel_err).
     """
     b, lq, h, d = q_codes.shape
     lk = k_codes.shape[1]
@@ -192,7 +194,7 @@ def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_sca
             for pieces in partials:
                 tiles = [(t0, min(t0 + BLK_K, hi_)) for lo, hi_ in pieces for t0 in range(lo, hi_, BLK_K)]
                 state = None
-                amb = None if ambiguous is None else torch.full((qf.shape[0],), -math.inf)
+                amb = None if ambiguous is None else torch.zeros(qf.shape[0], dtype=torch.float64)
                 for i, (t0, t1) in enumerate(tiles):
                     state = _attn_tile(qf, qs, kf, vf, k_scale[bi, hi][t0 // BLK_K], t0, t1, pv_accum, sm_log2,
                                        state, tail=i >= len(tiles) - 2, amb=amb)
@@ -210,11 +212,11 @@ def attn_from_codes(q_codes, q_scale, k_codes, k_scale, v_codes, v_scale, sm_sca
             o = acc * (1.0 / dsum)[:, None] * v_scale[bi, hi][None, :]
             out[bi, rows, hi] = o
             if ambiguous is not None:
-                # a flip of one e4m3 step 2^a (in units where the row max is 2^m_s... see _attn_tile)
-                # moves the output by at most 2^(a - M) * max|V| / D
+                # a flip of one e4m3 step 2^a (a in the log2 units of the partial's running max m_s, see
+                # _attn_tile) moves the output by at most 2^(a - M) * max|V| / D; `amb` sums 2^a
                 vmax = float(v_scale[bi, hi].max()) * V_SCALE_MAX
-                for a_log in ambs:
-                    ambiguous[bi, rows, hi] |= torch.exp2(a_log - mx) * vmax / dsum > AMBIGUOUS_IMPACT
+                total = sum(a_sum * torch.exp2(-mx.double()) for a_sum in ambs)
+                ambiguous[bi, rows, hi] |= total * vmax / dsum.double() > AMBIGUOUS_IMPACT
     return out
 
 
@@ -225,22 +227,47 @@ def _fma32(a, b, c):
 
 
 # ex2.approx.ftz.f32's relative error is about 2^-22 (2 ulp); a P within 2^-20 of an e4m3 rounding
-# midpoint (a margin of 4x) may round either way on the GPU. Such a P makes its row ambiguous when a
-# one-step flip of it could move an output by more than AMBIGUOUS_IMPACT.
+# midpoint (a margin of 4x) may round either way on the GPU. A row is ambiguous when one-step flips of
+# all such P of the row could together move an output by more than AMBIGUOUS_IMPACT (half the max-abs
+# tolerance of 2e-2, so that a row held to the tolerance keeps half of it for every other error).
 EXP2_REL_ERR = 2.0 ** -20
-AMBIGUOUS_IMPACT = 2e-3
+AMBIGUOUS_IMPACT = 1e-2
+# The GPU kernel's bulk tiles (all but the last two 64-key tiles of a pass) evaluate the exp2 argument as
+# fma(1.5*2^23 + S, c, fl(-1.5*2^23 * c - m)) where fl(1.5*2^23 * c) < FOLD_MAX (for both 64-key tiles of
+# a 128-key tile; taking the bound per 64-key tile here only widens the window), and take some keys'
+# exp2 from a degree-3 polynomial (max relative error 7.48e-5, measured on a 2e6-point grid of
+# [-0.5, 0.5], plus fp32 rounding).
+KERNEL_MAGIC = 12582912.0
+FOLD_MAX = 4096.0
+POLY_REL_ERR = 7.6e-5
 
 
-def _ambiguous_step_log2(p: torch.Tensor, m: torch.Tensor) -> torch.Tensor:
-    """Per row: the largest e4m3 step, as log2(step) + m (m: the running max P was taken against, so
-    that 2^(. - M) is the step relative to a final max M), of the P that lie within EXP2_REL_ERR
-    (relative) of a midpoint between two e4m3 values; -inf where none does."""
+def _ulp32(v: torch.Tensor) -> torch.Tensor:
+    """ulp of float32 values (0 -> the smallest normal's)."""
+    _, ex = torch.frexp(v.float().abs())
+    return torch.exp2((ex - 24).clamp(min=-149).double())
+
+
+def bulk_rel_err(x: torch.Tensor, scale: torch.Tensor, m_new: torch.Tensor) -> torch.Tensor:
+    """Bound on the relative error of the GPU kernel's P in a bulk tile, per element: ex2 or the
+    polynomial, plus ln 2 times the argument's error (one ulp of x, and where the kernel folds the
+    magic bias into the argument half an ulp of the folded constant fl(-1.5*2^23 * c - m))."""
+    fold = (torch.tensor(KERNEL_MAGIC, dtype=torch.float32) * scale.float()) < FOLD_MAX
+    b = _fma32(torch.full_like(scale, -KERNEL_MAGIC), scale, -m_new)
+    arg = torch.where(fold, 0.5 * _ulp32(b), torch.zeros_like(b, dtype=torch.float64))[:, None] + _ulp32(x)
+    return EXP2_REL_ERR + POLY_REL_ERR + math.log(2.0) * arg
+
+
+def _ambiguous_steps(p: torch.Tensor, m: torch.Tensor, rel_err=EXP2_REL_ERR) -> torch.Tensor:
+    """Per row (float64): the sum of the e4m3 steps, as 2^(log2(step) + m) (m: the running max P was
+    taken against, so that 2^(. - M) is the step relative to a final max M), of the P that lie within
+    `rel_err` (relative; a scalar or per element) of a midpoint between two e4m3 values."""
     mant, ex = torch.frexp(p)                                    # p = mant * 2^ex, mant in [0.5, 1)
     step_units = mant * 16.0                                     # p in units of the e4m3 step 2^(ex - 4)
     dist = (step_units - step_units.floor() - 0.5).abs() / step_units
-    near = (p > 0) & (dist < EXP2_REL_ERR)
-    lg = torch.where(near, (ex - 4).float() + m[:, None], torch.full_like(p, -math.inf))
-    return lg.max(dim=1).values
+    near = (p > 0) & (dist < rel_err)
+    lg = (ex - 4).double() + m.double()[:, None]
+    return torch.where(near, torch.exp2(lg), torch.zeros_like(lg)).sum(dim=1)
 
 
 def _attn_tile(qf, qs, kf, vf, ks, t0, t1, pv_accum, sm_log2, state, tail, amb=None):
@@ -265,10 +292,12 @@ def _attn_tile(qf, qs, kf, vf, ks, t0, t1, pv_accum, sm_log2, state, tail, amb=N
     m_t = _fma32(rs.max(dim=1).values, scale, neg_off.expand(r))
     m_new = torch.maximum(m, m_t)
     alpha = torch.exp2(m - m_new)
-    p = torch.exp2(_fma32(rs, scale[:, None], -m_new[:, None]))
+    x = _fma32(rs, scale[:, None], -m_new[:, None])
+    p = torch.exp2(x)
     dsum = dsum * alpha + p.sum(dim=1)
     if amb is not None:
-        torch.maximum(amb, _ambiguous_step_log2(p, m_new), out=amb)
+        rel = EXP2_REL_ERR if tail else bulk_rel_err(x, scale, m_new)
+        amb += _ambiguous_steps(p, m_new, rel)
     pq = e4m3_to_float(e4m3_rn_satfinite(p))
     if pv_accum == "fp16":
         tile_acc = torch.zeros(r, d)
