@@ -93,7 +93,9 @@ LBQ_API int lbq_quant_kv(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h
                  const float* vamax_total, int8_t* k_codes, float* k_scale, uint8_t* vt_codes,
                  void* km_out, float* v_scale, int write_totals, void* stream);
 
-/* Scratch bytes lbq_quant_qkv needs for batch x heads and kv_len tokens. */
+/* Scratch bytes lbq_quant_qkv needs for batch x heads and kv_len tokens:
+ * batch * heads * (ceil(kv_len/64) + 1) * 1536 + 64. SIZE_MAX when batch or heads is outside
+ * 1..65535, kv_len outside 1..2^30, or the size overflows. */
 LBQ_API size_t lbq_quant_qkv_workspace(int batch, int heads, int64_t kv_len);
 
 /* The whole per-call quantization of sageattn(q, k, v, "NHD") (lingbot/layers/attention.py:34):
@@ -110,8 +112,8 @@ LBQ_API int lbq_quant_qkv(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_
  * whose device memory pool is fixed and owned elsewhere (no allocation once serving starts), or an
  * FFI binding that can pass inputs and outputs but not a workspace. Same arguments and results as
  * lbq_quant_qkv without the workspace; the scratch is a 16 MiB array inside the library (one per
- * GPU that loads it, kept until exit), so a call needs batch * heads * (ceil(kv_len/64) + 1) * 1536
- * bytes <= 16 MiB (58176 keys at 12 heads, batch 1) and is rejected with LBQ_ERR_ARG beyond that.
+ * GPU that loads it, kept until exit), so a call needs lbq_quant_qkv_workspace(batch, heads, kv_len)
+ * <= 16 MiB (58176 keys at 12 heads, batch 1) and is rejected with LBQ_ERR_ARG beyond that.
  * The call allocates nothing. All calls on a device share the array: calls whose kernels overlap
  * on the GPU race. The first call on a device looks up the array's address; make it before any
  * stream capture. No counterpart in the reference (its quantizers allocate through torch). */

@@ -198,9 +198,17 @@ int lbq_quant_kv(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const 
 }
 
 size_t lbq_quant_qkv_workspace(int batch, int heads, int64_t kv_len) {
-  const int64_t nblk = (kv_len + 63) / 64;
-  const int64_t cols = int64_t(batch) * heads * 128;
-  return size_t(nblk * cols * (8 + 4) + cols * (8 + 4) + 64);
+  // SIZE_MAX for arguments no launch accepts (batch and heads index grid dimensions of at most 65535,
+  // kv_len at most 2^30) or a size that does not fit: every capacity check then rejects the call.
+  if (batch <= 0 || heads <= 0 || batch > 65535 || heads > 65535 || kv_len <= 0 || kv_len > (int64_t(1) << 30))
+    return SIZE_MAX;
+  const uint64_t nblk = uint64_t(kv_len + 63) / 64;
+  uint64_t cols, per_col, bytes;
+  if (__builtin_mul_overflow(uint64_t(batch) * uint64_t(heads), uint64_t(128), &cols) ||
+      __builtin_mul_overflow(nblk + 1, uint64_t(8 + 4), &per_col) || __builtin_mul_overflow(cols, per_col, &bytes) ||
+      __builtin_add_overflow(bytes, uint64_t(64), &bytes) || bytes > uint64_t(SIZE_MAX))
+    return SIZE_MAX;
+  return size_t(bytes);
 }
 
 int lbq_quant_qkv(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, int q_len, const void* k, int64_t sk_b,
@@ -209,6 +217,8 @@ int lbq_quant_qkv(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, int q
                   uint8_t* vt_codes, float* v_scale, void* km_out, void* workspace, size_t workspace_bytes,
                   void* stream) {
   if (kv_len <= 0 || kv_len > (int64_t(1) << 30)) return fail(LBQ_ERR_ARG, "kv_len %lld out of range", (long long)kv_len);
+  if (batch <= 0 || heads <= 0 || batch > 65535 || heads > 65535)
+    return fail(LBQ_ERR_ARG, "batch %d / heads %d out of range (1..65535)", batch, heads);
   if (workspace == nullptr || workspace_bytes < lbq_quant_qkv_workspace(batch, heads, kv_len))
     return fail(LBQ_ERR_ARG, "workspace of %zu bytes is smaller than the %zu needed", workspace_bytes,
                 lbq_quant_qkv_workspace(batch, heads, kv_len));

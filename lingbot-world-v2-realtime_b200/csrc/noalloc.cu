@@ -6,9 +6,9 @@
 // array below, so the call itself allocates nothing.
 //
 // Limits and sharing rules:
-//  * The array holds kStaticScratchBytes (16 MiB). A call needs
-//    batch * heads * (ceil(kv_len / 64) + 1) * 1536 bytes of it — e.g. up to 58176 keys at
-//    12 heads and batch 1 — and is rejected with LBQ_ERR_ARG beyond that.
+//  * The array holds kStaticScratchBytes (16 MiB). A call needs lbq_quant_qkv_workspace(batch,
+//    heads, kv_len) bytes of it, batch * heads * (ceil(kv_len / 64) + 1) * 1536 + 64 — e.g. up to
+//    58176 keys at 12 heads and batch 1 — and is rejected with LBQ_ERR_ARG beyond that.
 //  * Every GPU that loads the library keeps its own copy of the array until the process exits.
 //  * All calls on a device share that copy and it keeps the last call's contents. No part of it
 //    has to start at zero: each call writes every entry it reads before reading it. Two calls
@@ -61,8 +61,8 @@ int lbq_quant_qkv_static(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h
                          int64_t sv_h, int64_t kv_len, int batch, int heads, int8_t* q_codes, float* q_scale,
                          int8_t* k_codes, float* k_scale, uint8_t* vt_codes, float* v_scale, void* km_out,
                          void* stream) {
-  if (batch <= 0 || heads <= 0 || kv_len <= 0 || kv_len > (int64_t(1) << 30))
-    return lbq::set_error(LBQ_ERR_ARG, "batch, heads and kv_len must be positive (kv_len <= 2^30)");
+  if (batch <= 0 || heads <= 0 || batch > 65535 || heads > 65535 || kv_len <= 0 || kv_len > (int64_t(1) << 30))
+    return lbq::set_error(LBQ_ERR_ARG, "batch and heads must be in 1..65535 and kv_len in 1..2^30");
   const size_t need = lbq_quant_qkv_workspace(batch, heads, kv_len);
   if (need > kStaticScratchBytes)
     return lbq::set_error(LBQ_ERR_ARG,

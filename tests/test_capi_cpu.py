@@ -45,6 +45,19 @@ def test_argument_validation_without_a_gpu():
     assert lib.lbq_abi_version() == 100
 
 
+def test_quant_workspace_size_is_checked():
+    """lbq_quant_qkv_workspace: the documented size, and SIZE_MAX (so every capacity check rejects the
+    call) for out-of-range arguments or a size that would overflow."""
+    lib = _lib.load()
+    ws = lib.lbq_quant_qkv_workspace
+    size_max = ctypes.c_size_t(-1).value
+    assert ws(1, 12, 30160) == 1 * 12 * ((30160 + 63) // 64 + 1) * 1536 + 64
+    assert ws(1, 12, 58176) <= 16 << 20 < ws(1, 12, 58176 + 64)
+    for args in [(0, 12, 100), (1, 0, 100), (70000, 1, 100), (1, 70000, 100), (1, 12, 0), (1, 12, (1 << 30) + 1),
+                 (65535, 65535, 1 << 30)]:
+        assert ws(*args) == size_max, args
+
+
 
 def test_debug_library_exports_the_same_entry_points():
     """liblbq_debug.so (device-side index checks, LBQ_DEBUG_LIB=1) exports every declared entry point."""
