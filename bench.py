@@ -285,7 +285,7 @@ class Chunk:
         splits = ops.pick_splits(1, H, self.r1 - self.r0, LK)
         if self.splitter is not None:
             return self.splitter.launches(splits, persist)
-        return 5 + (1 if splits > 1 else 0)    # block stats, window sums, K/V codes, Q codes, attention
+        return 5 + (1 if splits > 1 else 0)    # cache write + block stats, window sums, K/V codes, Q codes, attention
 
     def call(self, layer, q=None, kv_part=None, attn_events=None, out=None, persist=True):
         """One (pass, layer): exchange the current chunk's K/V (N > 1), write it into the cache,
@@ -301,9 +301,7 @@ class Chunk:
                           persist=persist)
             return self.launches_per_call(persist)
         kcur, vcur = kv_part[0], kv_part[1]
-        c["k"][:, MEM:LK] = kcur
-        c["v"][:, MEM:LK] = vcur
-        kv_cache.refresh_stats(c, MEM, LK)
+        kv_cache.store(c, kcur, vcur, MEM)                  # cache write + block statistics, one kernel
         w = kv_cache.quantize_window(q, c, LK, self.quantizer)
         if attn_events is not None:
             attn_events[0].record()

@@ -79,6 +79,30 @@ LBQ_API int lbq_kv_window_sums(const double* ksum, const float* vamax, int batch
 LBQ_API int lbq_quant_q(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, int batch, int heads,
                 int q_len, int8_t* q_codes, float* q_scale, void* stream);
 
+/* RoPE + Q quantizer in one pass: the reference's `causal_rope_apply(q, rope)` (fp64 rotation of each
+ * channel pair, cast back to bf16; lingbot/models/lingbot_world/transformer.py:134-146, called at
+ * :212) followed by lbq_quant_q's codes of the roped rows, without the roped bf16 Q ever reaching
+ * memory. rope_cos / rope_sin: the chunk's float64 tables [B, L, 64] from causal_rope_freqs
+ * (transformer.py:53-76; the [B, L, 1, 64] tensors with the head axis dropped), element strides
+ * sr_b, sr_l (even), 16-byte aligned. */
+LBQ_API int lbq_rope_quant_q(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, const double* rope_cos,
+                             const double* rope_sin, int64_t sr_b, int64_t sr_l, int batch, int heads, int q_len,
+                             int8_t* q_codes, float* q_scale, void* stream);
+
+/* KV-cache write of one chunk with its block statistics, in one pass: stores K (roped first when
+ * rope_cos / rope_sin are given, as the reference's causal_rope_apply(k, rope) at transformer.py:213)
+ * and V at tokens [tok_begin, tok_begin + n_tokens) of the cache buffers (kv_cache.write's
+ * `kv_cache["k"][:, local_start_index:local_end_index] = k`, lingbot/layers/kv_cache.py:64-75), and
+ * recomputes the statistics rows of the 64-token blocks covering those tokens exactly as
+ * lbq_kv_block_stats(kv_len = tok_begin + n_tokens) would after the copy (earlier tokens of the first
+ * block are read back from the cache). The source must not overlap the cache. */
+LBQ_API int lbq_cache_write(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,
+                            int64_t sv_l, int64_t sv_h, const double* rope_cos, const double* rope_sin, int64_t sr_b,
+                            int64_t sr_l, void* k_cache, int64_t ck_b, int64_t ck_l, int64_t ck_h, void* v_cache,
+                            int64_t cv_b, int64_t cv_l, int64_t cv_h, int batch, int heads, int64_t kv_size,
+                            int64_t tok_begin, int64_t n_tokens, int64_t max_blocks, double* ksum, float* vamax,
+                            void* stream);
+
 /* K/V quantizer for one segment of the window: tokens [tok0, tok0 + seg_valid) of k/v become
  * segment `seg` of the code buffers (num_segments segments in total). km = bf16(ksum_total /
  * kv_len_total); K codes per 64-token block of (k - km); V codes e4m3 of v * (2.25/vamax_total).

@@ -44,6 +44,17 @@ int check_ptr(const char* name, const void* p) {
   if (!aligned16(p)) return fail(LBQ_ERR_ALIGN, "%s is not 16-byte aligned", name);
   return LBQ_OK;
 }
+// Checks a pair of [B, L, 64] float64 RoPE tables (cos, sin): both or neither given, 16-byte aligned,
+// strides even (so a thread's 4 angles load as two double2).
+int check_rope(const double* cs, const double* sn, int64_t sr_b, int64_t sr_l) {
+  if ((cs == nullptr) != (sn == nullptr)) return fail(LBQ_ERR_ARG, "rope_cos and rope_sin: give both or neither");
+  if (cs == nullptr) return LBQ_OK;
+  if (!aligned16(cs) || !aligned16(sn)) return fail(LBQ_ERR_ALIGN, "rope tables are not 16-byte aligned");
+  if (sr_b % 2 || sr_l % 2 || sr_b < 0 || sr_l < 64)
+    return fail(LBQ_ERR_ALIGN, "rope table strides (%lld, %lld) must be even, the token stride >= 64", (long long)sr_b,
+                (long long)sr_l);
+  return LBQ_OK;
+}
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -148,9 +159,52 @@ int lbq_quant_q(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, int bat
     return r;
   if (batch <= 0 || heads <= 0 || q_len <= 0) return fail(LBQ_ERR_ARG, "batch, heads and q_len must be positive");
   lbq::QuantQArgs a{static_cast<const __nv_bfloat16*>(q), sq_b, sq_l, sq_h, batch, heads, q_len,
-                    int(round_up(q_len, 128)), q_codes, q_scale};
+                    int(round_up(q_len, 128)), q_codes, q_scale, nullptr, nullptr, 0, 0};
   cudaError_t e = lbq::launch_quant_q(a, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "quant_q launch");
+}
+
+int lbq_rope_quant_q(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, const double* rope_cos,
+                     const double* rope_sin, int64_t sr_b, int64_t sr_l, int batch, int heads, int q_len,
+                     int8_t* q_codes, float* q_scale, void* stream) {
+  int r;
+  if ((r = check_act("q", q, sq_b, sq_l, sq_h)) || (r = check_ptr("q_codes", q_codes)) ||
+      (r = check_ptr("q_scale", q_scale)) || (r = check_rope(rope_cos, rope_sin, sr_b, sr_l)))
+    return r;
+  if (rope_cos == nullptr) return fail(LBQ_ERR_ARG, "rope tables are null (use lbq_quant_q for unroped Q)");
+  if (batch <= 0 || heads <= 0 || q_len <= 0) return fail(LBQ_ERR_ARG, "batch, heads and q_len must be positive");
+  lbq::QuantQArgs a{static_cast<const __nv_bfloat16*>(q), sq_b, sq_l, sq_h, batch, heads, q_len,
+                    int(round_up(q_len, 128)), q_codes, q_scale, rope_cos, rope_sin, sr_b, sr_l};
+  cudaError_t e = lbq::launch_quant_q(a, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "rope_quant_q launch");
+}
+
+int lbq_cache_write(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,
+                    int64_t sv_l, int64_t sv_h, const double* rope_cos, const double* rope_sin, int64_t sr_b,
+                    int64_t sr_l, void* k_cache, int64_t ck_b, int64_t ck_l, int64_t ck_h, void* v_cache,
+                    int64_t cv_b, int64_t cv_l, int64_t cv_h, int batch, int heads, int64_t kv_size,
+                    int64_t tok_begin, int64_t n_tokens, int64_t max_blocks, double* ksum, float* vamax,
+                    void* stream) {
+  int r;
+  if ((r = check_act("k", k, sk_b, sk_l, sk_h)) || (r = check_act("v", v, sv_b, sv_l, sv_h)) ||
+      (r = check_act("k_cache", k_cache, ck_b, ck_l, ck_h)) || (r = check_act("v_cache", v_cache, cv_b, cv_l, cv_h)) ||
+      (r = check_ptr("ksum", ksum)) || (r = check_ptr("vamax", vamax)) ||
+      (r = check_rope(rope_cos, rope_sin, sr_b, sr_l)))
+    return r;
+  if (batch <= 0 || heads <= 0 || batch > 65535 || heads > 65535)
+    return fail(LBQ_ERR_ARG, "batch %d / heads %d out of range (1..65535)", batch, heads);
+  if (n_tokens < 0 || tok_begin < 0 || tok_begin + n_tokens > kv_size)
+    return fail(LBQ_ERR_ARG, "tokens [%lld, %lld) outside the %lld-token cache", (long long)tok_begin,
+                (long long)(tok_begin + n_tokens), (long long)kv_size);
+  if (max_blocks < (kv_size + 63) / 64)
+    return fail(LBQ_ERR_ARG, "%lld stats rows for a %lld-token cache", (long long)max_blocks, (long long)kv_size);
+  if (n_tokens == 0) return LBQ_OK;
+  lbq::CacheWriteArgs a{static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), sk_b, sk_l, sk_h,
+                        sv_b, sv_l, sv_h, static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache),
+                        ck_b, ck_l, ck_h, cv_b, cv_l, cv_h, rope_cos, rope_sin, sr_b, sr_l, batch, heads, tok_begin,
+                        tok_begin + n_tokens, int(tok_begin / 64), max_blocks, ksum, vamax, lbq::device_status_ptr()};
+  cudaError_t e = lbq::launch_cache_write(a, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "cache_write launch");
 }
 
 int lbq_quant_kv_tiles(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,

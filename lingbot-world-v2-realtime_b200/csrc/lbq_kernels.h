@@ -39,6 +39,32 @@ struct QuantQArgs {
   int q_len, q_pad;
   int8_t* q_codes;            // [B][H][q_pad][128]
   float* q_scale;             // [B][H][q_pad/32]
+  const double* rope_cos;     // null: no RoPE; else [B][L][64] (strides sr_b, sr_l in elements)
+  const double* rope_sin;
+  int64_t sr_b, sr_l;
+};
+
+// Store a chunk of K/V into the cache buffer (K optionally roped) and recompute the statistics of
+// the 64-token blocks covering [tok_begin, tok_end): tokens of those blocks before tok_begin are read
+// back from the cache, tokens from tok_end on count as absent (as kv_block_stats with kv_len =
+// tok_end).
+struct CacheWriteArgs {
+  const __nv_bfloat16* k_src;   // [B][n][H][128] (token tok_begin + i at row i)
+  const __nv_bfloat16* v_src;
+  int64_t sk_b, sk_l, sk_h, sv_b, sv_l, sv_h;
+  __nv_bfloat16* k_cache;       // [B][kv_size][H][128]
+  __nv_bfloat16* v_cache;
+  int64_t ck_b, ck_l, ck_h, cv_b, cv_l, cv_h;
+  const double* rope_cos;       // null: K stored as given; else [B][n][64] for the chunk's tokens
+  const double* rope_sin;
+  int64_t sr_b, sr_l;
+  int batch, heads;
+  int64_t tok_begin, tok_end;
+  int blk_begin;
+  int64_t max_blocks;
+  double* ksum;                 // [B][max_blocks][H][128]
+  float* vamax;
+  int* status;
 };
 
 struct QuantKArgs {
@@ -221,6 +247,7 @@ struct PeerWaitArgs {
 cudaError_t launch_kv_block_stats(const KvBlockStatsArgs& a, cudaStream_t st);
 cudaError_t launch_kv_window_sums(const KvWindowSumsArgs& a, cudaStream_t st);
 cudaError_t launch_quant_q(const QuantQArgs& a, cudaStream_t st);
+cudaError_t launch_cache_write(const CacheWriteArgs& a, cudaStream_t st);
 cudaError_t launch_quant_kv(const QuantKArgs& ka, const QuantVArgs& va, int tile0, int tiles, cudaStream_t st);
 cudaError_t launch_attn(const AttnArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                         const CUtensorMap& tm_v, cudaStream_t st);

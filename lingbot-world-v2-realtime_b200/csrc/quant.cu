@@ -45,6 +45,29 @@ __device__ __forceinline__ float warp_max(float x) {
   return x;
 }
 
+// RoPE of 8 consecutive channels (4 rotation pairs) of one token in the reference's fp64 form
+// (lingbot/models/lingbot_world/transformer.py:142-146): (xr, xi) -> (xr cos - xi sin, xr sin + xi cos)
+// with every product and sum rounded in fp64 (torch evaluates the expression op by op, no fma), then
+// cast to bf16 through fp32 (torch's double -> bfloat16 conversion). cs / sn: the pairs' 4 angles.
+__device__ __forceinline__ uint4 rope_bf16x8(const uint4 raw, const double* cs, const double* sn) {
+  float f[8];
+  bf16x8_to_f32(raw, f);
+  const double2 c01 = *reinterpret_cast<const double2*>(cs), c23 = *reinterpret_cast<const double2*>(cs + 2);
+  const double2 s01 = *reinterpret_cast<const double2*>(sn), s23 = *reinterpret_cast<const double2*>(sn + 2);
+  const double c[4] = {c01.x, c01.y, c23.x, c23.y}, s[4] = {s01.x, s01.y, s23.x, s23.y};
+  uint32_t w[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const double xr = f[2 * p], xi = f[2 * p + 1];
+    const double re = __dsub_rn(__dmul_rn(xr, c[p]), __dmul_rn(xi, s[p]));
+    const double im = __dadd_rn(__dmul_rn(xr, s[p]), __dmul_rn(xi, c[p]));
+    const __nv_bfloat16 lo = __float2bfloat16_rn(__double2float_rn(re));
+    const __nv_bfloat16 hi = __float2bfloat16_rn(__double2float_rn(im));
+    w[p] = uint32_t(__bfloat16_as_ushort(lo)) | (uint32_t(__bfloat16_as_ushort(hi)) << 16);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 // ------------------------------------------------------------------ K/V block statistics
 // One CTA per (64-token block, head, batch). ksum: fp64 sum of K over the block's tokens that are
 // < kv_len; vamax: max |V|. 128 threads = 8 row groups x 16 chunks of 8 channels.
@@ -71,6 +94,71 @@ __global__ void __launch_bounds__(128) kv_block_stats_kernel(KvBlockStatsArgs a)
     }
   }
   // [row group][channel within chunk][chunk]: a warp's 16 chunks of one slot are consecutive words
+  __shared__ double sh_s[8][8][16];
+  __shared__ float sh_v[8][8][16];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    sh_s[rg][i][c16] = s[i];
+    sh_v[rg][i][c16] = vm[i];
+  }
+  __syncthreads();
+  double tot = 0.0;
+  float vmax = 0.f;
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    tot += sh_s[g][t & 7][t >> 3];
+    vmax = fmaxf(vmax, sh_v[g][t & 7][t >> 3]);
+  }
+  const int64_t o = ((int64_t(b) * a.max_blocks + blk) * a.heads + h) * 128 + t;
+  if (LBQ_CHECK(blk < a.max_blocks, a.status, kDevBadStatsRow)) {
+    a.ksum[o] = tot;
+    a.vamax[o] = vmax;
+  }
+}
+
+// ------------------------------------------------------------------ cache write + block statistics
+// One CTA per (64-token block, head, batch) over the blocks covering [tok_begin, tok_end): stores
+// the block's new tokens into the cache (K roped when the tables are given) and accumulates the
+// block's statistics in exactly kv_block_stats_kernel's order and thread layout, so the tables are
+// bit-identical to a copy followed by kv_block_stats. Tokens of the block before tok_begin are read
+// back from the cache.
+__global__ void __launch_bounds__(128) cache_write_kernel(CacheWriteArgs a) {
+  const int blk = a.blk_begin + blockIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int t = threadIdx.x, c16 = t & 15, rg = t >> 4;
+  double s[8];
+  float vm[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) { s[i] = 0.0; vm[i] = 0.f; }
+  for (int r = rg; r < 64; r += 8) {
+    const int64_t tok = int64_t(blk) * 64 + r;
+    if (tok >= a.tok_end) break;
+    __nv_bfloat16* kc = a.k_cache + b * a.ck_b + tok * a.ck_l + h * a.ck_h + c16 * 8;
+    __nv_bfloat16* vc = a.v_cache + b * a.cv_b + tok * a.cv_l + h * a.cv_h + c16 * 8;
+    uint4 kr, vr;
+    if (tok < a.tok_begin) {
+      kr = *reinterpret_cast<const uint4*>(kc);
+      vr = *reinterpret_cast<const uint4*>(vc);
+    } else {
+      const int64_t i = tok - a.tok_begin;
+      kr = *reinterpret_cast<const uint4*>(a.k_src + b * a.sk_b + i * a.sk_l + h * a.sk_h + c16 * 8);
+      vr = *reinterpret_cast<const uint4*>(a.v_src + b * a.sv_b + i * a.sv_l + h * a.sv_h + c16 * 8);
+      if (a.rope_cos != nullptr) {
+        const int64_t o = b * a.sr_b + i * a.sr_l + c16 * 4;
+        kr = rope_bf16x8(kr, a.rope_cos + o, a.rope_sin + o);
+      }
+      *reinterpret_cast<uint4*>(kc) = kr;
+      *reinterpret_cast<uint4*>(vc) = vr;
+    }
+    float kf[8], vf[8];
+    bf16x8_to_f32(kr, kf);
+    bf16x8_to_f32(vr, vf);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      s[i] += double(kf[i]);
+      vm[i] = fmaxf(vm[i], fabsf(vf[i]));
+    }
+  }
   __shared__ double sh_s[8][8][16];
   __shared__ float sh_v[8][8][16];
 #pragma unroll
@@ -145,6 +233,16 @@ __global__ void __launch_bounds__(256) quant_q_kernel(QuantQArgs a) {
     raw[i] = row < a.q_len
                  ? *reinterpret_cast<const uint4*>(a.q + b * a.sq_b + int64_t(row) * a.sq_l + h * a.sq_h + c16 * 8)
                  : make_uint4(0u, 0u, 0u, 0u);
+  }
+  if (a.rope_cos != nullptr) {                  // roped Q: the reference's causal_rope_apply, fused
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int row = row0 + 2 * i + (l >> 4);
+      if (row < a.q_len) {
+        const int64_t o = b * a.sr_b + int64_t(row) * a.sr_l + c16 * 4;
+        raw[i] = rope_bf16x8(raw[i], a.rope_cos + o, a.rope_sin + o);
+      }
+    }
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -336,6 +434,14 @@ cudaError_t launch_quant_q(const QuantQArgs& a, cudaStream_t st) {
   dim3 grid(a.q_pad / 128, a.heads, a.batch);
   if (cudaError_t e0 = prefer_max_shared<quant_q_kernel>(); e0 != cudaSuccess) return e0;
   quant_q_kernel<<<grid, 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t launch_cache_write(const CacheWriteArgs& a, cudaStream_t st) {
+  const int blk_end = int((a.tok_end + 63) / 64);
+  if (blk_end <= a.blk_begin) return cudaSuccess;
+  dim3 grid(blk_end - a.blk_begin, a.heads, a.batch);
+  if (cudaError_t e0 = prefer_max_shared<cache_write_kernel>(); e0 != cudaSuccess) return e0;
+  cache_write_kernel<<<grid, 128, 0, st>>>(a);
   return cudaGetLastError();
 }
 // `tiles` 128-token tiles from tile0, stopping at the last tile holding valid tokens: a short last

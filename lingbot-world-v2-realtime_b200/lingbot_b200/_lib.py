@@ -23,6 +23,10 @@ SIGNATURES = {
                                   _i64, _vp, _vp, _vp]),
     "lbq_kv_window_sums": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _i64, _vp, _vp, _vp]),
     "lbq_quant_q": (_i32, [_vp, _i64, _i64, _i64, _i32, _i32, _i32, _vp, _vp, _vp]),
+    "lbq_rope_quant_q": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _vp, _vp, _vp]),
+    "lbq_cache_write": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _i64,
+                               _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _i32, _i64, _i64, _i64, _i64,
+                               _vp, _vp, _vp]),
     "lbq_quant_kv": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _i32, _i64, _i32, _i32, _i32, _i32,
                             _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp]),
     "lbq_quant_qkv_workspace": (_sz, [_i32, _i32, _i64]),

@@ -115,13 +115,51 @@ def evict(kv_cache, sink_tokens, evicted, rolled):
     refresh_stats(kv_cache, sink_tokens, sink_tokens + rolled)
 
 
-def write(kv_cache, k, v, current_start, sink_tokens, local_attn_size):
+def _rope_args(rope):
+    """(cos, sin) float64 tables [B, L, 64] (or the reference's [B, L, 1, 64]) -> C-ABI arguments."""
+    if rope is None:
+        return None, None, 0, 0
+    cos, sin = rope
+    if cos.dim() == 4:
+        cos, sin = cos[:, :, 0], sin[:, :, 0]
+    for t in (cos, sin):
+        if t.dtype != torch.float64 or not t.is_cuda or t.stride(-1) != 1 or t.shape[-1] != 64:
+            raise ValueError("rope tables must be CUDA float64 [B, L, 64] with unit last stride")
+    if cos.stride() != sin.stride():
+        raise ValueError("rope cos and sin tables must share strides")
+    return ops._ptr(cos), ops._ptr(sin), cos.stride(0), cos.stride(1)
+
+
+def store(kv_cache, k, v, tok_begin, rope=None):
+    """Store K/V at tokens [tok_begin, tok_begin + n) of the cache buffers and refresh the statistics
+    of the blocks they touch, in one kernel (lbq_cache_write); with `rope` = the chunk's (cos, sin)
+    tables, K is roped on the way (the reference ropes it before kv_cache.write,
+    transformer.py:213-219)."""
+    kc, vc = kv_cache["k"], kv_cache["v"]
+    if "lbq_ksum" not in kv_cache:
+        kv_cache["lbq_ksum"], kv_cache["lbq_vamax"] = _stats_tables(tuple(kc.shape), kc.device)
+    b, n, h, _ = k.shape
+    ksum, vamax = kv_cache["lbq_ksum"], kv_cache["lbq_vamax"]
+    rc, rs, sr_b, sr_l = _rope_args(rope)
+    _lib.call("lbq_cache_write", ops._ptr(k), *k.stride()[:3], ops._ptr(v), *v.stride()[:3], rc, rs, sr_b, sr_l,
+              ops._ptr(kc), *kc.stride()[:3], ops._ptr(vc), *vc.stride()[:3], b, h, kc.shape[1], tok_begin, n,
+              ksum.shape[1], ops._ptr(ksum), ops._ptr(vamax), ops._stream())
+
+
+def write(kv_cache, k, v, current_start, sink_tokens, local_attn_size, rope=None):
     """Store this forward's K/V, evicting the oldest non-sink tokens when the window is full
-    (kv_cache.py:64-75). Returns (local_end_index, current_end)."""
+    (kv_cache.py:64-75). Returns (local_end_index, current_end). On the GPU the store and the block
+    statistics are one kernel (`store`); `rope` (optional, GPU only) ropes K in that kernel, for a
+    caller that would otherwise pass causal_rope_apply(k, rope)."""
     evicted, rolled, local_start_index, local_end_index, current_end = plan(
         kv_cache, k.shape[1], current_start, sink_tokens, local_attn_size)
     if evicted:
         evict(kv_cache, sink_tokens, evicted, rolled)
+    if kv_cache["k"].is_cuda:
+        store(kv_cache, k, v, local_start_index, rope)
+        return local_end_index, current_end
+    if rope is not None:
+        raise ValueError("rope inside write is a GPU kernel; rope K on the host first")
     kv_cache["k"][:, local_start_index:local_end_index] = k
     kv_cache["v"][:, local_start_index:local_end_index] = v
     refresh_stats(kv_cache, local_start_index, local_end_index)
@@ -162,9 +200,10 @@ class WindowQuantizer:
 _default_quantizer = WindowQuantizer()
 
 
-def quantize_window(q, kv_cache, end, quantizer=None) -> ops.QuantWindow:
+def quantize_window(q, kv_cache, end, quantizer=None, rope=None) -> ops.QuantWindow:
     """Quantize q and the cache window [0, end) with the cached block statistics
-    (lbq_requant_cache + lbq_quant_q)."""
+    (lbq_requant_cache + lbq_quant_q; with `rope` = the chunk's (cos, sin) tables, q is roped in the
+    Q quantizer, lbq_rope_quant_q)."""
     k, v = kv_cache["k"], kv_cache["v"]
     ops._check_act("q", q)
     b, lq, h, _ = q.shape
@@ -174,14 +213,21 @@ def quantize_window(q, kv_cache, end, quantizer=None) -> ops.QuantWindow:
     _lib.call("lbq_requant_cache", ops._ptr(k), *k.stride()[:3], ops._ptr(v), *v.stride()[:3], b, h, end,
               ksum.shape[1], ops._ptr(ksum), ops._ptr(vamax), ops._ptr(qz.sums), ops._ptr(qz.k_codes),
               ops._ptr(qz.k_scale), ops._ptr(qz.vt_codes), ops._ptr(qz.v_scale), ops._ptr(qz.km), st)
-    _lib.call("lbq_quant_q", ops._ptr(q), *q.stride()[:3], b, h, lq, ops._ptr(qz.q_codes), ops._ptr(qz.q_scale), st)
+    if rope is None:
+        _lib.call("lbq_quant_q", ops._ptr(q), *q.stride()[:3], b, h, lq, ops._ptr(qz.q_codes), ops._ptr(qz.q_scale),
+                  st)
+    else:
+        rc, rs, sr_b, sr_l = _rope_args(rope)
+        _lib.call("lbq_rope_quant_q", ops._ptr(q), *q.stride()[:3], rc, rs, sr_b, sr_l, b, h, lq,
+                  ops._ptr(qz.q_codes), ops._ptr(qz.q_scale), st)
     return ops.QuantWindow(qz.q_codes, qz.q_scale, qz.k_codes, qz.k_scale, qz.vt_codes, qz.v_scale, qz.km, lq, end,
                            end, 1)
 
 
-def attend(q, kv_cache, start, end, sm_scale=None, num_splits=None, out=None, quantizer=None):
+def attend(q, kv_cache, start, end, sm_scale=None, num_splits=None, out=None, quantizer=None, rope=None):
     """`sageattn(q, k_win, v_win, "NHD")` with the window [0, end) of `kv_cache`, whose tokens
     [start, end) were written by this forward — the role of sage_preq.attend (sage_preq.py:107-128).
-    `start` is accepted for signature parity; the statistics were refreshed by `write`."""
-    w = quantize_window(q, kv_cache, end, quantizer)
+    `start` is accepted for signature parity; the statistics were refreshed by `write`. With `rope`,
+    q is the un-roped query and is roped in the Q quantizer."""
+    w = quantize_window(q, kv_cache, end, quantizer, rope)
     return ops.attn_from_codes(w, sm_scale=sm_scale, out=out, num_splits=num_splits)

@@ -11,6 +11,11 @@ What it records:
     blocks after subtracting km = k.mean over the window) and `_quant_v_fp8` (V: per-channel e4m3 in
     Sage's permuted [B, D, H, n] layout, amax = max |v| over the window, no margin), exactly as
     `lingbot/layers/sage_preq.py:115-124` drives Sage's quantizers per call.
+  * rope_grid2x4x6.npz — the reference's RoPE: its `rope_params` table
+    (reference/wan/modules/model.py:29-36) as the DiT builds it (lingbot/models/lingbot_world/
+    transformer.py:553-558), `causal_rope_freqs` for a two-sample batch (transformer.py:53-76) and
+    `causal_rope_apply` of a bf16 input (transformer.py:134-146). transformer.py itself imports
+    diffusers and the Wan model, so the three functions are taken from its source text and run alone.
   * kv_schedule.json — the host bookkeeping of `lingbot/layers/kv_cache.py` (plan/evict/write/
     window/commit) over the write / rewrite / eviction schedule of
     `experiments/bench_attn/sage_preq_check.py:11-36`, with float64 (order-independent) checksums of the cache buffers after
@@ -32,6 +37,38 @@ def load(path, name):
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
     return mod
+
+
+def load_functions(path, names, env):
+    """The named top-level functions of a source file, compiled on their own into `env`."""
+    import ast
+    src = open(path).read()
+    tree = ast.parse(src)
+    for node in tree.body:
+        if isinstance(node, ast.FunctionDef) and node.name in names:
+            exec(compile(ast.Module(body=[node], type_ignores=[]), path, "exec"), env)
+    missing = [n for n in names if n not in env]
+    assert not missing, missing
+    return env
+
+
+def rope_golden(ref):
+    env = {"torch": torch, "_ROPE_FP32C": False}
+    load_functions(os.path.join(ref, "reference/wan/modules/model.py"), ["rope_params"], env)
+    load_functions(os.path.join(ref, "lingbot/models/lingbot_world/transformer.py"),
+                   ["causal_rope_freqs", "causal_rope_apply"], env)
+    d = 128
+    freqs = torch.view_as_real(torch.cat([env["rope_params"](1024, d - 4 * (d // 6)),
+                                          env["rope_params"](1024, 2 * (d // 6)),
+                                          env["rope_params"](1024, 2 * (d // 6))], dim=1))
+    grid = [(2, 4, 6), (2, 4, 6)]
+    cos, sin = env["causal_rope_freqs"](grid, freqs, start_frame=5)          # [B, L, 1, 64] each
+    g = torch.Generator().manual_seed(77)
+    x = (torch.randn(2, 48, 2, d, generator=g) * 2.0).bfloat16()
+    out = env["causal_rope_apply"](x, (cos, sin))
+    # the first 16 positions of the table cover every frame, row and column used here
+    return dict(freqs16=freqs[:16].numpy(), grid=np.array(grid), start_frame=np.array(5),
+                cos=cos[:, :, 0].numpy(), sin=sin[:, :, 0].numpy(), x=bf16_bits(x), out=bf16_bits(out))
 
 
 def bf16_bits(x):
@@ -129,6 +166,8 @@ def main():
                                         k_offset_std=koff, outlier=outlier)))
         np.savez_compressed(os.path.join(HERE, f"quant_{name}.npz"), meta=meta, **out)
         print("wrote", name)
+    np.savez_compressed(os.path.join(HERE, "rope_grid2x4x6.npz"), **rope_golden(args.ref))
+    print("wrote rope_grid2x4x6.npz")
     with open(os.path.join(HERE, "kv_schedule.json"), "w") as f:
         json.dump(kv_schedule(kvc), f, indent=1)
     print("wrote kv_schedule.json")
