@@ -403,7 +403,50 @@ def run_ours(args, world, rank, local):
     if args.timeline:
         write_timeline(chunk, args.timeline, world, rank)
     e2e = None if args.no_e2e else run_e2e(chunk, args, world)
+    if e2e is not None and world == 1:
+        e2e["plugin"] = run_plugin(args, chunk.dev)
     return dict(tops=tops, ms=ms, roofline=roofline, clocks=clk.summary(), launches=launches, e2e=e2e, check=check)
+
+
+def run_plugin(args, dev, calls=10):
+    """The reference-facing operator itself: `attention(q, k, v)` (lingbot_b200.attention, the custom op
+    lbq::sage_attn) on one (pass, layer)'s q and full bf16 window, as the reference's DiT calls
+    `attention()` when it does not use the cache-aware path: quantize the whole window and attend, every
+    call, with its buffers from the caching allocator. Timed with the inputs resident on the GPU, and
+    again with each call's q, k, v copied from pinned host memory and its output read back."""
+    from lingbot_b200.attention import attention
+    g = torch.Generator(device=dev).manual_seed(99)
+    q = torch.randn(1, LQ, H, D, generator=g, device=dev).bfloat16()
+    k = (torch.randn(1, LK, H, D, generator=g, device=dev) + 3 * torch.randn(1, 1, H, D, generator=g, device=dev)).bfloat16()
+    v = torch.randn(1, LK, H, D, generator=g, device=dev).bfloat16()
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    hout = torch.empty(1, LQ, H, D, dtype=torch.bfloat16).pin_memory()
+    flops = 4.0 * LQ * LK * H * D
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(calls):
+            fn()
+        t1.record()
+        torch.cuda.synchronize()
+        return t0.elapsed_time(t1) / calls
+
+    ms_res = timed(lambda: attention(q, k, v))
+
+    def host_call():
+        dq, dk, dv = (x.to(dev, non_blocking=True) for x in (hq, hk, hv))
+        hout.copy_(attention(dq, dk, dv), non_blocking=True)
+    ms_host = timed(host_call)
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
+    return {"call": f"attention(q, k, v): q {LQ} x kv {LK} x {H} heads, bf16, quantize + attend per call",
+            "value": round(flops / (ms_res * 1e-3) / 1e12, 2), "unit": "TOPS", "ms_per_call": round(ms_res, 4),
+            "host_buffers": {"value": round(flops / (ms_host * 1e-3) / 1e12, 2), "unit": "TOPS",
+                             "ms_per_call": round(ms_host, 4), "h2d_bytes_per_call": int(h2d),
+                             "d2h_bytes_per_call": int(hout.numel() * 2)}}
 
 
 def verify_output(chunk, world, heads=(0, 11), min_cos=0.998):

@@ -41,7 +41,13 @@ extern "C" {
 #define LBQ_ERR_ARG 1          /* bad shape, stride, length or null pointer */
 #define LBQ_ERR_ALIGN 2        /* pointer or stride not 16-byte aligned */
 #define LBQ_ERR_CUDA 3         /* CUDA runtime / driver error (launch, tensor map) */
-#define LBQ_ERR_UNSUPPORTED 4  /* head_dim != 128, causal, ... */
+#define LBQ_ERR_UNSUPPORTED 4  /* causal attention in the quantized kernel */
+
+/* Activation types of the drop-in path (lbq_quant_qkv, lbq_quant_qkv_static, lbq_attn_fwd,
+ * lbq_splitkv_combine): the `dtype` the reference's attention() casts q/k/v to before Sage
+ * (lingbot/layers/attention.py:30,34). The other entries take bf16. */
+#define LBQ_DTYPE_BF16 0
+#define LBQ_DTYPE_F16 1
 
 /* Version of this ABI (major * 100 + minor). */
 LBQ_API int lbq_abi_version(void);
@@ -130,7 +136,7 @@ LBQ_API int lbq_quant_qkv(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_
                   const void* v, int64_t sv_b, int64_t sv_l, int64_t sv_h, int64_t kv_len,
                   int batch, int heads, int8_t* q_codes, float* q_scale, int8_t* k_codes,
                   float* k_scale, uint8_t* vt_codes, float* v_scale, void* km_out,
-                  void* workspace, size_t workspace_bytes, void* stream);
+                  void* workspace, size_t workspace_bytes, int dtype, void* stream);
 
 /* lbq_quant_qkv for callers that cannot give this library device memory: an embedding runtime
  * whose device memory pool is fixed and owned elsewhere (no allocation once serving starts), or an
@@ -146,7 +152,7 @@ LBQ_API int lbq_quant_qkv_static(const void* q, int64_t sq_b, int64_t sq_l, int6
                                  const void* v, int64_t sv_b, int64_t sv_l, int64_t sv_h, int64_t kv_len,
                                  int batch, int heads, int8_t* q_codes, float* q_scale, int8_t* k_codes,
                                  float* k_scale, uint8_t* vt_codes, float* v_scale, void* km_out,
-                                 void* stream);
+                                 int dtype, void* stream);
 
 /* Re-quantize a bf16 KV cache window [0, kv_len) whose block statistics are current (kept by
  * lbq_kv_block_stats on every write): window sums + K/V codes, one segment, in 3 launches.
@@ -160,8 +166,10 @@ LBQ_API int lbq_requant_cache(const void* k, int64_t sk_b, int64_t sk_l, int64_t
                       int8_t* k_codes, float* k_scale, uint8_t* vt_codes, float* v_scale,
                       void* km_out, void* stream);
 
-/* Attention over quantized codes (non-causal). out [B, q_len, H, 128] bf16 with element strides
- * so_*. sm_scale <= 0 means 1/sqrt(128). num_splits > 1 splits the key range (flash-decoding):
+/* Attention over quantized codes. out [B, q_len, H, 128] in `dtype` (LBQ_DTYPE_BF16 or _F16) with
+ * element strides so_*. sm_scale <= 0 means 1/sqrt(128). is_causal != 0 returns LBQ_ERR_UNSUPPORTED:
+ * the kernel has no causal mask (the drop-in attention() sends causal calls to the reference's
+ * non-Sage branch instead; the DiT never makes one). num_splits > 1 splits the key range (flash-decoding):
  * partial results go to o_part (f32, [splits][B*H][q_pad][128]) and ml_part (f32 pairs,
  * [splits][B*H][q_pad]) and lbq_splitkv_combine finishes them; num_splits is clamped so that no
  * split is empty (the value used is written to *splits_used when non-null).
@@ -172,9 +180,9 @@ LBQ_API int lbq_requant_cache(const void* k, int64_t sk_b, int64_t sk_l, int64_t
 LBQ_API int lbq_attn_fwd(const int8_t* q_codes, const float* q_scale, int q_len,
                  const int8_t* k_codes, const float* k_scale, const uint8_t* vt_codes,
                  const float* v_scale, int64_t kv_len, int num_segments, int seg_len,
-                 int batch, int heads, float sm_scale, void* out, int64_t so_b, int64_t so_l,
-                 int64_t so_h, int num_splits, float* o_part, float* ml_part, int* splits_used,
-                 void* stream);
+                 int batch, int heads, float sm_scale, int is_causal, void* out, int64_t so_b,
+                 int64_t so_l, int64_t so_h, int num_splits, float* o_part, float* ml_part,
+                 int* splits_used, int dtype, void* stream);
 
 /* lbq_quant_kv restricted to the 128-token tiles [tile_begin, tile_end) of the segment (those holding
  * valid tokens: tile_end <= ceil(seg_valid / 128)); segment token t reads source token tok0 + t, and
@@ -216,11 +224,11 @@ LBQ_API int lbq_keys_combine(const void* recv_o, const float* recv_ml, int nrank
                      const float* v_scale, int batch, int heads, void* out, int64_t so_b,
                      int64_t so_l, int64_t so_h, void* stream);
 
-/* Flash-decoding merge of lbq_attn_fwd's split partials into out (bf16), applying the V scale.
+/* Flash-decoding merge of lbq_attn_fwd's split partials into out (in `dtype`), applying the V scale.
  * The combine kernel of experiments/bench_attn/splitkv/README.md:67-69 (`splitkv_combine_kernel`). */
 LBQ_API int lbq_splitkv_combine(const float* o_part, const float* ml_part, int num_splits,
                         const float* v_scale, int batch, int heads, int q_len, void* out,
-                        int64_t so_b, int64_t so_l, int64_t so_h, void* stream);
+                        int64_t so_b, int64_t so_l, int64_t so_h, int dtype, void* stream);
 
 /* ---------------------------------------------------------------- sequence split over peer memory
  * The ranks of one node share a "peer heap": a device buffer per rank, mapped into every other

@@ -711,8 +711,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             for (int e = 0; e < 16; ++e) {
               const float o0 = __fmul_rn(__fmul_rn(__uint_as_float(ov[2 * e]), rd), vs[32 * c + 2 * e]);
               const float o1 = __fmul_rn(__fmul_rn(__uint_as_float(ov[2 * e + 1]), rd), vs[32 * c + 2 * e + 1]);
-              const __nv_bfloat162 pr = __floats2bfloat162_rn(o0, o1);
-              packed[e] = *reinterpret_cast<const uint32_t*>(&pr);
+              packed[e] = pack_act2(o0, o1, a.dtype);
             }
             if (row < a.q_len) {
 #pragma unroll
@@ -776,11 +775,9 @@ __global__ void __launch_bounds__(128) splitkv_combine_kernel(const CombineArgs 
   const float rl = __frcp_rn(L);
   const float4 vs = reinterpret_cast<const float4*>(a.v_scale + int64_t(bh) * 128)[lane];
   const int b = bh / a.heads, h = bh - b * a.heads;
-  const __nv_bfloat162 p0 = __floats2bfloat162_rn(o.x * rl * vs.x, o.y * rl * vs.y);
-  const __nv_bfloat162 p1 = __floats2bfloat162_rn(o.z * rl * vs.z, o.w * rl * vs.w);
   uint2 st;
-  st.x = *reinterpret_cast<const uint32_t*>(&p0);
-  st.y = *reinterpret_cast<const uint32_t*>(&p1);
+  st.x = pack_act2(o.x * rl * vs.x, o.y * rl * vs.y, a.dtype);
+  st.y = pack_act2(o.z * rl * vs.z, o.w * rl * vs.w, a.dtype);
   *reinterpret_cast<uint2*>(a.out + b * a.so_b + int64_t(row) * a.so_l + h * a.so_h + lane * 4) = st;
 }
 

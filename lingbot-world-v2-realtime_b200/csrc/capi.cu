@@ -99,7 +99,7 @@ int set_error(int code, const char* fmt, ...) {
 
 extern "C" {
 
-int lbq_abi_version(void) { return 100; }
+int lbq_abi_version(void) { return 101; }
 
 const char* lbq_last_error(void) { return g_err; }
 
@@ -118,9 +118,11 @@ int lbq_device_status(int clear, int* status_out) {
   return LBQ_OK;
 }
 
-int lbq_kv_block_stats(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,
-                       int64_t sv_l, int64_t sv_h, int batch, int heads, int64_t kv_len, int blk_begin, int blk_end,
-                       int64_t max_blocks, double* ksum, float* vamax, void* stream) {
+// The entries below with a `dtype` argument (0: bf16, 1: fp16 activations) are the bodies of the
+// public bf16 entries; lbq_quant_qkv passes the caller's dtype through them.
+static int kv_block_stats_dt(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,
+                             int64_t sv_l, int64_t sv_h, int batch, int heads, int64_t kv_len, int blk_begin,
+                             int blk_end, int64_t max_blocks, double* ksum, float* vamax, int dtype, void* stream) {
   int r;
   if ((r = check_act("k", k, sk_b, sk_l, sk_h)) || (r = check_act("v", v, sv_b, sv_l, sv_h))) return r;
   if ((r = check_ptr("ksum", ksum)) || (r = check_ptr("vamax", vamax))) return r;
@@ -131,9 +133,16 @@ int lbq_kv_block_stats(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, 
   if (blk_end <= blk_begin) return LBQ_OK;
   lbq::KvBlockStatsArgs a{static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v),
                           sk_b, sk_l, sk_h, sv_b, sv_l, sv_h, batch, heads, kv_len, blk_begin, blk_end,
-                          max_blocks, ksum, vamax, lbq::device_status_ptr()};
+                          max_blocks, ksum, vamax, lbq::device_status_ptr(), dtype};
   cudaError_t e = lbq::launch_kv_block_stats(a, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "kv_block_stats launch");
+}
+
+int lbq_kv_block_stats(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,
+                       int64_t sv_l, int64_t sv_h, int batch, int heads, int64_t kv_len, int blk_begin, int blk_end,
+                       int64_t max_blocks, double* ksum, float* vamax, void* stream) {
+  return kv_block_stats_dt(k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h, batch, heads, kv_len, blk_begin, blk_end,
+                           max_blocks, ksum, vamax, 0, stream);
 }
 
 int lbq_kv_window_sums(const double* ksum, const float* vamax, int batch, int heads, int blk_begin, int blk_end,
@@ -151,17 +160,22 @@ int lbq_kv_window_sums(const double* ksum, const float* vamax, int batch, int he
   return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "kv_window_sums launch");
 }
 
-int lbq_quant_q(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, int batch, int heads, int q_len,
-                int8_t* q_codes, float* q_scale, void* stream) {
+static int quant_q_dt(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, int batch, int heads, int q_len,
+                      int8_t* q_codes, float* q_scale, int dtype, void* stream) {
   int r;
   if ((r = check_act("q", q, sq_b, sq_l, sq_h)) || (r = check_ptr("q_codes", q_codes)) ||
       (r = check_ptr("q_scale", q_scale)))
     return r;
   if (batch <= 0 || heads <= 0 || q_len <= 0) return fail(LBQ_ERR_ARG, "batch, heads and q_len must be positive");
   lbq::QuantQArgs a{static_cast<const __nv_bfloat16*>(q), sq_b, sq_l, sq_h, batch, heads, q_len,
-                    int(round_up(q_len, 128)), q_codes, q_scale, nullptr, nullptr, 0, 0};
+                    int(round_up(q_len, 128)), q_codes, q_scale, nullptr, nullptr, 0, 0, dtype};
   cudaError_t e = lbq::launch_quant_q(a, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "quant_q launch");
+}
+
+int lbq_quant_q(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, int batch, int heads, int q_len,
+                int8_t* q_codes, float* q_scale, void* stream) {
+  return quant_q_dt(q, sq_b, sq_l, sq_h, batch, heads, q_len, q_codes, q_scale, 0, stream);
 }
 
 int lbq_rope_quant_q(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, const double* rope_cos,
@@ -207,11 +221,12 @@ int lbq_cache_write(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, con
   return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "cache_write launch");
 }
 
-int lbq_quant_kv_tiles(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,
-                       int64_t sv_l, int64_t sv_h, int batch, int heads, int64_t tok0, int seg, int num_segments,
-                       int seg_valid, int seg_len, int64_t kv_len_total, const double* ksum_total,
-                       const float* vamax_total, int8_t* k_codes, float* k_scale, uint8_t* vt_codes, void* km_out,
-                       float* v_scale, int write_totals, int tile_begin, int tile_end, void* stream) {
+static int quant_kv_tiles_dt(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,
+                             int64_t sv_l, int64_t sv_h, int batch, int heads, int64_t tok0, int seg, int num_segments,
+                             int seg_valid, int seg_len, int64_t kv_len_total, const double* ksum_total,
+                             const float* vamax_total, int8_t* k_codes, float* k_scale, uint8_t* vt_codes,
+                             void* km_out, float* v_scale, int write_totals, int tile_begin, int tile_end, int dtype,
+                             void* stream) {
   int r;
   if ((r = check_act("k", k, sk_b, sk_l, sk_h)) || (r = check_act("v", v, sv_b, sv_l, sv_h))) return r;
   if ((r = check_ptr("ksum_total", ksum_total)) || (r = check_ptr("vamax_total", vamax_total)) ||
@@ -233,11 +248,21 @@ int lbq_quant_kv_tiles(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, 
   const int seg_pad = int(round_up(seg_len, 128));
   lbq::QuantKArgs ka{static_cast<const __nv_bfloat16*>(k), sk_b, sk_l, sk_h, batch, heads, tok0, seg, seg_valid,
                      seg_pad, kv_len_total, ksum_total, k_codes, k_scale,
-                     static_cast<__nv_bfloat16*>(km_out), write_totals, lbq::device_status_ptr()};
+                     static_cast<__nv_bfloat16*>(km_out), write_totals, lbq::device_status_ptr(), dtype};
   lbq::QuantVArgs va{static_cast<const __nv_bfloat16*>(v), sv_b, sv_l, sv_h, batch, heads, tok0, seg, seg_valid,
-                     seg_pad, vamax_total, vt_codes, v_scale, write_totals, lbq::device_status_ptr()};
+                     seg_pad, vamax_total, vt_codes, v_scale, write_totals, lbq::device_status_ptr(), dtype};
   cudaError_t e = lbq::launch_quant_kv(ka, va, tile_begin, tile_end - tile_begin, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "quant_kv launch");
+}
+
+int lbq_quant_kv_tiles(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,
+                       int64_t sv_l, int64_t sv_h, int batch, int heads, int64_t tok0, int seg, int num_segments,
+                       int seg_valid, int seg_len, int64_t kv_len_total, const double* ksum_total,
+                       const float* vamax_total, int8_t* k_codes, float* k_scale, uint8_t* vt_codes, void* km_out,
+                       float* v_scale, int write_totals, int tile_begin, int tile_end, void* stream) {
+  return quant_kv_tiles_dt(k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h, batch, heads, tok0, seg, num_segments, seg_valid,
+                           seg_len, kv_len_total, ksum_total, vamax_total, k_codes, k_scale, vt_codes, km_out,
+                           v_scale, write_totals, tile_begin, tile_end, 0, stream);
 }
 
 int lbq_quant_kv(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b, int64_t sv_l,
@@ -269,7 +294,8 @@ int lbq_quant_qkv(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, int q
                   int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b, int64_t sv_l, int64_t sv_h, int64_t kv_len,
                   int batch, int heads, int8_t* q_codes, float* q_scale, int8_t* k_codes, float* k_scale,
                   uint8_t* vt_codes, float* v_scale, void* km_out, void* workspace, size_t workspace_bytes,
-                  void* stream) {
+                  int dtype, void* stream) {
+  if (dtype != LBQ_DTYPE_BF16 && dtype != LBQ_DTYPE_F16) return fail(LBQ_ERR_ARG, "dtype %d is neither bf16 nor fp16", dtype);
   if (kv_len <= 0 || kv_len > (int64_t(1) << 30)) return fail(LBQ_ERR_ARG, "kv_len %lld out of range", (long long)kv_len);
   if (batch <= 0 || heads <= 0 || batch > 65535 || heads > 65535)
     return fail(LBQ_ERR_ARG, "batch %d / heads %d out of range (1..65535)", batch, heads);
@@ -283,13 +309,14 @@ int lbq_quant_qkv(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, int q
   double* ksum_total = ksum + int64_t(nblk) * cols;
   float* vamax = reinterpret_cast<float*>(ksum_total + cols);
   float* vamax_total = vamax + int64_t(nblk) * cols;
-  int r = lbq_kv_block_stats(k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h, batch, heads, kv_len, 0, nblk, nblk, ksum,
-                             vamax, stream);
+  int r = kv_block_stats_dt(k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h, batch, heads, kv_len, 0, nblk, nblk, ksum,
+                            vamax, dtype, stream);
   if (r) return r;
   if ((r = lbq_kv_window_sums(ksum, vamax, batch, heads, 0, nblk, nblk, ksum_total, vamax_total, stream))) return r;
-  if ((r = lbq_quant_q(q, sq_b, sq_l, sq_h, batch, heads, q_len, q_codes, q_scale, stream))) return r;
-  return lbq_quant_kv(k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h, batch, heads, 0, 0, 1, int(kv_len), int(kv_len),
-                      kv_len, ksum_total, vamax_total, k_codes, k_scale, vt_codes, km_out, v_scale, 1, stream);
+  if ((r = quant_q_dt(q, sq_b, sq_l, sq_h, batch, heads, q_len, q_codes, q_scale, dtype, stream))) return r;
+  return quant_kv_tiles_dt(k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h, batch, heads, 0, 0, 1, int(kv_len), int(kv_len),
+                           kv_len, ksum_total, vamax_total, k_codes, k_scale, vt_codes, km_out, v_scale, 1, 0,
+                           int((kv_len + 127) / 128), dtype, stream);
 }
 
 int lbq_requant_cache(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,
@@ -312,9 +339,15 @@ int lbq_requant_cache(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, c
 
 int lbq_attn_fwd(const int8_t* q_codes, const float* q_scale, int q_len, const int8_t* k_codes, const float* k_scale,
                  const uint8_t* vt_codes, const float* v_scale, int64_t kv_len, int num_segments, int seg_len,
-                 int batch, int heads, float sm_scale, void* out, int64_t so_b, int64_t so_l, int64_t so_h,
-                 int num_splits, float* o_part, float* ml_part, int* splits_used, void* stream) {
+                 int batch, int heads, float sm_scale, int is_causal, void* out, int64_t so_b, int64_t so_l,
+                 int64_t so_h, int num_splits, float* o_part, float* ml_part, int* splits_used, int dtype,
+                 void* stream) {
   int r;
+  if (is_causal)
+    return fail(LBQ_ERR_UNSUPPORTED,
+                "causal attention is not implemented by the quantized kernel (the drop-in attention() routes "
+                "causal calls to the reference's non-Sage branch)");
+  if (dtype != LBQ_DTYPE_BF16 && dtype != LBQ_DTYPE_F16) return fail(LBQ_ERR_ARG, "dtype %d is neither bf16 nor fp16", dtype);
   if ((r = check_ptr("q_codes", q_codes)) || (r = check_ptr("q_scale", q_scale)) || (r = check_ptr("k_codes", k_codes)) ||
       (r = check_ptr("k_scale", k_scale)) || (r = check_ptr("vt_codes", vt_codes)) || (r = check_ptr("v_scale", v_scale)))
     return r;
@@ -350,6 +383,7 @@ int lbq_attn_fwd(const int8_t* q_codes, const float* q_scale, int q_len, const i
     return r;
   if (sm_scale <= 0.f) sm_scale = 0.08838834764831845f;   // 128 ** -0.5
   lbq::AttnArgs a{};
+  a.dtype = dtype;
   a.q_scale = q_scale;
   a.k_scale = k_scale;
   a.v_scale = v_scale;
@@ -377,15 +411,17 @@ int lbq_attn_fwd(const int8_t* q_codes, const float* q_scale, int q_len, const i
 }
 
 int lbq_splitkv_combine(const float* o_part, const float* ml_part, int num_splits, const float* v_scale, int batch,
-                        int heads, int q_len, void* out, int64_t so_b, int64_t so_l, int64_t so_h, void* stream) {
+                        int heads, int q_len, void* out, int64_t so_b, int64_t so_l, int64_t so_h, int dtype,
+                        void* stream) {
   int r;
+  if (dtype != LBQ_DTYPE_BF16 && dtype != LBQ_DTYPE_F16) return fail(LBQ_ERR_ARG, "dtype %d is neither bf16 nor fp16", dtype);
   if ((r = check_ptr("o_part", o_part)) || (r = check_ptr("ml_part", ml_part)) || (r = check_ptr("v_scale", v_scale)))
     return r;
   if ((r = check_act("out", out, so_b, so_l, so_h))) return r;
   if (num_splits < 1 || batch <= 0 || heads <= 0 || q_len <= 0)
     return fail(LBQ_ERR_ARG, "num_splits, batch, heads and q_len must be positive");
   lbq::CombineArgs a{o_part, reinterpret_cast<const float2*>(ml_part), v_scale, static_cast<__nv_bfloat16*>(out),
-                     so_b, so_l, so_h, batch, heads, q_len, int(round_up(q_len, 128)), num_splits};
+                     so_b, so_l, so_h, batch, heads, q_len, int(round_up(q_len, 128)), num_splits, dtype};
   cudaError_t e = lbq::launch_combine(a, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "splitkv_combine launch");
 }

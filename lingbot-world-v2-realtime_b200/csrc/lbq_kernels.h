@@ -20,6 +20,7 @@ struct KvBlockStatsArgs {
   double* ksum;               // [B][max_blocks][H][128]
   float* vamax;               // [B][max_blocks][H][128]
   int* status;                // device status word (debug-build index checks)
+  int dtype;                  // activations: 0 bf16, 1 fp16
 };
 
 struct KvWindowSumsArgs {
@@ -42,6 +43,7 @@ struct QuantQArgs {
   const double* rope_cos;     // null: no RoPE; else [B][L][64] (strides sr_b, sr_l in elements)
   const double* rope_sin;
   int64_t sr_b, sr_l;
+  int dtype;                  // q: 0 bf16, 1 fp16 (RoPE only with bf16)
 };
 
 // Store a chunk of K/V into the cache buffer (K optionally roped) and recompute the statistics of
@@ -77,9 +79,10 @@ struct QuantKArgs {
   const double* ksum_total;   // [B][H][128]
   int8_t* k_codes;            // [S][B][H][seg_pad][128]
   float* k_scale;             // [S][B][H][seg_pad/64]
-  __nv_bfloat16* km_out;      // [B][H][128] or null
+  __nv_bfloat16* km_out;      // [B][H][128] (in k's dtype) or null
   int write_km;
   int* status;                // device status word (debug-build index checks)
+  int dtype;                  // k: 0 bf16, 1 fp16
 };
 
 struct QuantVArgs {
@@ -93,6 +96,7 @@ struct QuantVArgs {
   float* v_scale;             // [B][H][128]
   int write_scale;
   int* status;                // device status word (debug-build index checks)
+  int dtype;                  // v: 0 bf16, 1 fp16
 };
 
 struct AttnArgs {
@@ -123,6 +127,7 @@ struct AttnArgs {
   int64_t xchg_off;
   int64_t recv_o_off;         // heap offset of the receive slots [ranks][B*H][part][128] fp16
   int64_t recv_ml_off;        //                                  [ranks][B*H][part] float2
+  int dtype;                  // out: 0 bf16, 1 fp16 (one-pass and split-KV modes)
 };
 
 // Merge of the key-range partials a rank received for its query rows (flash-decoding merge).
@@ -156,6 +161,7 @@ struct CombineArgs {
   __nv_bfloat16* out;
   int64_t so_b, so_l, so_h;
   int batch, heads, q_len, q_pad, num_splits;
+  int dtype;                  // out: 0 bf16, 1 fp16
 };
 
 // Exchange area of a sequence split (byte offsets from its start, inside the peer heap).

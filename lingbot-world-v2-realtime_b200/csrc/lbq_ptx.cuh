@@ -7,6 +7,8 @@
 #pragma once
 #include <cstdint>
 #include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #ifndef LBQ_SPIN_LIMIT
@@ -352,6 +354,27 @@ __device__ __forceinline__ uint32_t pack_e4m3x2(float lo, float hi) {
   uint16_t r;
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
   return r;
+}
+// Two floats to an activation pair (dtype 0: bf16, 1: fp16; round to nearest even), `lo` in the low
+// 16 bits.
+__device__ __forceinline__ uint32_t pack_act2(float lo, float hi, int dtype) {
+  if (dtype) {
+    const __half2 p = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&p);
+  }
+  const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&p);
+}
+// The two activations of a 32-bit pair (dtype 0: bf16, 1: fp16) as floats (exact).
+__device__ __forceinline__ void act2_to_f32(uint32_t w, int dtype, float& lo, float& hi) {
+  if (dtype) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+    lo = f.x;
+    hi = f.y;
+  } else {
+    lo = __uint_as_float(w << 16);
+    hi = __uint_as_float(w & 0xffff0000u);
+  }
 }
 // ---- packed fp32 pairs (sm_100 f32x2 instructions: one issue slot for two lanes of work)
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {

@@ -60,7 +60,7 @@ int lbq_quant_qkv_static(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h
                          int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b, int64_t sv_l,
                          int64_t sv_h, int64_t kv_len, int batch, int heads, int8_t* q_codes, float* q_scale,
                          int8_t* k_codes, float* k_scale, uint8_t* vt_codes, float* v_scale, void* km_out,
-                         void* stream) {
+                         int dtype, void* stream) {
   if (batch <= 0 || heads <= 0 || batch > 65535 || heads > 65535 || kv_len <= 0 || kv_len > (int64_t(1) << 30))
     return lbq::set_error(LBQ_ERR_ARG, "batch and heads must be in 1..65535 and kv_len in 1..2^30");
   const size_t need = lbq_quant_qkv_workspace(batch, heads, kv_len);
@@ -76,7 +76,7 @@ int lbq_quant_qkv_static(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h
                           cudaGetErrorString(e));
   return lbq_quant_qkv(q, sq_b, sq_l, sq_h, q_len, k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h, kv_len, batch, heads,
                        q_codes, q_scale, k_codes, k_scale, vt_codes, v_scale, km_out, scratch,
-                       kStaticScratchBytes, stream);
+                       kStaticScratchBytes, dtype, stream);
 }
 
 }  // extern "C"

@@ -34,6 +34,12 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4 raw, float (&f)[8]) {
     f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
   }
 }
+// 8 activations (dtype 0: bf16, 1: fp16) as floats, exactly.
+__device__ __forceinline__ void act8_to_f32(const uint4 raw, int dtype, float (&f)[8]) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) act2_to_f32(w[i], dtype, f[2 * i], f[2 * i + 1]);
+}
 
 __device__ __forceinline__ uint32_t pack_s8x4(int32_t a, int32_t b, int32_t c, int32_t d) {
   return (uint32_t(a) & 0xff) | ((uint32_t(b) & 0xff) << 8) | ((uint32_t(c) & 0xff) << 16) | (uint32_t(d) << 24);
@@ -85,8 +91,8 @@ __global__ void __launch_bounds__(128) kv_block_stats_kernel(KvBlockStatsArgs a)
     const uint4 kr = *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + tok * a.sk_l + h * a.sk_h + c16 * 8);
     const uint4 vr = *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + tok * a.sv_l + h * a.sv_h + c16 * 8);
     float kf[8], vf[8];
-    bf16x8_to_f32(kr, kf);
-    bf16x8_to_f32(vr, vf);
+    act8_to_f32(kr, a.dtype, kf);
+    act8_to_f32(vr, a.dtype, vf);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       s[i] += double(kf[i]);
@@ -247,7 +253,7 @@ __global__ void __launch_bounds__(256) quant_q_kernel(QuantQArgs a) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     float x[8];
-    bf16x8_to_f32(raw[i], x);
+    act8_to_f32(raw[i], a.dtype, x);
 #pragma unroll
     for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(x[j]));
   }
@@ -262,7 +268,7 @@ __global__ void __launch_bounds__(256) quant_q_kernel(QuantQArgs a) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     float x[8];
-    bf16x8_to_f32(raw[i], x);
+    act8_to_f32(raw[i], a.dtype, x);
     uint2 packed;
     packed.x = pack_s8x4(cvt_rni_sat_s8(__fmul_rn(x[0], inv)), cvt_rni_sat_s8(__fmul_rn(x[1], inv)),
                          cvt_rni_sat_s8(__fmul_rn(x[2], inv)), cvt_rni_sat_s8(__fmul_rn(x[3], inv)));
@@ -272,11 +278,19 @@ __global__ void __launch_bounds__(256) quant_q_kernel(QuantQArgs a) {
   }
 }
 
-// km for channel c of (b, h): the window mean rounded through fp32 to bf16 (the rounding torch
-// applies when a float64 mean is cast to bfloat16).
-__device__ __forceinline__ float window_mean_bf16(const double* ksum_total, int64_t o, int64_t kv_len) {
-  const double mean = ksum_total[o] / double(kv_len);
-  return __bfloat162float(__float2bfloat16_rn(__double2float_rn(mean)));
+// km for channel c of (b, h): the window mean rounded through fp32 to k's dtype (the rounding torch
+// applies when a float64 mean is cast to bfloat16 or float16); its 16 bits in *bits.
+__device__ __forceinline__ float window_mean_act(const double* ksum_total, int64_t o, int64_t kv_len, int dtype,
+                                                 uint16_t* bits) {
+  const float mean = __double2float_rn(ksum_total[o] / double(kv_len));
+  if (dtype) {
+    const __half hm = __float2half_rn(mean);
+    *bits = __half_as_ushort(hm);
+    return __half2float(hm);
+  }
+  const __nv_bfloat16 bm = __float2bfloat16_rn(mean);
+  *bits = __bfloat16_as_ushort(bm);
+  return __bfloat162float(bm);
 }
 
 // ------------------------------------------------------------------ K/V quantizer (one launch)
@@ -309,9 +323,10 @@ __device__ __forceinline__ void quant_k_tile(const QuantKArgs& a, QuantKvShared&
   const int blk = tile * 2 + half;
   const int64_t bh = int64_t(b) * a.heads + h;
   if (half == 0) {
-    const float km = window_mean_bf16(a.ksum_total, bh * 128 + t, a.kv_len_total);
+    uint16_t km_bits;
+    const float km = window_mean_act(a.ksum_total, bh * 128 + t, a.kv_len_total, a.dtype, &km_bits);
     sh.km[t] = km;
-    if (a.km_out != nullptr && first && a.write_km) a.km_out[bh * 128 + t] = __float2bfloat16_rn(km);
+    if (a.km_out != nullptr && first && a.write_km) reinterpret_cast<uint16_t*>(a.km_out)[bh * 128 + t] = km_bits;
   }
   uint4 raw[8];
 #pragma unroll
@@ -331,7 +346,7 @@ __device__ __forceinline__ void quant_k_tile(const QuantKArgs& a, QuantKvShared&
     const int64_t tok = int64_t(blk) * 64 + rg + 8 * i;
     if (tok < a.seg_valid) {
       float x[8];
-      bf16x8_to_f32(raw[i], x);
+      act8_to_f32(raw[i], a.dtype, x);
 #pragma unroll
       for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(__fsub_rn(x[j], km[j])));
     }
@@ -350,7 +365,7 @@ __device__ __forceinline__ void quant_k_tile(const QuantKArgs& a, QuantKvShared&
     const int r = rg + 8 * i;
     const bool valid = int64_t(blk) * 64 + r < a.seg_valid;   // pad tokens encode 0
     float x[8];
-    bf16x8_to_f32(raw[i], x);
+    act8_to_f32(raw[i], a.dtype, x);
 #pragma unroll
     for (int j = 0; j < 8; ++j) x[j] = valid ? __fmul_rn(__fsub_rn(x[j], km[j]), inv) : 0.f;
     packed[i].x = pack_s8x4(cvt_rni_sat_s8(x[0]), cvt_rni_sat_s8(x[1]), cvt_rni_sat_s8(x[2]), cvt_rni_sat_s8(x[3]));
@@ -392,8 +407,10 @@ __device__ __forceinline__ void quant_v_tile(const QuantVArgs& a, QuantKvShared&
     for (int e = 0; e < 4; ++e) {
       const int r = tq * 32 + 4 * k4 + e;
       const uint32_t pair = *reinterpret_cast<const uint32_t*>(&sh.v[r * kVtPitch + cp * 4]);
-      lo[e] = fminf(fmaxf(__fmul_rn(__uint_as_float(pair << 16), r0), -2.25f), 2.25f);
-      hi[e] = fminf(fmaxf(__fmul_rn(__uint_as_float(pair & 0xffff0000u), r1), -2.25f), 2.25f);
+      float v0, v1;
+      act2_to_f32(pair, a.dtype, v0, v1);
+      lo[e] = fminf(fmaxf(__fmul_rn(v0, r0), -2.25f), 2.25f);
+      hi[e] = fminf(fmaxf(__fmul_rn(v1, r1), -2.25f), 2.25f);
     }
     // padded tokens were staged as 0 and encode as 0
     w0[k4] = pack_e4m3x2(lo[0], lo[1]) | (pack_e4m3x2(lo[2], lo[3]) << 16);

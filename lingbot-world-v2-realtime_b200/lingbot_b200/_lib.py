@@ -31,14 +31,14 @@ SIGNATURES = {
                             _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp]),
     "lbq_quant_qkv_workspace": (_sz, [_i32, _i32, _i64]),
     "lbq_quant_qkv": (_i32, [_vp, _i64, _i64, _i64, _i32, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
-                             _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+                             _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i32, _vp]),
     "lbq_quant_qkv_static": (_i32, [_vp, _i64, _i64, _i64, _i32, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
-                                    _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+                                    _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp]),
     "lbq_requant_cache": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _i32, _i64, _i64, _vp, _vp,
                                  _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
-    "lbq_attn_fwd": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _f32, _vp, _i64,
-                            _i64, _i64, _i32, _vp, _vp, ctypes.POINTER(_i32), _vp]),
-    "lbq_splitkv_combine": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i32, _vp, _i64, _i64, _i64, _vp]),
+    "lbq_attn_fwd": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _i64,
+                            _i64, _i64, _i32, _vp, _vp, ctypes.POINTER(_i32), _i32, _vp]),
+    "lbq_splitkv_combine": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i32, _vp, _i64, _i64, _i64, _i32, _vp]),
     "lbq_peer_export": (_i32, [_vp, _vp, ctypes.POINTER(ctypes.c_uint64)]),
     "lbq_peer_open": (_i32, [_vp, ctypes.POINTER(_vp)]),
     "lbq_peer_close": (_i32, [_vp]),

@@ -3,8 +3,11 @@
 `attention(q, k, v, ...)` keeps the reference's signature. The plain batched call (no q_lens /
 k_lens, no dropout, not causal) — the only way the causal DiT calls it
 (models/lingbot_world/transformer.py:225) — runs the B200 quantized kernels (INT8 QK^T, FP8 PV,
-SageAttention-2 semantics). Every other call takes the reference's non-Sage branch, which is the
-paper's attention (wan/modules/attention.py:132-178); here that is torch's SDPA on the GPU.
+SageAttention-2 semantics) on q/k/v cast to `dtype` (bf16 by default, or fp16), as the reference
+casts before Sage (lingbot/layers/attention.py:30-36). Every other call takes the reference's non-Sage
+branch, which is the paper's attention (wan/modules/attention.py:132-178); here that is torch's SDPA
+on the GPU. That includes causal=True, which the reference would hand to Sage with is_causal: the
+quantized kernel has no causal mask and its C ABI refuses one (LBQ_ERR_UNSUPPORTED).
 The quantized path is registered as the custom op `lbq::sage_attn` (with a fake implementation) so
 torch.compile keeps the DiT in one graph, as the reference relied on for `sageattn`.
 
@@ -26,6 +29,7 @@ __all__ = ["attention", "flash_attention", "set_cross_attention"]
 
 @torch.library.custom_op("lbq::sage_attn", mutates_args=())
 def sage_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: float) -> torch.Tensor:
+    """q/k/v [B, L, H, 128], all bf16 or all fp16 -> [B, Lq, H, 128] in that dtype."""
     return ops.sage_attn(q, k, v, sm_scale=sm_scale if sm_scale > 0 else None)
 
 
@@ -89,10 +93,11 @@ def attention(q, k, v, q_lens=None, k_lens=None, dropout_p=0., softmax_scale=Non
               causal=False, window_size=(-1, -1), deterministic=False, dtype=None, fa_version=None):
     dtype = torch.bfloat16 if dtype is None else dtype
     if q_lens is None and k_lens is None and dropout_p == 0. and not causal:
+        if dtype not in ops.DTYPE_CODES:
+            raise TypeError(f"attention(dtype={dtype}): the quantized kernels take bfloat16 or float16")
         # q/k/v are [B, L, H, D] ("NHD"); Lq != Lk is fine without a mask (attention.py:32-36)
         out_dtype = q.dtype
-        x = sage_attn(q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16),
-                      float(softmax_scale) if softmax_scale else 0.0)
+        x = sage_attn(q.to(dtype), k.to(dtype), v.to(dtype), float(softmax_scale) if softmax_scale else 0.0)
         return x.to(out_dtype)
     return _paper_attention(q, k, v, q_lens=q_lens, k_lens=k_lens, dropout_p=dropout_p,
                             softmax_scale=softmax_scale, causal=causal, dtype=dtype)

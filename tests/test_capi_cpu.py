@@ -42,7 +42,7 @@ def test_argument_validation_without_a_gpu():
     mis = ctypes.c_void_p(ctypes.addressof(buf) + 1)
     rc = lib.lbq_quant_q(mis, 0, 0, 0, 1, 1, 1, mis, mis, None)
     assert rc == 2 and b"aligned" in lib.lbq_last_error()
-    assert lib.lbq_abi_version() == 100
+    assert lib.lbq_abi_version() == 101
 
 
 def test_quant_workspace_size_is_checked():

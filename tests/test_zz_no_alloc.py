@@ -38,7 +38,7 @@ def _call(name, q, k, v, bufs, ws=None):
             *[_ptr(t) for t in _outs(bufs)]]
     if ws is not None:
         args += [_ptr(ws), ws.numel()]
-    _lib.call(name, *args, _stream())
+    _lib.call(name, *args, 0, _stream())                    # LBQ_DTYPE_BF16
 
 
 @pytest.mark.parametrize("shape", [(1, 12, 6032, 12064), (2, 3, 513, 4097)], ids=["config1", "batch2-odd"])
@@ -68,6 +68,6 @@ def test_static_scratch_rejects_windows_past_its_capacity():
     assert ok <= (16 << 20) < too_big
     null = ctypes.c_void_p(0)
     rc = lib.lbq_quant_qkv_static(null, 0, 0, 0, 1, null, 0, 0, 0, null, 0, 0, 0, 58177, 1, 12,
-                                  null, null, null, null, null, null, null, null)
+                                  null, null, null, null, null, null, null, 0, null)
     assert rc == 1
     assert b"static" in lib.lbq_last_error() and b"workspace" in lib.lbq_last_error()
