@@ -61,7 +61,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["chunk", "call", "requant", "streams", "cross", "keys-rank"],
+    ap.add_argument("--workload", choices=["chunk", "call", "requant", "streams", "cross", "keys-rank", "evict"],
                     default="chunk")
     ap.add_argument("--ranks", type=int, default=8, help="--workload keys-rank: ranks of the emulated split")
     ap.add_argument("--rank", type=int, default=1, help="--workload keys-rank: the emulated rank")
@@ -898,6 +898,49 @@ def run_keys_rank(args, world, rank, local):
                           "peak_source": f"2 x bf16_tflops burst ({src})", "attn_ms_per_call": round(attn_ms, 4)})
 
 
+def run_evict(args, world, rank, local):
+    """The memory-write pass's cache write with an eviction, per chunk (30 layers): a full window of
+    30160 tokens with a one-frame sink (1508 tokens) takes the chunk's 6032 tokens, dropping the oldest
+    6032 after the sink (kv_cache.write, lingbot/layers/kv_cache.py:64-75). Timed for the reference's
+    left-shift eviction (the default cache: copy, then the blocks after the sink re-read) and for the
+    ring cache (head moves, the blocks after the sink re-read through the map); `value` is the ring's."""
+    from lingbot_b200 import kv_cache
+    dev = torch.device("cuda", local)
+    sink, n = 1508, LQ
+    g = torch.Generator(device=dev).manual_seed(5)
+    kv = torch.randn(2, 1, n, H, D, generator=g, device=dev).bfloat16()
+    res = {}
+    for mode in ("shift", "ring"):
+        caches = kv_cache.allocate(LAYERS, [1, LK, H, D], torch.bfloat16, dev, ring=(mode == "ring"))
+        start = 0
+        for _ in range(LK // n):                                     # fill the window
+            for c in caches:
+                end, cur = kv_cache.write(c, kv[0], kv[1], start, sink, 20)
+                kv_cache.commit(c, cur, end)
+            start += n
+        state = {"start": start}
+
+        def fn():
+            for c in caches:
+                end, cur = kv_cache.write(c, kv[0], kv[1], state["start"], sink, 20)
+                kv_cache.commit(c, cur, end)
+            state["start"] += n
+        res[mode], clocks = _timed(fn, args.steps, args.warmup, dev, world)
+        del caches
+        torch.cuda.empty_cache()
+    rolled = LK - sink - n
+    return dict(tops=res["ring"], ms=res["ring"], clocks=clocks, launches=LAYERS * 2 * args.steps, e2e=None, unit="ms",
+                higher_is_better=False,
+                roofline={"bound": "hbm", "achieved": None, "peak": None, "unit": "GB/s", "frac": None,
+                          "traffic": None, "kernel": "kv_block_stats_kernel + cache_write_kernel",
+                          "note": "eviction work per layer: the ring re-reads the rolled tokens' blocks "
+                                  f"({rolled} tokens of bf16 K and V); the shift also copies them"},
+                config={"workload": "cache write of a chunk with eviction, 30 layers",
+                        "window": LK, "sink": sink, "chunk": n, "rolled": rolled, "heads": H, "head_dim": D,
+                        "shift_ms_per_chunk": round(res["shift"], 3), "ring_ms_per_chunk": round(res["ring"], 3),
+                        "parallelism": "single GPU"})
+
+
 def run_requant(args, world, rank, local):
     """re-quantize the 30-layer bf16 memory cache [30, 24128, 12, 128] (K int8 per
     64-token block after the channel mean, V e4m3 per channel) from its block statistics."""
@@ -913,7 +956,7 @@ def run_requant(args, world, rank, local):
     vamax = torch.empty(nl, nb, H, D, dtype=torch.float32, device=dev)
     st = ops._stream()
     _lib.call("lbq_kv_block_stats", ops._ptr(k), *k.stride()[:3], ops._ptr(v), *v.stride()[:3], nl, H, lk, 0, nb, nb,
-              ops._ptr(ksum), ops._ptr(vamax), st)
+              ops._ptr(ksum), ops._ptr(vamax), 0, 0, 0, st)
     kc, ks, vt, vs, km = ops.alloc_kv(nl, H, lk, 1, dev)
     sums = torch.empty(nl * H * D * 3, dtype=torch.float32, device=dev)
     ev = []
@@ -923,7 +966,7 @@ def run_requant(args, world, rank, local):
         a.record()
         _lib.call("lbq_requant_cache", ops._ptr(k), *k.stride()[:3], ops._ptr(v), *v.stride()[:3], nl, H, lk, nb,
                   ops._ptr(ksum), ops._ptr(vamax), ops._ptr(sums), ops._ptr(kc), ops._ptr(ks), ops._ptr(vt),
-                  ops._ptr(vs), ops._ptr(km), ops._stream())
+                  ops._ptr(vs), ops._ptr(km), 0, 0, 0, ops._stream())
         b.record()
         ev.append((a, b))
 
@@ -984,6 +1027,8 @@ def main():
             res = run_cross(args, world, rank, local)
         elif args.workload == "keys-rank":
             res = run_keys_rank(args, world, rank, local)
+        elif args.workload == "evict":
+            res = run_evict(args, world, rank, local)
         else:
             res = run_requant(args, world, rank, local)
         if rank == 0:
@@ -999,11 +1044,13 @@ def main():
                       "requant": "K/V re-quant HBM GB/s (BASELINE config 2, 30 layers x 24128 tokens)",
                       "streams": "aggregate attention TOPS, independent streams (BASELINE config 5)",
                       "cross": "cross-attention TOPS, quantized (q 6032 x 512 text keys; quantize + attend)",
-                      "keys-rank": "key-range attention TOPS of one emulated rank (BASELINE config 4)"}[args.workload]
+                      "keys-rank": "key-range attention TOPS of one emulated rank (BASELINE config 4)",
+                      "evict": "KV-cache write with eviction, ms per chunk (30 layers)"}[args.workload]
             line = {"metric": metric,
                     "value": round(res["tops"], 2), "unit": res.get("unit", "TOPS"), "n_gpus": world, "steps": args.steps,
                     "warmup": args.warmup, "ms_per_step": round(res["ms"], 3), "s_per_chunk": round(res["ms"] / 1e3, 5),
-                    "higher_is_better": True, "scaling": res.get("scaling", "strong"), "vs_baseline": None,
+                    "higher_is_better": res.get("higher_is_better", True), "scaling": res.get("scaling", "strong"),
+                    "vs_baseline": None,
                     "dtype": "int8 QK^T / fp8 e4m3 PV (bf16 in/out)", "data": "synthetic",
                     "config": {"workload": {"chunk": "BASELINE config 4: full chunk, 4 denoise + 1 memory-write pass x 30 layers",
                                             "call": f"BASELINE config 1: q 6032 x kv {args.call_kv}",

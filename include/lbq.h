@@ -60,15 +60,22 @@ LBQ_API const char* lbq_last_error(void);
  * invalid). Synchronous. `clear` != 0 resets it to 0 afterwards. */
 LBQ_API int lbq_device_status(int clear, int* status_out);
 
+/* Ring layout of a KV-cache buffer (the arguments ring_sink, ring_len, ring_head of the three cache
+ * entries below): logical window token t — the reference's cache row after its left-shift eviction
+ * (lingbot/layers/kv_cache.py:52-61) — is stored at buffer row t when t < ring_sink, else at
+ * ring_sink + ((t - ring_sink + ring_head) mod ring_len). An eviction is then ring_head += evicted
+ * (mod ring_len) instead of a copy. ring_len = 0 (with sink and head 0): rows are logical tokens. */
+
 /* Per-64-token-block statistics of a bf16 K/V window: ksum (fp64 sum of K per channel) and vamax
- * (max |V| per channel) for blocks [blk_begin, blk_end) of tokens [0, kv_len).
+ * (max |V| per channel) for blocks [blk_begin, blk_end) of logical tokens [0, kv_len).
  * Tables are [B][max_blocks][H][128]. Block b covers tokens [64b, min(64b+64, kv_len)).
  * Replaces the per-64-token V min/max table of lingbot/layers/sage_preq.py:36-44,87-98
  * (`_blk_minmax`, `_update`) and extends it with the K sums the mean-smoothing needs. */
 LBQ_API int lbq_kv_block_stats(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h,
                        const void* v, int64_t sv_b, int64_t sv_l, int64_t sv_h,
                        int batch, int heads, int64_t kv_len, int blk_begin, int blk_end,
-                       int64_t max_blocks, double* ksum, float* vamax, void* stream);
+                       int64_t max_blocks, double* ksum, float* vamax, int64_t ring_sink,
+                       int64_t ring_len, int64_t ring_head, void* stream);
 
 /* Reduce the block statistics of blocks [blk_begin, blk_end) into per-(batch, head, channel)
  * totals: ksum_total (fp64) and vamax_total. With several ranks, each reduces its own blocks and
@@ -101,13 +108,14 @@ LBQ_API int lbq_rope_quant_q(const void* q, int64_t sq_b, int64_t sq_l, int64_t 
  * `kv_cache["k"][:, local_start_index:local_end_index] = k`, lingbot/layers/kv_cache.py:64-75), and
  * recomputes the statistics rows of the 64-token blocks covering those tokens exactly as
  * lbq_kv_block_stats(kv_len = tok_begin + n_tokens) would after the copy (earlier tokens of the first
- * block are read back from the cache). The source must not overlap the cache. */
+ * block are read back from the cache). The source must not overlap the cache. Tokens are logical;
+ * rows follow the ring layout. */
 LBQ_API int lbq_cache_write(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,
                             int64_t sv_l, int64_t sv_h, const double* rope_cos, const double* rope_sin, int64_t sr_b,
                             int64_t sr_l, void* k_cache, int64_t ck_b, int64_t ck_l, int64_t ck_h, void* v_cache,
                             int64_t cv_b, int64_t cv_l, int64_t cv_h, int batch, int heads, int64_t kv_size,
                             int64_t tok_begin, int64_t n_tokens, int64_t max_blocks, double* ksum, float* vamax,
-                            void* stream);
+                            int64_t ring_sink, int64_t ring_len, int64_t ring_head, void* stream);
 
 /* K/V quantizer for one segment of the window: tokens [tok0, tok0 + seg_valid) of k/v become
  * segment `seg` of the code buffers (num_segments segments in total). km = bf16(ksum_total /
@@ -164,7 +172,8 @@ LBQ_API int lbq_requant_cache(const void* k, int64_t sk_b, int64_t sk_l, int64_t
                       int batch, int heads, int64_t kv_len, int64_t max_blocks,
                       const double* ksum, const float* vamax, void* sums_ws,
                       int8_t* k_codes, float* k_scale, uint8_t* vt_codes, float* v_scale,
-                      void* km_out, void* stream);
+                      void* km_out, int64_t ring_sink, int64_t ring_len, int64_t ring_head,
+                      void* stream);
 
 /* Attention over quantized codes. out [B, q_len, H, 128] in `dtype` (LBQ_DTYPE_BF16 or _F16) with
  * element strides so_*. sm_scale <= 0 means 1/sqrt(128). is_causal != 0 returns LBQ_ERR_UNSUPPORTED:

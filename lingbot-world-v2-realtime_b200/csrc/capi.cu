@@ -44,6 +44,17 @@ int check_ptr(const char* name, const void* p) {
   if (!aligned16(p)) return fail(LBQ_ERR_ALIGN, "%s is not 16-byte aligned", name);
   return LBQ_OK;
 }
+// Checks a ring layout (len == 0: none) over a buffer whose logical window is `window` tokens.
+int check_ring(int64_t sink, int64_t len, int64_t head, int64_t window) {
+  if (len == 0) return (sink == 0 && head == 0) ? LBQ_OK : fail(LBQ_ERR_ARG, "ring_sink / ring_head without ring_len");
+  if (sink < 0 || len < 0 || head < 0 || head >= len)
+    return fail(LBQ_ERR_ARG, "ring (sink %lld, len %lld, head %lld) invalid", (long long)sink, (long long)len,
+                (long long)head);
+  if (window > sink + len)
+    return fail(LBQ_ERR_ARG, "window of %lld tokens exceeds the ring's sink %lld + %lld", (long long)window,
+                (long long)sink, (long long)len);
+  return LBQ_OK;
+}
 // Checks a pair of [B, L, 64] float64 RoPE tables (cos, sin): both or neither given, 16-byte aligned,
 // strides even (so a thread's 4 angles load as two double2).
 int check_rope(const double* cs, const double* sn, int64_t sr_b, int64_t sr_l) {
@@ -122,7 +133,8 @@ int lbq_device_status(int clear, int* status_out) {
 // public bf16 entries; lbq_quant_qkv passes the caller's dtype through them.
 static int kv_block_stats_dt(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,
                              int64_t sv_l, int64_t sv_h, int batch, int heads, int64_t kv_len, int blk_begin,
-                             int blk_end, int64_t max_blocks, double* ksum, float* vamax, int dtype, void* stream) {
+                             int blk_end, int64_t max_blocks, double* ksum, float* vamax, int dtype, lbq::Ring ring,
+                             void* stream) {
   int r;
   if ((r = check_act("k", k, sk_b, sk_l, sk_h)) || (r = check_act("v", v, sv_b, sv_l, sv_h))) return r;
   if ((r = check_ptr("ksum", ksum)) || (r = check_ptr("vamax", vamax))) return r;
@@ -133,16 +145,19 @@ static int kv_block_stats_dt(const void* k, int64_t sk_b, int64_t sk_l, int64_t 
   if (blk_end <= blk_begin) return LBQ_OK;
   lbq::KvBlockStatsArgs a{static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v),
                           sk_b, sk_l, sk_h, sv_b, sv_l, sv_h, batch, heads, kv_len, blk_begin, blk_end,
-                          max_blocks, ksum, vamax, lbq::device_status_ptr(), dtype};
+                          max_blocks, ksum, vamax, lbq::device_status_ptr(), dtype, ring};
   cudaError_t e = lbq::launch_kv_block_stats(a, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "kv_block_stats launch");
 }
 
 int lbq_kv_block_stats(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,
                        int64_t sv_l, int64_t sv_h, int batch, int heads, int64_t kv_len, int blk_begin, int blk_end,
-                       int64_t max_blocks, double* ksum, float* vamax, void* stream) {
+                       int64_t max_blocks, double* ksum, float* vamax, int64_t ring_sink, int64_t ring_len,
+                       int64_t ring_head, void* stream) {
+  int r;
+  if ((r = check_ring(ring_sink, ring_len, ring_head, kv_len))) return r;
   return kv_block_stats_dt(k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h, batch, heads, kv_len, blk_begin, blk_end,
-                           max_blocks, ksum, vamax, 0, stream);
+                           max_blocks, ksum, vamax, 0, lbq::Ring{ring_sink, ring_len, ring_head}, stream);
 }
 
 int lbq_kv_window_sums(const double* ksum, const float* vamax, int batch, int heads, int blk_begin, int blk_end,
@@ -198,8 +213,12 @@ int lbq_cache_write(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, con
                     int64_t sr_l, void* k_cache, int64_t ck_b, int64_t ck_l, int64_t ck_h, void* v_cache,
                     int64_t cv_b, int64_t cv_l, int64_t cv_h, int batch, int heads, int64_t kv_size,
                     int64_t tok_begin, int64_t n_tokens, int64_t max_blocks, double* ksum, float* vamax,
-                    void* stream) {
+                    int64_t ring_sink, int64_t ring_len, int64_t ring_head, void* stream) {
   int r;
+  if ((r = check_ring(ring_sink, ring_len, ring_head, tok_begin + n_tokens))) return r;
+  if (ring_len && ring_sink + ring_len > kv_size)
+    return fail(LBQ_ERR_ARG, "ring of %lld rows after a %lld-token sink exceeds the %lld-token cache", (long long)ring_len,
+                (long long)ring_sink, (long long)kv_size);
   if ((r = check_act("k", k, sk_b, sk_l, sk_h)) || (r = check_act("v", v, sv_b, sv_l, sv_h)) ||
       (r = check_act("k_cache", k_cache, ck_b, ck_l, ck_h)) || (r = check_act("v_cache", v_cache, cv_b, cv_l, cv_h)) ||
       (r = check_ptr("ksum", ksum)) || (r = check_ptr("vamax", vamax)) ||
@@ -216,7 +235,8 @@ int lbq_cache_write(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, con
   lbq::CacheWriteArgs a{static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), sk_b, sk_l, sk_h,
                         sv_b, sv_l, sv_h, static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache),
                         ck_b, ck_l, ck_h, cv_b, cv_l, cv_h, rope_cos, rope_sin, sr_b, sr_l, batch, heads, tok_begin,
-                        tok_begin + n_tokens, int(tok_begin / 64), max_blocks, ksum, vamax, lbq::device_status_ptr()};
+                        tok_begin + n_tokens, int(tok_begin / 64), max_blocks, ksum, vamax, lbq::device_status_ptr(),
+                        lbq::Ring{ring_sink, ring_len, ring_head}};
   cudaError_t e = lbq::launch_cache_write(a, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "cache_write launch");
 }
@@ -226,7 +246,7 @@ static int quant_kv_tiles_dt(const void* k, int64_t sk_b, int64_t sk_l, int64_t 
                              int seg_valid, int seg_len, int64_t kv_len_total, const double* ksum_total,
                              const float* vamax_total, int8_t* k_codes, float* k_scale, uint8_t* vt_codes,
                              void* km_out, float* v_scale, int write_totals, int tile_begin, int tile_end, int dtype,
-                             void* stream) {
+                             lbq::Ring ring, void* stream) {
   int r;
   if ((r = check_act("k", k, sk_b, sk_l, sk_h)) || (r = check_act("v", v, sv_b, sv_l, sv_h))) return r;
   if ((r = check_ptr("ksum_total", ksum_total)) || (r = check_ptr("vamax_total", vamax_total)) ||
@@ -248,9 +268,9 @@ static int quant_kv_tiles_dt(const void* k, int64_t sk_b, int64_t sk_l, int64_t 
   const int seg_pad = int(round_up(seg_len, 128));
   lbq::QuantKArgs ka{static_cast<const __nv_bfloat16*>(k), sk_b, sk_l, sk_h, batch, heads, tok0, seg, seg_valid,
                      seg_pad, kv_len_total, ksum_total, k_codes, k_scale,
-                     static_cast<__nv_bfloat16*>(km_out), write_totals, lbq::device_status_ptr(), dtype};
+                     static_cast<__nv_bfloat16*>(km_out), write_totals, lbq::device_status_ptr(), dtype, ring};
   lbq::QuantVArgs va{static_cast<const __nv_bfloat16*>(v), sv_b, sv_l, sv_h, batch, heads, tok0, seg, seg_valid,
-                     seg_pad, vamax_total, vt_codes, v_scale, write_totals, lbq::device_status_ptr(), dtype};
+                     seg_pad, vamax_total, vt_codes, v_scale, write_totals, lbq::device_status_ptr(), dtype, ring};
   cudaError_t e = lbq::launch_quant_kv(ka, va, tile_begin, tile_end - tile_begin, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "quant_kv launch");
 }
@@ -262,7 +282,7 @@ int lbq_quant_kv_tiles(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, 
                        float* v_scale, int write_totals, int tile_begin, int tile_end, void* stream) {
   return quant_kv_tiles_dt(k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h, batch, heads, tok0, seg, num_segments, seg_valid,
                            seg_len, kv_len_total, ksum_total, vamax_total, k_codes, k_scale, vt_codes, km_out,
-                           v_scale, write_totals, tile_begin, tile_end, 0, stream);
+                           v_scale, write_totals, tile_begin, tile_end, 0, lbq::Ring{0, 0, 0}, stream);
 }
 
 int lbq_quant_kv(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b, int64_t sv_l,
@@ -310,21 +330,22 @@ int lbq_quant_qkv(const void* q, int64_t sq_b, int64_t sq_l, int64_t sq_h, int q
   float* vamax = reinterpret_cast<float*>(ksum_total + cols);
   float* vamax_total = vamax + int64_t(nblk) * cols;
   int r = kv_block_stats_dt(k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h, batch, heads, kv_len, 0, nblk, nblk, ksum,
-                            vamax, dtype, stream);
+                            vamax, dtype, lbq::Ring{0, 0, 0}, stream);
   if (r) return r;
   if ((r = lbq_kv_window_sums(ksum, vamax, batch, heads, 0, nblk, nblk, ksum_total, vamax_total, stream))) return r;
   if ((r = quant_q_dt(q, sq_b, sq_l, sq_h, batch, heads, q_len, q_codes, q_scale, dtype, stream))) return r;
   return quant_kv_tiles_dt(k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h, batch, heads, 0, 0, 1, int(kv_len), int(kv_len),
                            kv_len, ksum_total, vamax_total, k_codes, k_scale, vt_codes, km_out, v_scale, 1, 0,
-                           int((kv_len + 127) / 128), dtype, stream);
+                           int((kv_len + 127) / 128), dtype, lbq::Ring{0, 0, 0}, stream);
 }
 
 int lbq_requant_cache(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b,
                       int64_t sv_l, int64_t sv_h, int batch, int heads, int64_t kv_len, int64_t max_blocks,
                       const double* ksum, const float* vamax, void* sums_ws, int8_t* k_codes, float* k_scale,
-                      uint8_t* vt_codes, float* v_scale, void* km_out, void* stream) {
+                      uint8_t* vt_codes, float* v_scale, void* km_out, int64_t ring_sink, int64_t ring_len,
+                      int64_t ring_head, void* stream) {
   int r;
-  if ((r = check_ptr("sums_ws", sums_ws))) return r;
+  if ((r = check_ptr("sums_ws", sums_ws)) || (r = check_ring(ring_sink, ring_len, ring_head, kv_len))) return r;
   if (kv_len <= 0 || kv_len > (int64_t(1) << 30)) return fail(LBQ_ERR_ARG, "kv_len %lld out of range", (long long)kv_len);
   const int nblk = int((kv_len + 63) / 64);
   if (nblk > max_blocks) return fail(LBQ_ERR_ARG, "kv_len %lld needs %d stats rows, table has %lld", (long long)kv_len,
@@ -333,8 +354,9 @@ int lbq_requant_cache(const void* k, int64_t sk_b, int64_t sk_l, int64_t sk_h, c
   double* ksum_total = static_cast<double*>(sums_ws);
   float* vamax_total = reinterpret_cast<float*>(ksum_total + cols);
   if ((r = lbq_kv_window_sums(ksum, vamax, batch, heads, 0, nblk, max_blocks, ksum_total, vamax_total, stream))) return r;
-  return lbq_quant_kv(k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h, batch, heads, 0, 0, 1, int(kv_len), int(kv_len),
-                      kv_len, ksum_total, vamax_total, k_codes, k_scale, vt_codes, km_out, v_scale, 1, stream);
+  return quant_kv_tiles_dt(k, sk_b, sk_l, sk_h, v, sv_b, sv_l, sv_h, batch, heads, 0, 0, 1, int(kv_len), int(kv_len),
+                           kv_len, ksum_total, vamax_total, k_codes, k_scale, vt_codes, km_out, v_scale, 1, 0,
+                           int((kv_len + 127) / 128), 0, lbq::Ring{ring_sink, ring_len, ring_head}, stream);
 }
 
 int lbq_attn_fwd(const int8_t* q_codes, const float* q_scale, int q_len, const int8_t* k_codes, const float* k_scale,

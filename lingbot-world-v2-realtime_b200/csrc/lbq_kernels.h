@@ -8,6 +8,18 @@
 
 namespace lbq {
 
+// Ring layout of a KV-cache buffer: logical token t (the reference's window position) lives at buffer
+// row t when t < sink, else at sink + ((t - sink + head) mod len). len == 0: rows are logical tokens.
+struct Ring {
+  int64_t sink, len, head;
+};
+__host__ __device__ inline int64_t phys_tok(const Ring& r, int64_t t) {
+  if (r.len == 0 || t < r.sink) return t;
+  int64_t u = t - r.sink + r.head;
+  if (u >= r.len) u -= r.len;
+  return r.sink + u;
+}
+
 struct KvBlockStatsArgs {
   const __nv_bfloat16* k;
   const __nv_bfloat16* v;
@@ -21,6 +33,7 @@ struct KvBlockStatsArgs {
   float* vamax;               // [B][max_blocks][H][128]
   int* status;                // device status word (debug-build index checks)
   int dtype;                  // activations: 0 bf16, 1 fp16
+  Ring ring;                  // k / v rows of logical tokens
 };
 
 struct KvWindowSumsArgs {
@@ -67,6 +80,7 @@ struct CacheWriteArgs {
   double* ksum;                 // [B][max_blocks][H][128]
   float* vamax;
   int* status;
+  Ring ring;                    // cache rows of logical tokens (tok_begin.. are logical)
 };
 
 struct QuantKArgs {
@@ -83,6 +97,7 @@ struct QuantKArgs {
   int write_km;
   int* status;                // device status word (debug-build index checks)
   int dtype;                  // k: 0 bf16, 1 fp16
+  Ring ring;                  // k rows of logical tokens
 };
 
 struct QuantVArgs {
@@ -97,6 +112,7 @@ struct QuantVArgs {
   int write_scale;
   int* status;                // device status word (debug-build index checks)
   int dtype;                  // v: 0 bf16, 1 fp16
+  Ring ring;                  // v rows of logical tokens
 };
 
 struct AttnArgs {

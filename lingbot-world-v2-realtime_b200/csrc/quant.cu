@@ -88,8 +88,9 @@ __global__ void __launch_bounds__(128) kv_block_stats_kernel(KvBlockStatsArgs a)
   for (int r = rg; r < 64; r += 8) {
     const int64_t tok = int64_t(blk) * 64 + r;
     if (tok >= a.kv_len) break;
-    const uint4 kr = *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + tok * a.sk_l + h * a.sk_h + c16 * 8);
-    const uint4 vr = *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + tok * a.sv_l + h * a.sv_h + c16 * 8);
+    const int64_t row = phys_tok(a.ring, tok);
+    const uint4 kr = *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + row * a.sk_l + h * a.sk_h + c16 * 8);
+    const uint4 vr = *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + row * a.sv_l + h * a.sv_h + c16 * 8);
     float kf[8], vf[8];
     act8_to_f32(kr, a.dtype, kf);
     act8_to_f32(vr, a.dtype, vf);
@@ -139,8 +140,9 @@ __global__ void __launch_bounds__(128) cache_write_kernel(CacheWriteArgs a) {
   for (int r = rg; r < 64; r += 8) {
     const int64_t tok = int64_t(blk) * 64 + r;
     if (tok >= a.tok_end) break;
-    __nv_bfloat16* kc = a.k_cache + b * a.ck_b + tok * a.ck_l + h * a.ck_h + c16 * 8;
-    __nv_bfloat16* vc = a.v_cache + b * a.cv_b + tok * a.cv_l + h * a.cv_h + c16 * 8;
+    const int64_t row = phys_tok(a.ring, tok);
+    __nv_bfloat16* kc = a.k_cache + b * a.ck_b + row * a.ck_l + h * a.ck_h + c16 * 8;
+    __nv_bfloat16* vc = a.v_cache + b * a.cv_b + row * a.cv_l + h * a.cv_h + c16 * 8;
     uint4 kr, vr;
     if (tok < a.tok_begin) {
       kr = *reinterpret_cast<const uint4*>(kc);
@@ -333,7 +335,8 @@ __device__ __forceinline__ void quant_k_tile(const QuantKArgs& a, QuantKvShared&
   for (int i = 0; i < 8; ++i) {
     const int64_t tok = int64_t(blk) * 64 + rg + 8 * i;      // token index inside this segment
     raw[i] = tok < a.seg_valid && LBQ_CHECK(a.tok0 + tok >= 0, a.status, kDevBadSourceToken)
-                 ? *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + (a.tok0 + tok) * a.sk_l + h * a.sk_h + c16 * 8)
+                 ? *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + phys_tok(a.ring, a.tok0 + tok) * a.sk_l +
+                                                   h * a.sk_h + c16 * 8)
                  : make_uint4(0u, 0u, 0u, 0u);
   }
   __syncthreads();
@@ -392,7 +395,8 @@ __device__ __forceinline__ void quant_v_tile(const QuantVArgs& a, QuantKvShared&
     const int r = piece >> 4, c16 = piece & 15;
     const int64_t tok = int64_t(tile) * 128 + r;
     const uint4 raw = tok < a.seg_valid && LBQ_CHECK(a.tok0 + tok >= 0, a.status, kDevBadSourceToken)
-                          ? *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + (a.tok0 + tok) * a.sv_l + h * a.sv_h + c16 * 8)
+                          ? *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + phys_tok(a.ring, a.tok0 + tok) * a.sv_l +
+                                                            h * a.sv_h + c16 * 8)
                           : make_uint4(0u, 0u, 0u, 0u);
     *reinterpret_cast<uint4*>(&sh.v[r * kVtPitch + c16 * 16]) = raw;
   }

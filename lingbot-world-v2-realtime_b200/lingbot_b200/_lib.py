@@ -20,13 +20,13 @@ SIGNATURES = {
     "lbq_last_error": (ctypes.c_char_p, []),
     "lbq_device_status": (_i32, [_i32, ctypes.POINTER(_i32)]),
     "lbq_kv_block_stats": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _i32, _i64, _i32, _i32,
-                                  _i64, _vp, _vp, _vp]),
+                                  _i64, _vp, _vp, _i64, _i64, _i64, _vp]),
     "lbq_kv_window_sums": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _i64, _vp, _vp, _vp]),
     "lbq_quant_q": (_i32, [_vp, _i64, _i64, _i64, _i32, _i32, _i32, _vp, _vp, _vp]),
     "lbq_rope_quant_q": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _vp, _vp, _vp]),
     "lbq_cache_write": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _i64,
                                _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _i32, _i64, _i64, _i64, _i64,
-                               _vp, _vp, _vp]),
+                               _vp, _vp, _i64, _i64, _i64, _vp]),
     "lbq_quant_kv": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _i32, _i64, _i32, _i32, _i32, _i32,
                             _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp]),
     "lbq_quant_qkv_workspace": (_sz, [_i32, _i32, _i64]),
@@ -35,7 +35,7 @@ SIGNATURES = {
     "lbq_quant_qkv_static": (_i32, [_vp, _i64, _i64, _i64, _i32, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
                                     _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp]),
     "lbq_requant_cache": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _i32, _i64, _i64, _vp, _vp,
-                                 _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+                                 _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "lbq_attn_fwd": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _i64,
                             _i64, _i64, _i32, _vp, _vp, ctypes.POINTER(_i32), _i32, _vp]),
     "lbq_splitkv_combine": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i32, _vp, _i64, _i64, _i64, _i32, _vp]),

@@ -7,6 +7,17 @@ beside each layer's K/V (fp64 K sums and max |V| per channel, the generalisation
 V min/max table, sage_preq.py:36-44,87-104): `write` refreshes the blocks it touched and `evict`
 the blocks after the sink, so `attend` re-quantizes the window with one read of the bf16 cache
 (window sums -> K/V codes) instead of two.
+
+With `allocate(..., ring=True)` the part of the buffer after the sink is a ring: an eviction moves
+a head index instead of shifting the window left by a copy (the reference's kv_cache.py:52-61; its
+ring-buffer attempt is experiments/modules/model_fast_kv_ring.py). Logical window token t — the row
+the reference would hold it in — lives at row t below the sink, else at
+sink + ((t - sink + head) mod (size - sink)); the cache kernels read and write through that map, and
+the quantized codes come out in logical order, so the attention is the same call. The statistics
+are kept per logical block: when the sink and the eviction are multiples of 64 tokens an eviction
+moves the rows of the table (a few MB) and nothing is re-read; otherwise the blocks after the sink
+are recomputed through the map (one read, where the shift costs a read and a write more). `window`
+of a ring cache materialises the logical slice (a copy), for callers that need bf16 K/V.
 """
 from __future__ import annotations
 
@@ -36,10 +47,13 @@ def heap_bytes(num_layers, shape, dtype):
     return num_layers * (2 * up(b * kv_size * h * d * esz) + up(b * nb * h * d * 8) + up(b * nb * h * d * 4))
 
 
-def allocate(num_layers, shape, dtype, device, heap=None):
+def allocate(num_layers, shape, dtype, device, heap=None, ring=False):
     """One cache dict per layer; `shape` is [batch, window tokens, heads, head_dim] (kv_cache.py:11-20).
     With a `peer.PeerHeap`, K, V and the block tables are carved from it (zeroed) so that the other
-    ranks of a sequence split can write the current chunk straight into this rank's replica."""
+    ranks of a sequence split can write the current chunk straight into this rank's replica.
+    ring=True: evictions move a ring head instead of copying (GPU caches; not with a peer heap)."""
+    if ring and heap is not None:
+        raise ValueError("a ring cache is per GPU: the sequence split's peer pushes write logical rows")
     caches = []
     for _ in range(num_layers):
         if heap is None:
@@ -60,8 +74,32 @@ def allocate(num_layers, shape, dtype, device, heap=None):
             'local_end_int': 0,
             'lbq_ksum': ksum,
             'lbq_vamax': vamax,
+            'lbq_ring': bool(ring),
+            'lbq_ring_sink': None,
+            'lbq_ring_head': 0,
         })
     return caches
+
+
+def ring_args(kv_cache):
+    """(sink, len, head) of a ring cache for the C ABI; (0, 0, 0) otherwise or before its first eviction
+    fixed the sink."""
+    sink = kv_cache.get("lbq_ring_sink")
+    if not kv_cache.get("lbq_ring") or sink is None:
+        return 0, 0, 0
+    return sink, kv_cache["k"].shape[1] - sink, kv_cache["lbq_ring_head"]
+
+
+def _ring_sink(kv_cache, sink_tokens):
+    """Fix (first call) or check the sink size of a ring cache."""
+    if not kv_cache.get("lbq_ring"):
+        return
+    if kv_cache["lbq_ring_sink"] is None:
+        if not kv_cache["k"].is_cuda:
+            raise ValueError("ring caches are GPU caches")
+        kv_cache["lbq_ring_sink"] = int(sink_tokens)
+    elif kv_cache["lbq_ring_sink"] != sink_tokens:
+        raise ValueError(f"ring cache built for a {kv_cache['lbq_ring_sink']}-token sink, called with {sink_tokens}")
 
 
 def plan(kv_cache, num_new_tokens, current_start, sink_tokens, local_attn_size):
@@ -102,12 +140,28 @@ def refresh_stats(kv_cache, tok_begin, tok_end):
     ksum, vamax = kv_cache["lbq_ksum"], kv_cache["lbq_vamax"]
     _lib.call("lbq_kv_block_stats", ops._ptr(k), *k.stride()[:3], ops._ptr(v), *v.stride()[:3], b, h, tok_end,
               tok_begin // BLK, (tok_end + BLK - 1) // BLK, ksum.shape[1], ops._ptr(ksum), ops._ptr(vamax),
-              ops._stream())
+              *ring_args(kv_cache), ops._stream())
 
 
 def evict(kv_cache, sink_tokens, evicted, rolled):
-    """Shift the window left past the sink to drop the oldest tokens (kv_cache.py:52-61), then
-    refresh the block statistics of everything after the sink."""
+    """Drop the oldest `evicted` tokens after the sink, keeping the `rolled` after them
+    (kv_cache.py:52-61): the reference shifts them left by a copy; a ring cache advances its head.
+    Then the block statistics of the tokens after the sink are brought up to date."""
+    _ring_sink(kv_cache, sink_tokens)
+    if kv_cache.get("lbq_ring"):
+        size = kv_cache["k"].shape[1]
+        kv_cache["lbq_ring_head"] = (kv_cache["lbq_ring_head"] + evicted) % (size - sink_tokens)
+        if sink_tokens % BLK == 0 and evicted % BLK == 0 and "lbq_ksum" in kv_cache:
+            # logical block b now holds what block b + evicted/64 held: move the statistics rows
+            b0, sh = sink_tokens // BLK, evicted // BLK
+            nfull = rolled // BLK
+            for t in (kv_cache["lbq_ksum"], kv_cache["lbq_vamax"]):
+                t[:, b0:b0 + nfull] = t[:, b0 + sh:b0 + sh + nfull].clone()
+            if rolled % BLK:                                   # the partial last block: recompute
+                refresh_stats(kv_cache, sink_tokens + nfull * BLK, sink_tokens + rolled)
+            return
+        refresh_stats(kv_cache, sink_tokens, sink_tokens + rolled)
+        return
     kv_cache["k"][:, sink_tokens:sink_tokens + rolled] = \
         kv_cache["k"][:, sink_tokens + evicted:sink_tokens + evicted + rolled].clone()
     kv_cache["v"][:, sink_tokens:sink_tokens + rolled] = \
@@ -143,7 +197,7 @@ def store(kv_cache, k, v, tok_begin, rope=None):
     rc, rs, sr_b, sr_l = _rope_args(rope)
     _lib.call("lbq_cache_write", ops._ptr(k), *k.stride()[:3], ops._ptr(v), *v.stride()[:3], rc, rs, sr_b, sr_l,
               ops._ptr(kc), *kc.stride()[:3], ops._ptr(vc), *vc.stride()[:3], b, h, kc.shape[1], tok_begin, n,
-              ksum.shape[1], ops._ptr(ksum), ops._ptr(vamax), ops._stream())
+              ksum.shape[1], ops._ptr(ksum), ops._ptr(vamax), *ring_args(kv_cache), ops._stream())
 
 
 def write(kv_cache, k, v, current_start, sink_tokens, local_attn_size, rope=None):
@@ -153,6 +207,7 @@ def write(kv_cache, k, v, current_start, sink_tokens, local_attn_size, rope=None
     caller that would otherwise pass causal_rope_apply(k, rope)."""
     evicted, rolled, local_start_index, local_end_index, current_end = plan(
         kv_cache, k.shape[1], current_start, sink_tokens, local_attn_size)
+    _ring_sink(kv_cache, sink_tokens)
     if evicted:
         evict(kv_cache, sink_tokens, evicted, rolled)
     if kv_cache["k"].is_cuda:
@@ -167,9 +222,15 @@ def write(kv_cache, k, v, current_start, sink_tokens, local_attn_size, rope=None
 
 
 def window(kv_cache, local_end_index, max_attention_size):
-    """The K/V slice this forward attends to (kv_cache.py:78-81)."""
+    """The K/V slice this forward attends to (kv_cache.py:78-81). A ring cache returns the logical
+    slice as a copy (the rows gathered in window order)."""
     start = max(0, local_end_index - max_attention_size)
-    return kv_cache["k"][:, start:local_end_index], kv_cache["v"][:, start:local_end_index]
+    sink, rlen, head = ring_args(kv_cache)
+    if rlen == 0 or head == 0:
+        return kv_cache["k"][:, start:local_end_index], kv_cache["v"][:, start:local_end_index]
+    t = torch.arange(start, local_end_index, device=kv_cache["k"].device)
+    rows = torch.where(t < sink, t, sink + (t - sink + head) % rlen)
+    return kv_cache["k"][:, rows], kv_cache["v"][:, rows]
 
 
 def commit(kv_cache, current_end, local_end_index):
@@ -212,7 +273,8 @@ def quantize_window(q, kv_cache, end, quantizer=None, rope=None) -> ops.QuantWin
     ksum, vamax = kv_cache["lbq_ksum"], kv_cache["lbq_vamax"]
     _lib.call("lbq_requant_cache", ops._ptr(k), *k.stride()[:3], ops._ptr(v), *v.stride()[:3], b, h, end,
               ksum.shape[1], ops._ptr(ksum), ops._ptr(vamax), ops._ptr(qz.sums), ops._ptr(qz.k_codes),
-              ops._ptr(qz.k_scale), ops._ptr(qz.vt_codes), ops._ptr(qz.v_scale), ops._ptr(qz.km), st)
+              ops._ptr(qz.k_scale), ops._ptr(qz.vt_codes), ops._ptr(qz.v_scale), ops._ptr(qz.km),
+              *ring_args(kv_cache), st)
     if rope is None:
         _lib.call("lbq_quant_q", ops._ptr(q), *q.stride()[:3], b, h, lq, ops._ptr(qz.q_codes), ops._ptr(qz.q_scale),
                   st)

@@ -222,7 +222,8 @@ class SplitAttention:
         group = self._group()
         if nb_valid > 0:
             _lib.call("lbq_kv_block_stats", *self._share(k_part, v_part), b, h, self.share_valid, 0, nb_valid,
-                      max_blocks, ksum.data_ptr() + row0 * h * 128 * 8, vamax.data_ptr() + row0 * h * 128 * 4, stp)
+                      max_blocks, ksum.data_ptr() + row0 * h * 128 * 8, vamax.data_ptr() + row0 * h * 128 * 4,
+                      0, 0, 0, stp)
         _lib.call("lbq_share_totals_push", ops._ptr(ksum), ops._ptr(vamax), max_blocks, row0, nb_valid, b, h,
                   *group, stp)
         _lib.call("lbq_chunk_totals", *group, b, h, ops._ptr(cache["lbq_mem_ksum"]), ops._ptr(cache["lbq_mem_vamax"]),
