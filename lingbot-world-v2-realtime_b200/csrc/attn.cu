@@ -17,9 +17,10 @@
 // exp2 is ex2.approx (upstream's ptx_exp2). Differences from the sm89 kernel: P.V accumulates in fp32 in
 // tensor memory where Sage sums each 64-key tile in fp16; and in the bulk tiles (full 128-key tiles
 // other than the last two 64-key tiles) x is fma(1.5*2^23 + S, c, fl(-1.5*2^23 * c - m)) where
-// 1.5*2^23 * c < 4096 (within 2^-13 of upstream's x), and 2 of every 16 key pairs take a degree-3
-// polynomial exp2 (relative error 7.5e-5). Both can move a P across an e4m3 rounding midpoint only when it lies
-// that close to one; the masked and last two tiles, where few keys carry the row, are exact.
+// 1.5*2^23 * c < 4096 (within 2^-13 of upstream's x), where also 2 of every 16 key pairs take a
+// degree-3 polynomial exp2 (relative error 7.5e-5). Both can move a P across an e4m3 rounding midpoint
+// only when it lies that close to one; the masked and last two tiles, where few keys carry the row, are
+// exact.
 //
 // CTA = two 128-row Q tiles (A, B) x one (batch, head) x one KV split, 512 threads:
 //   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B: one thread per row (= TMEM lane);
@@ -66,8 +67,9 @@ constexpr uint32_t kColS = 0, kColO = 256;
 constexpr uint32_t kRegSoftmax = 160, kRegCorrection = 120, kRegMisc = 72;
 static_assert(128 * (2 * kRegSoftmax + kRegCorrection + kRegMisc) <= kAttnThreads * 128, "register split");
 
-// In the bulk tiles, of every 16 key pairs this many take the FMA-pipe polynomial exp2 (relative error
-// 7.5e-5) instead of MUFU ex2, which is the busiest unit (measured: 2 of 16 is the fastest split).
+// In the bulk tiles with the folded exp2 argument, of every 16 key pairs this many take the FMA-pipe
+// polynomial exp2 (relative error 7.5e-5) instead of MUFU ex2, the busiest unit (measured: 2 of 16 is
+// the fastest split; with the exact argument, MUFU for every key is faster).
 constexpr int kPolyPairs = 2;
 
 struct AttnShared {
@@ -264,7 +266,7 @@ __device__ __forceinline__ float2 tile128_exp(const uint32_t* sv, float2 smax, f
       float x0, x1;
       f2_unpack(x, x0, x1);
       uint64_t p;
-      if (((j >> 1) & 15) >= 16 - kPolyPairs) {
+      if (kFold && ((j >> 1) & 15) >= 16 - kPolyPairs) {
         p = exp2_poly_x2(x0, x1);
       } else {
         p = f2_pack(ex2_approx(x0), ex2_approx(x1));

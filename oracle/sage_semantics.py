@@ -234,8 +234,8 @@ EXP2_REL_ERR = 2.0 ** -20
 AMBIGUOUS_IMPACT = 1e-2
 # The GPU kernel's bulk tiles (all but the last two 64-key tiles of a pass) evaluate the exp2 argument as
 # fma(1.5*2^23 + S, c, fl(-1.5*2^23 * c - m)) where fl(1.5*2^23 * c) < FOLD_MAX (for both 64-key tiles of
-# a 128-key tile; taking the bound per 64-key tile here only widens the window), and take some keys'
-# exp2 from a degree-3 polynomial (max relative error 7.48e-5, measured on a 2e6-point grid of
+# a 128-key tile; taking the bound per 64-key tile here only widens the window), and there take some
+# keys' exp2 from a degree-3 polynomial (max relative error 7.48e-5, measured on a 2e6-point grid of
 # [-0.5, 0.5], plus fp32 rounding).
 KERNEL_MAGIC = 12582912.0
 FOLD_MAX = 4096.0
@@ -249,13 +249,15 @@ def _ulp32(v: torch.Tensor) -> torch.Tensor:
 
 
 def bulk_rel_err(x: torch.Tensor, scale: torch.Tensor, m_new: torch.Tensor) -> torch.Tensor:
-    """Bound on the relative error of the GPU kernel's P in a bulk tile, per element: ex2 or the
-    polynomial, plus ln 2 times the argument's error (one ulp of x, and where the kernel folds the
-    magic bias into the argument half an ulp of the folded constant fl(-1.5*2^23 * c - m))."""
+    """Bound on the relative error of the GPU kernel's P in a bulk tile, per element: ex2, plus ln 2
+    times one ulp of x; and where the kernel folds the magic bias into the argument (and then takes some
+    keys' exp2 from the polynomial), the polynomial's error and ln 2 times half an ulp of the folded
+    constant fl(-1.5*2^23 * c - m)."""
     fold = (torch.tensor(KERNEL_MAGIC, dtype=torch.float32) * scale.float()) < FOLD_MAX
     b = _fma32(torch.full_like(scale, -KERNEL_MAGIC), scale, -m_new)
-    arg = torch.where(fold, 0.5 * _ulp32(b), torch.zeros_like(b, dtype=torch.float64))[:, None] + _ulp32(x)
-    return EXP2_REL_ERR + POLY_REL_ERR + math.log(2.0) * arg
+    zero = torch.zeros_like(b, dtype=torch.float64)
+    extra = torch.where(fold, POLY_REL_ERR + math.log(2.0) * 0.5 * _ulp32(b), zero)
+    return EXP2_REL_ERR + extra[:, None] + math.log(2.0) * _ulp32(x)
 
 
 def _ambiguous_steps(p: torch.Tensor, m: torch.Tensor, rel_err=EXP2_REL_ERR) -> torch.Tensor:
