@@ -61,7 +61,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["chunk", "call", "requant", "streams", "cross", "keys-rank", "evict"],
+    ap.add_argument("--workload", choices=["chunk", "call", "requant", "streams", "cross", "keys-rank", "evict", "linear"],
                     default="chunk")
     ap.add_argument("--ranks", type=int, default=8, help="--workload keys-rank: ranks of the emulated split")
     ap.add_argument("--rank", type=int, default=1, help="--workload keys-rank: the emulated rank")
@@ -898,6 +898,71 @@ def run_keys_rank(args, world, rank, local):
                           "peak_source": f"2 x bf16_tflops burst ({src})", "attn_ms_per_call": round(attn_ms, 4)})
 
 
+def run_linear(args, world, rank, local):
+    """FP8 linears of one DiT layer (lingbot/layers/linear.py FP8Linear on the q, k, v, o projections,
+    1536 -> 1536, and the FFN, 1536 -> 8960 -> 1536) over one chunk's 6032 tokens: per-token activation
+    quantization + tcgen05 FP8 GEMM with the row scales and bias in its epilogue. Timed beside the
+    reference's own forward on the same GPU: the activation quantization in torch ops and
+    torch._scaled_mm (cuBLASLt) with rowwise scales."""
+    from lingbot_b200.fp8_linear import FP8Linear
+    dev = torch.device("cuda", local)
+    torch.manual_seed(0)
+    dims = [(1536, 1536)] * 4 + [(1536, 8960), (8960, 1536)]
+    lins = [torch.nn.Linear(i, o).bfloat16().to(dev) for i, o in dims]
+    ours = [FP8Linear(l) for l in lins]
+    xs = {i: torch.randn(1, LQ, i, device=dev).bfloat16() for i in (1536, 8960)}
+    flops = sum(2.0 * LQ * i * o for i, o in dims)
+
+    def ref_prep(l):
+        w = l.weight.detach()
+        ws = (w.abs().amax(dim=1, keepdim=True).float() / 448.0).clamp(min=1e-12)
+        return (w.float() / ws).to(torch.float8_e4m3fn), ws.t().contiguous(), l.bias.to(torch.bfloat16)
+    refs = [ref_prep(l) for l in lins]
+
+    def ref_fwd(x, w8, wst, b):
+        x2 = x.reshape(-1, x.shape[-1])
+        sc = (x2.abs().amax(dim=1, keepdim=True).float() / 448.0).clamp(min=1e-12)
+        x8 = (x2.float() / sc).to(torch.float8_e4m3fn)
+        return torch._scaled_mm(x8, w8.t(), scale_a=sc, scale_b=wst, bias=b, out_dtype=torch.bfloat16)
+
+    def fn_ours():
+        for (i, _), m in zip(dims, ours):
+            m(xs[i])
+
+    def fn_ref():
+        for (i, _), r in zip(dims, refs):
+            ref_fwd(xs[i], *r)
+    ms, clocks = _timed(fn_ours, args.steps, args.warmup, dev, world)
+    ms_ref, _ = _timed(fn_ref, args.steps, args.warmup, dev, world)
+    from lingbot_b200 import fp8_linear as L
+    q, s = L.quant_rows(xs[1536][0])
+    big = ours[4]
+    for _ in range(3):
+        L.gemm(q, s, big.w8, big.w_scale, big.bias)
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record()
+    for _ in range(10):
+        L.gemm(q, s, big.w8, big.w_scale, big.bias)
+    a1.record()
+    torch.cuda.synchronize()
+    gemm_ms = a0.elapsed_time(a1) / 10
+    gemm_tops = 2.0 * LQ * 1536 * 8960 / (gemm_ms * 1e-3) / 1e12
+    peaks, src = measured_peaks()
+    peak = 2.0 * peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+    tops = flops / (ms * 1e-3) / 1e12
+    return dict(tops=tops, ms=ms, clocks=clocks, launches=2 * len(dims) * args.steps, e2e=None,
+                roofline={"bound": "tensor", "achieved": round(gemm_tops, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                          "frac": round(gemm_tops / peak, 4), "traffic": None, "kernel": "fp8_gemm_kernel",
+                          "peak_source": f"2 x bf16_tflops_sustained ({src}); B200's dense FP8 rate is twice its bf16 rate",
+                          "shape": f"{LQ} x 8960 x 1536", "gemm_ms": round(gemm_ms, 4)},
+                config={"workload": "FP8 linears of one DiT layer (q, k, v, o, FFN up and down), 6032 tokens",
+                        "layers": [f"{i}->{o}" for i, o in dims], "tokens": LQ,
+                        "reference_ms": round(ms_ref, 4),
+                        "reference_tops": round(flops / (ms_ref * 1e-3) / 1e12, 1),
+                        "reference": "torch ops + torch._scaled_mm (cuBLASLt), rowwise scales, as linear.py:22-31",
+                        "parallelism": "single GPU"})
+
+
 def run_evict(args, world, rank, local):
     """The memory-write pass's cache write with an eviction, per chunk (30 layers): a full window of
     30160 tokens with a one-frame sink (1508 tokens) takes the chunk's 6032 tokens, dropping the oldest
@@ -1029,6 +1094,8 @@ def main():
             res = run_keys_rank(args, world, rank, local)
         elif args.workload == "evict":
             res = run_evict(args, world, rank, local)
+        elif args.workload == "linear":
+            res = run_linear(args, world, rank, local)
         else:
             res = run_requant(args, world, rank, local)
         if rank == 0:
@@ -1045,7 +1112,8 @@ def main():
                       "streams": "aggregate attention TOPS, independent streams (BASELINE config 5)",
                       "cross": "cross-attention TOPS, quantized (q 6032 x 512 text keys; quantize + attend)",
                       "keys-rank": "key-range attention TOPS of one emulated rank (BASELINE config 4)",
-                      "evict": "KV-cache write with eviction, ms per chunk (30 layers)"}[args.workload]
+                      "evict": "KV-cache write with eviction, ms per chunk (30 layers)",
+                      "linear": "FP8 linear TOPS, one DiT layer's projections and FFN (6032 tokens)"}[args.workload]
             line = {"metric": metric,
                     "value": round(res["tops"], 2), "unit": res.get("unit", "TOPS"), "n_gpus": world, "steps": args.steps,
                     "warmup": args.warmup, "ms_per_step": round(res["ms"], 3), "s_per_chunk": round(res["ms"] / 1e3, 5),

@@ -233,6 +233,22 @@ LBQ_API int lbq_keys_combine(const void* recv_o, const float* recv_ml, int nrank
                      const float* v_scale, int batch, int heads, void* out, int64_t so_b,
                      int64_t so_l, int64_t so_h, void* stream);
 
+/* Rowwise FP8 quantization of FP8Linear (lingbot/layers/linear.py:16-18 for weights, :24-26 for the
+ * activations of each call): per row, s = max(fl(max|x| / 448), 1e-12) and q = e4m3(fl(x / s)) with
+ * true fp32 divisions. x [rows][cols], row stride sx elements, dtype 0 bf16 / 1 fp16 / 2 fp32;
+ * q [rows][cols] e4m3 bytes, row stride sq; scale [rows] f32. cols a multiple of 16. */
+LBQ_API int lbq_fp8_quant_rows(const void* x, int64_t sx, int dtype, int rows, int cols, uint8_t* q, int64_t sq,
+                               float* scale, void* stream);
+
+/* FP8 GEMM of FP8Linear.forward (lingbot/layers/linear.py:27-29, torch._scaled_mm with rowwise scales):
+ * y [M][N] bf16 (row stride sy elements) = (a [M][K] . w [N][K]^T) * a_scale[m] * w_scale[n] + bias[n]
+ * (bias bf16 [N] or null), e4m3 operands with row strides sa / sw bytes, fp32 accumulation on the
+ * tensor cores. N a multiple of 32, K of 16. num_ctas <= 0: one CTA per SM (persistent over the
+ * 128 x 256 output tiles). */
+LBQ_API int lbq_fp8_gemm(const uint8_t* a, int64_t sa, const float* a_scale, const uint8_t* w, int64_t sw,
+                         const float* w_scale, const void* bias, int M, int N, int K, void* y, int64_t sy,
+                         int num_ctas, void* stream);
+
 /* Flash-decoding merge of lbq_attn_fwd's split partials into out (in `dtype`), applying the V scale.
  * The combine kernel of experiments/bench_attn/splitkv/README.md:67-69 (`splitkv_combine_kernel`). */
 LBQ_API int lbq_splitkv_combine(const float* o_part, const float* ml_part, int num_splits,

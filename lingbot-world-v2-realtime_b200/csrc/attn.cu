@@ -838,17 +838,7 @@ __global__ void __launch_bounds__(128) keys_combine_kernel(const KeysCombineArgs
 template <bool kKeyRange>
 cudaError_t launch_attn_variant(const AttnArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                                 const CUtensorMap& tm_v, cudaStream_t st) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  static bool configured[64] = {};
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!configured[dev]) {
-    e = cudaFuncSetAttribute(attn_fwd_kernel<kKeyRange>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             int(kAttnSmemBytes));
-    if (e != cudaSuccess) return e;
-    configured[dev] = true;
-  }
+  if (cudaError_t e = allow_dynamic_smem<attn_fwd_kernel<kKeyRange>>(int(kAttnSmemBytes)); e != cudaSuccess) return e;
   dim3 grid((a.q_pad / 128 + 1) / 2, a.batch * a.heads, a.num_splits);
   if (cudaError_t e0 = prefer_max_shared<attn_fwd_kernel<kKeyRange>>(); e0 != cudaSuccess) return e0;
   attn_fwd_kernel<kKeyRange><<<grid, kAttnThreads, kAttnSmemBytes, st>>>(tm_q, tm_k, tm_v, a);

@@ -82,12 +82,12 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 3-D uint8 tensor map with a 128 x 128 box and 128-byte swizzle.
 int make_map(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
-             uint64_t stride2, const char* name) {
+             uint64_t stride2, const char* name, uint32_t box_rows = 128) {
   auto fn = encode_fn();
   if (fn == nullptr) return fail(LBQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
   const cuuint64_t dims[3] = {d0, d1, d2};
   const cuuint64_t strides[2] = {stride1, stride2};
-  const cuuint32_t box[3] = {128, 128, 1};
+  const cuuint32_t box[3] = {128, box_rows, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -430,6 +430,61 @@ int lbq_attn_fwd(const int8_t* q_codes, const float* q_scale, int q_len, const i
   a.status = lbq::device_status_ptr();
   cudaError_t e = lbq::launch_attn(a, tq, tk, tv, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "attn_fwd launch");
+}
+
+int lbq_fp8_quant_rows(const void* x, int64_t sx, int dtype, int rows, int cols, uint8_t* q, int64_t sq,
+                       float* scale, void* stream) {
+  int r;
+  if ((r = check_ptr("x", x)) || (r = check_ptr("q", q)) || (r = check_ptr("scale", scale))) return r;
+  if (dtype < 0 || dtype > 2) return fail(LBQ_ERR_ARG, "dtype %d is not bf16 (0), fp16 (1) or fp32 (2)", dtype);
+  if (rows < 0 || cols <= 0 || cols % 16) return fail(LBQ_ERR_ARG, "cols %d must be a positive multiple of 16", cols);
+  const int esize = dtype == 2 ? 4 : 2;
+  if ((sx * esize) % 16 || sq % 16 || sx < cols || sq < cols)
+    return fail(LBQ_ERR_ALIGN, "row strides (%lld elements, %lld bytes) must cover a row and be 16-byte multiples",
+                (long long)sx, (long long)sq);
+  if (rows == 0) return LBQ_OK;
+  lbq::Fp8QuantArgs a{x, sx, esize, dtype, rows, cols, q, sq, scale};
+  cudaError_t e = lbq::launch_fp8_quant_rows(a, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "fp8_quant_rows launch");
+}
+
+int lbq_fp8_gemm(const uint8_t* a, int64_t sa, const float* a_scale, const uint8_t* w, int64_t sw,
+                 const float* w_scale, const void* bias, int M, int N, int K, void* y, int64_t sy, int num_ctas,
+                 void* stream) {
+  int r;
+  if ((r = check_ptr("a", a)) || (r = check_ptr("a_scale", a_scale)) || (r = check_ptr("w", w)) ||
+      (r = check_ptr("w_scale", w_scale)) || (r = check_ptr("y", y)))
+    return r;
+  if (bias != nullptr && !aligned16(bias)) return fail(LBQ_ERR_ALIGN, "bias is not 16-byte aligned");
+  if (M <= 0 || N <= 0 || K <= 0 || N % 32 || K % 16)
+    return fail(LBQ_ERR_ARG, "M %d, N %d, K %d: N must be a multiple of 32 and K of 16", M, N, K);
+  if (sa % 16 || sw % 16 || sa < K || sw < K || sy % 8 || sy < N)
+    return fail(LBQ_ERR_ALIGN, "row strides (a %lld, w %lld bytes; y %lld elements) must cover a row and be 16-byte "
+                "multiples", (long long)sa, (long long)sw, (long long)sy);
+  CUtensorMap ta, tb;
+  if ((r = make_map(&ta, a, uint64_t(K), uint64_t(M), 1, uint64_t(sa), uint64_t(sa) * M, "a", 128))) return r;
+  if ((r = make_map(&tb, w, uint64_t(K), uint64_t(N), 1, uint64_t(sw), uint64_t(sw) * N, "w", 256))) return r;
+  lbq::Fp8GemmArgs g{};
+  g.x_scale = a_scale;
+  g.w_scale = w_scale;
+  g.bias = static_cast<const __nv_bfloat16*>(bias);
+  g.y = static_cast<__nv_bfloat16*>(y);
+  g.sy = sy;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.tiles_m = (M + 127) / 128;
+  g.tiles_n = (N + 255) / 256;
+  g.status = lbq::device_status_ptr();
+  const int tiles = g.tiles_m * g.tiles_n;
+  if (num_ctas <= 0) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    num_ctas = sms;
+  }
+  if (num_ctas > tiles) num_ctas = tiles;
+  cudaError_t e = lbq::launch_fp8_gemm(g, ta, tb, num_ctas, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LBQ_OK : cuda_fail(e, "fp8_gemm launch");
 }
 
 int lbq_splitkv_combine(const float* o_part, const float* ml_part, int num_splits, const float* v_scale, int batch,

@@ -4,9 +4,35 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <atomic>
 #include <cstdint>
 
 namespace lbq {
+
+// Rowwise FP8 quantization (lingbot/layers/linear.py:FP8Linear): x [rows][cols] (row stride sx
+// elements, dtype 0 bf16 / 1 fp16 / 2 fp32) -> e4m3 codes q [rows][cols] (row stride sq bytes) and one
+// fp32 scale per row.
+struct Fp8QuantArgs {
+  const void* x;
+  int64_t sx;
+  int esize, dtype;
+  int rows, cols;
+  uint8_t* q;
+  int64_t sq;
+  float* scale;
+};
+// y [M][N] bf16 (row stride sy) = (q_x [M][K] . q_w [N][K]^T) * x_scale[m] * w_scale[n] + bias[n].
+constexpr int kGemmThreads = 192;
+struct Fp8GemmArgs {
+  const float* x_scale;
+  const float* w_scale;
+  const __nv_bfloat16* bias;    // [N] or null
+  __nv_bfloat16* y;
+  int64_t sy;
+  int M, N, K;
+  int tiles_m, tiles_n;
+  int* status;
+};
 
 // Ring layout of a KV-cache buffer: logical token t (the reference's window position) lives at buffer
 // row t when t < sink, else at sink + ((t - sink + head) mod len). len == 0: rows are logical tokens.
@@ -269,6 +295,9 @@ struct PeerWaitArgs {
 cudaError_t launch_kv_block_stats(const KvBlockStatsArgs& a, cudaStream_t st);
 cudaError_t launch_kv_window_sums(const KvWindowSumsArgs& a, cudaStream_t st);
 cudaError_t launch_quant_q(const QuantQArgs& a, cudaStream_t st);
+cudaError_t launch_fp8_quant_rows(const Fp8QuantArgs& a, cudaStream_t st);
+cudaError_t launch_fp8_gemm(const Fp8GemmArgs& a, const CUtensorMap& tm_a, const CUtensorMap& tm_b, int ctas,
+                            cudaStream_t st);
 cudaError_t launch_cache_write(const CacheWriteArgs& a, cudaStream_t st);
 cudaError_t launch_quant_kv(const QuantKArgs& ka, const QuantVArgs& va, int tile0, int tiles, cudaStream_t st);
 cudaError_t launch_attn(const AttnArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
@@ -295,15 +324,31 @@ int* device_status_ptr();
 template <auto Kernel>
 inline cudaError_t prefer_max_shared() {
   if (LBQ_CARVEOUT < 0) return cudaSuccess;
-  static bool done[64] = {};
+  // per-device flags; two host threads may both set the (idempotent) attribute, nothing races
+  static std::atomic<bool> done[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!done[dev]) {
+  if (!done[dev].load(std::memory_order_acquire)) {
     e = cudaFuncSetAttribute(Kernel, cudaFuncAttributePreferredSharedMemoryCarveout, int(LBQ_CARVEOUT));
     if (e != cudaSuccess) return e;
-    done[dev] = true;
+    done[dev].store(true, std::memory_order_release);
+  }
+  return cudaSuccess;
+}
+// Allows `Kernel` `bytes` of dynamic shared memory on the current device (once per device, as above).
+template <auto Kernel>
+inline cudaError_t allow_dynamic_smem(int bytes) {
+  static std::atomic<bool> done[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!done[dev].load(std::memory_order_acquire)) {
+    e = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return e;
+    done[dev].store(true, std::memory_order_release);
   }
   return cudaSuccess;
 }

@@ -38,6 +38,8 @@ SIGNATURES = {
                                  _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "lbq_attn_fwd": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _i64,
                             _i64, _i64, _i32, _vp, _vp, ctypes.POINTER(_i32), _i32, _vp]),
+    "lbq_fp8_quant_rows": (_i32, [_vp, _i64, _i32, _i32, _i32, _vp, _i64, _vp, _vp]),
+    "lbq_fp8_gemm": (_i32, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _i32, _i32, _i32, _vp, _i64, _i32, _vp]),
     "lbq_splitkv_combine": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i32, _vp, _i64, _i64, _i64, _i32, _vp]),
     "lbq_peer_export": (_i32, [_vp, _vp, ctypes.POINTER(ctypes.c_uint64)]),
     "lbq_peer_open": (_i32, [_vp, ctypes.POINTER(_vp)]),

@@ -11,7 +11,7 @@ ROOT = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(ROOT, "csrc")
 LIB = os.path.join(PKG_DIR, "liblbq.so")
 DEBUG_LIB = os.path.join(PKG_DIR, "liblbq_debug.so")
-SOURCES = ["quant.cu", "attn.cu", "capi.cu", "noalloc.cu", "peer.cu", "capi_peer.cu"]
+SOURCES = ["quant.cu", "attn.cu", "fp8lin.cu", "capi.cu", "noalloc.cu", "peer.cu", "capi_peer.cu"]
 HEADERS = ["lbq_ptx.cuh", "lbq_kernels.h", "lbq_peer.cuh", os.path.join("..", "..", "include", "lbq.h")]
 
 

@@ -16,6 +16,10 @@ What it records:
     transformer.py:553-558), `causal_rope_freqs` for a two-sample batch (transformer.py:53-76) and
     `causal_rope_apply` of a bf16 input (transformer.py:134-146). transformer.py itself imports
     diffusers and the Wan model, so the three functions are taken from its source text and run alone.
+  * fp8_linear.npz — the reference's rowwise FP8Linear (lingbot/layers/linear.py:10-31) built from a
+    seeded bf16 nn.Linear: its e4m3 weights and row scales, and the e4m3 activations and row scales
+    its forward hands to torch._scaled_mm (recorded by intercepting that call, which has no rowwise CPU
+    kernel), for an input with a zero row.
   * kv_schedule.json — the host bookkeeping of `lingbot/layers/kv_cache.py` (plan/evict/write/
     window/commit) over the write / rewrite / eviction schedule of
     `experiments/bench_attn/sage_preq_check.py:11-36`, with float64 (order-independent) checksums of the cache buffers after
@@ -69,6 +73,33 @@ def rope_golden(ref):
     # the first 16 positions of the table cover every frame, row and column used here
     return dict(freqs16=freqs[:16].numpy(), grid=np.array(grid), start_frame=np.array(5),
                 cos=cos[:, :, 0].numpy(), sin=sin[:, :, 0].numpy(), x=bf16_bits(x), out=bf16_bits(out))
+
+
+def fp8_golden(ref):
+    lin_mod = load(os.path.join(ref, "lingbot/layers/linear.py"), "ref_linear")
+    g = torch.Generator().manual_seed(88)
+    lin = torch.nn.Linear(256, 96).bfloat16()
+    with torch.no_grad():
+        lin.weight.copy_((torch.randn(96, 256, generator=g) * 0.05).bfloat16())
+        lin.bias.copy_((torch.randn(96, generator=g) * 0.1).bfloat16())
+    f = lin_mod.FP8Linear(lin)
+    x = (torch.randn(7, 256, generator=g) * 3).bfloat16()
+    x[3] = 0
+    seen = {}
+
+    def record(a, b, scale_a=None, scale_b=None, bias=None, out_dtype=None):
+        seen.update(x8=a, xs=scale_a, w8t=b, ws=scale_b)
+        return torch.zeros(a.shape[0], b.shape[1], dtype=out_dtype)
+    real = torch._scaled_mm
+    torch._scaled_mm = record
+    try:
+        f(x)
+    finally:
+        torch._scaled_mm = real
+    u8 = lambda t: t.contiguous().view(torch.uint8).numpy()  # noqa: E731
+    return dict(weight=bf16_bits(lin.weight.detach()), bias=bf16_bits(lin.bias.detach()), x=bf16_bits(x),
+                w8=u8(f.w8), w_scale=f.w_scale_t.numpy(), x8=u8(seen["x8"]), x_scale=seen["xs"].numpy(),
+                w8_seen=u8(seen["w8t"].t()), w_scale_seen=seen["ws"].numpy())
 
 
 def bf16_bits(x):
@@ -167,6 +198,8 @@ def main():
         np.savez_compressed(os.path.join(HERE, f"quant_{name}.npz"), meta=meta, **out)
         print("wrote", name)
     np.savez_compressed(os.path.join(HERE, "rope_grid2x4x6.npz"), **rope_golden(args.ref))
+    np.savez_compressed(os.path.join(HERE, "fp8_linear.npz"), **fp8_golden(args.ref))
+    print("wrote fp8_linear.npz")
     print("wrote rope_grid2x4x6.npz")
     with open(os.path.join(HERE, "kv_schedule.json"), "w") as f:
         json.dump(kv_schedule(kvc), f, indent=1)
