@@ -947,6 +947,15 @@ def run_linear(args, world, rank, local):
     torch.cuda.synchronize()
     gemm_ms = a0.elapsed_time(a1) / 10
     gemm_tops = 2.0 * LQ * 1536 * 8960 / (gemm_ms * 1e-3) / 1e12
+    w8r, wsr, br = refs[4]                              # cuBLASLt on the same operands, for comparison
+    for _ in range(3):
+        torch._scaled_mm(q, w8r.t(), scale_a=s.reshape(-1, 1), scale_b=wsr, bias=br, out_dtype=torch.bfloat16)
+    a0.record()
+    for _ in range(10):
+        torch._scaled_mm(q, w8r.t(), scale_a=s.reshape(-1, 1), scale_b=wsr, bias=br, out_dtype=torch.bfloat16)
+    a1.record()
+    torch.cuda.synchronize()
+    cublas_ms = a0.elapsed_time(a1) / 10
     peaks, src = measured_peaks()
     peak = 2.0 * peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
     tops = flops / (ms * 1e-3) / 1e12
@@ -954,7 +963,9 @@ def run_linear(args, world, rank, local):
                 roofline={"bound": "tensor", "achieved": round(gemm_tops, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
                           "frac": round(gemm_tops / peak, 4), "traffic": None, "kernel": "fp8_gemm_kernel",
                           "peak_source": f"2 x bf16_tflops_sustained ({src}); B200's dense FP8 rate is twice its bf16 rate",
-                          "shape": f"{LQ} x 8960 x 1536", "gemm_ms": round(gemm_ms, 4)},
+                          "shape": f"{LQ} x 8960 x 1536", "gemm_ms": round(gemm_ms, 4),
+                          "scaled_mm_ms": round(cublas_ms, 4),
+                          "scaled_mm_tflops": round(2.0 * LQ * 1536 * 8960 / (cublas_ms * 1e-3) / 1e12, 1)},
                 config={"workload": "FP8 linears of one DiT layer (q, k, v, o, FFN up and down), 6032 tokens",
                         "layers": [f"{i}->{o}" for i, o in dims], "tokens": LQ,
                         "reference_ms": round(ms_ref, 4),
