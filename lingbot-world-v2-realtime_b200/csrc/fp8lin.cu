@@ -11,8 +11,10 @@
 // persistent tcgen05 kernel: 128 x 256 output tiles, e4m3 x e4m3 -> fp32 in tensor memory (kind::f8f6f4,
 // M = 128, N = 256, K = 32 per instruction), operands staged by TMA (128-byte swizzle, 128-byte K steps,
 // 4 stages of 48 KB), two 256-column accumulators so the epilogue of one tile overlaps the main loop of
-// the next. 192 threads: warp 0 TMA producer, warp 1 MMA issuer and tensor-memory owner, warps 2-5 the
-// epilogue (warp w reads TMEM lanes 32 * (w % 4) .. +31, one output row per thread).
+// the next. 320 threads: warp 0 TMA producer, warp 1 MMA issuer and tensor-memory owner, warps 2-9 the
+// epilogue (warp w reads TMEM lanes 32 * (w % 4) .. +31, one output row per thread, and columns
+// 128 * ((w - 2) / 4) .. +127 of the tile: two warps per lane quarter double the store issue rate,
+// which limits the epilogue).
 #include <cuda_bf16.h>
 #include <cstdint>
 
@@ -102,7 +104,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sh->acc_full[b], 1);
-      mbar_init(&sh->acc_empty[b], 128);
+      mbar_init(&sh->acc_empty[b], 256);
     }
     mbar_init(&sh->drain, 1);
     sh->abort = 0;
@@ -177,8 +179,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
     mbar_drain_wait(&sh->drain, 0);
   } else {
-    // ------------------------------------------------ epilogue: TMEM -> scales, bias -> bf16
-    const int quarter = warp & 3;
+    // ------------------------------------------------ epilogue: TMEM -> scales, bias -> bf16 (8 warps)
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
     int lt = 0;
     bool ok = true;
@@ -192,7 +194,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const float xs = row_ok ? a.x_scale[row] : 0.f;
       __nv_bfloat16* dst = a.y + int64_t(row) * a.sy + tn * 256;
 #pragma unroll 1
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 4 * half; c < 4 * half + 4; ++c) {
         const int col0 = tn * 256 + c * 32;
         uint32_t v[32];
         tmem_ld32(tmem + 256 * buf + 32 * c + lane_off, v);

@@ -22,7 +22,7 @@ struct Fp8QuantArgs {
   float* scale;
 };
 // y [M][N] bf16 (row stride sy) = (q_x [M][K] . q_w [N][K]^T) * x_scale[m] * w_scale[n] + bias[n].
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;
 struct Fp8GemmArgs {
   const float* x_scale;
   const float* w_scale;

@@ -74,9 +74,17 @@ __device__ __forceinline__ uint4 rope_bf16x8(const uint4 raw, const double* cs, 
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// The buffer row of logical token t: through the ring map when the cache is a ring (kRing), else t.
+template <bool kRing>
+__device__ __forceinline__ int64_t ring_row(const Ring& r, int64_t t) {
+  if constexpr (kRing) return phys_tok(r, t);
+  return t;
+}
+
 // ------------------------------------------------------------------ K/V block statistics
 // One CTA per (64-token block, head, batch). ksum: fp64 sum of K over the block's tokens that are
 // < kv_len; vamax: max |V|. 128 threads = 8 row groups x 16 chunks of 8 channels.
+template <int kDt, bool kRing>
 __global__ void __launch_bounds__(128) kv_block_stats_kernel(KvBlockStatsArgs a) {
   const int blk = a.blk_begin + blockIdx.x;
   const int h = blockIdx.y, b = blockIdx.z;
@@ -88,12 +96,12 @@ __global__ void __launch_bounds__(128) kv_block_stats_kernel(KvBlockStatsArgs a)
   for (int r = rg; r < 64; r += 8) {
     const int64_t tok = int64_t(blk) * 64 + r;
     if (tok >= a.kv_len) break;
-    const int64_t row = phys_tok(a.ring, tok);
+    const int64_t row = ring_row<kRing>(a.ring, tok);
     const uint4 kr = *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + row * a.sk_l + h * a.sk_h + c16 * 8);
     const uint4 vr = *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + row * a.sv_l + h * a.sv_h + c16 * 8);
     float kf[8], vf[8];
-    act8_to_f32(kr, a.dtype, kf);
-    act8_to_f32(vr, a.dtype, vf);
+    act8_to_f32(kr, kDt, kf);
+    act8_to_f32(vr, kDt, vf);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       s[i] += double(kf[i]);
@@ -129,6 +137,7 @@ __global__ void __launch_bounds__(128) kv_block_stats_kernel(KvBlockStatsArgs a)
 // block's statistics in exactly kv_block_stats_kernel's order and thread layout, so the tables are
 // bit-identical to a copy followed by kv_block_stats. Tokens of the block before tok_begin are read
 // back from the cache.
+template <bool kRing>
 __global__ void __launch_bounds__(128) cache_write_kernel(CacheWriteArgs a) {
   const int blk = a.blk_begin + blockIdx.x;
   const int h = blockIdx.y, b = blockIdx.z;
@@ -140,7 +149,7 @@ __global__ void __launch_bounds__(128) cache_write_kernel(CacheWriteArgs a) {
   for (int r = rg; r < 64; r += 8) {
     const int64_t tok = int64_t(blk) * 64 + r;
     if (tok >= a.tok_end) break;
-    const int64_t row = phys_tok(a.ring, tok);
+    const int64_t row = ring_row<kRing>(a.ring, tok);
     __nv_bfloat16* kc = a.k_cache + b * a.ck_b + row * a.ck_l + h * a.ck_h + c16 * 8;
     __nv_bfloat16* vc = a.v_cache + b * a.cv_b + row * a.cv_l + h * a.cv_h + c16 * 8;
     uint4 kr, vr;
@@ -319,6 +328,7 @@ struct QuantKvShared {
   float red[8];
 };
 
+template <int kDt, bool kRing>
 __device__ __forceinline__ void quant_k_tile(const QuantKArgs& a, QuantKvShared& sh, int tile, bool first, int h,
                                              int b) {
   const int half = threadIdx.x >> 7, t = threadIdx.x & 127, c16 = t & 15, rg = t >> 4;
@@ -326,7 +336,7 @@ __device__ __forceinline__ void quant_k_tile(const QuantKArgs& a, QuantKvShared&
   const int64_t bh = int64_t(b) * a.heads + h;
   if (half == 0) {
     uint16_t km_bits;
-    const float km = window_mean_act(a.ksum_total, bh * 128 + t, a.kv_len_total, a.dtype, &km_bits);
+    const float km = window_mean_act(a.ksum_total, bh * 128 + t, a.kv_len_total, kDt, &km_bits);
     sh.km[t] = km;
     if (a.km_out != nullptr && first && a.write_km) reinterpret_cast<uint16_t*>(a.km_out)[bh * 128 + t] = km_bits;
   }
@@ -335,7 +345,7 @@ __device__ __forceinline__ void quant_k_tile(const QuantKArgs& a, QuantKvShared&
   for (int i = 0; i < 8; ++i) {
     const int64_t tok = int64_t(blk) * 64 + rg + 8 * i;      // token index inside this segment
     raw[i] = tok < a.seg_valid && LBQ_CHECK(a.tok0 + tok >= 0, a.status, kDevBadSourceToken)
-                 ? *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + phys_tok(a.ring, a.tok0 + tok) * a.sk_l +
+                 ? *reinterpret_cast<const uint4*>(a.k + b * a.sk_b + ring_row<kRing>(a.ring, a.tok0 + tok) * a.sk_l +
                                                    h * a.sk_h + c16 * 8)
                  : make_uint4(0u, 0u, 0u, 0u);
   }
@@ -349,7 +359,7 @@ __device__ __forceinline__ void quant_k_tile(const QuantKArgs& a, QuantKvShared&
     const int64_t tok = int64_t(blk) * 64 + rg + 8 * i;
     if (tok < a.seg_valid) {
       float x[8];
-      act8_to_f32(raw[i], a.dtype, x);
+      act8_to_f32(raw[i], kDt, x);
 #pragma unroll
       for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(__fsub_rn(x[j], km[j])));
     }
@@ -368,7 +378,7 @@ __device__ __forceinline__ void quant_k_tile(const QuantKArgs& a, QuantKvShared&
     const int r = rg + 8 * i;
     const bool valid = int64_t(blk) * 64 + r < a.seg_valid;   // pad tokens encode 0
     float x[8];
-    act8_to_f32(raw[i], a.dtype, x);
+    act8_to_f32(raw[i], kDt, x);
 #pragma unroll
     for (int j = 0; j < 8; ++j) x[j] = valid ? __fmul_rn(__fsub_rn(x[j], km[j]), inv) : 0.f;
     packed[i].x = pack_s8x4(cvt_rni_sat_s8(x[0]), cvt_rni_sat_s8(x[1]), cvt_rni_sat_s8(x[2]), cvt_rni_sat_s8(x[3]));
@@ -380,6 +390,7 @@ __device__ __forceinline__ void quant_k_tile(const QuantKArgs& a, QuantKvShared&
   for (int i = 0; i < 8; ++i) *reinterpret_cast<uint2*>(dst + (rg + 8 * i) * 128 + c16 * 8) = packed[i];
 }
 
+template <int kDt, bool kRing>
 __device__ __forceinline__ void quant_v_tile(const QuantVArgs& a, QuantKvShared& sh, int tile, bool first, int h,
                                              int b) {
   const int t = threadIdx.x;
@@ -395,7 +406,7 @@ __device__ __forceinline__ void quant_v_tile(const QuantVArgs& a, QuantKvShared&
     const int r = piece >> 4, c16 = piece & 15;
     const int64_t tok = int64_t(tile) * 128 + r;
     const uint4 raw = tok < a.seg_valid && LBQ_CHECK(a.tok0 + tok >= 0, a.status, kDevBadSourceToken)
-                          ? *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + phys_tok(a.ring, a.tok0 + tok) * a.sv_l +
+                          ? *reinterpret_cast<const uint4*>(a.v + b * a.sv_b + ring_row<kRing>(a.ring, a.tok0 + tok) * a.sv_l +
                                                             h * a.sv_h + c16 * 8)
                           : make_uint4(0u, 0u, 0u, 0u);
     *reinterpret_cast<uint4*>(&sh.v[r * kVtPitch + c16 * 16]) = raw;
@@ -412,7 +423,7 @@ __device__ __forceinline__ void quant_v_tile(const QuantVArgs& a, QuantKvShared&
       const int r = tq * 32 + 4 * k4 + e;
       const uint32_t pair = *reinterpret_cast<const uint32_t*>(&sh.v[r * kVtPitch + cp * 4]);
       float v0, v1;
-      act2_to_f32(pair, a.dtype, v0, v1);
+      act2_to_f32(pair, kDt, v0, v1);
       lo[e] = fminf(fmaxf(__fmul_rn(v0, r0), -2.25f), 2.25f);
       hi[e] = fminf(fmaxf(__fmul_rn(v1, r1), -2.25f), 2.25f);
     }
@@ -430,20 +441,27 @@ __device__ __forceinline__ void quant_v_tile(const QuantVArgs& a, QuantKvShared&
   d1[1] = make_uint4(w1[4], w1[5], w1[6], w1[7]);
 }
 
+template <int kDt, bool kRing>
 __global__ void __launch_bounds__(256) quant_kv_kernel(QuantKArgs ka, QuantVArgs va, int tile0) {
   __shared__ __align__(16) QuantKvShared sh;
   const int tile = tile0 + int(blockIdx.x >> 1), h = blockIdx.y, b = blockIdx.z;
   const bool first = (blockIdx.x >> 1) == 0;
-  if (blockIdx.x & 1) quant_v_tile(va, sh, tile, first, h, b);
-  else quant_k_tile(ka, sh, tile, first, h, b);
+  if (blockIdx.x & 1) quant_v_tile<kDt, kRing>(va, sh, tile, first, h, b);
+  else quant_k_tile<kDt, kRing>(ka, sh, tile, first, h, b);
 }
 
 // ------------------------------------------------------------------ launchers
+template <int kDt, bool kRing>
+cudaError_t launch_stats(const KvBlockStatsArgs& a, dim3 grid, cudaStream_t st) {
+  if (cudaError_t e0 = prefer_max_shared<kv_block_stats_kernel<kDt, kRing>>(); e0 != cudaSuccess) return e0;
+  kv_block_stats_kernel<kDt, kRing><<<grid, 128, 0, st>>>(a);
+  return cudaGetLastError();
+}
 cudaError_t launch_kv_block_stats(const KvBlockStatsArgs& a, cudaStream_t st) {
   dim3 grid(a.blk_end - a.blk_begin, a.heads, a.batch);
-  if (cudaError_t e0 = prefer_max_shared<kv_block_stats_kernel>(); e0 != cudaSuccess) return e0;
-  kv_block_stats_kernel<<<grid, 128, 0, st>>>(a);
-  return cudaGetLastError();
+  const bool ring = a.ring.len != 0;
+  if (a.dtype) return ring ? launch_stats<1, true>(a, grid, st) : launch_stats<1, false>(a, grid, st);
+  return ring ? launch_stats<0, true>(a, grid, st) : launch_stats<0, false>(a, grid, st);
 }
 cudaError_t launch_kv_window_sums(const KvWindowSumsArgs& a, cudaStream_t st) {
   dim3 grid(4, a.heads, a.batch);
@@ -461,8 +479,13 @@ cudaError_t launch_cache_write(const CacheWriteArgs& a, cudaStream_t st) {
   const int blk_end = int((a.tok_end + 63) / 64);
   if (blk_end <= a.blk_begin) return cudaSuccess;
   dim3 grid(blk_end - a.blk_begin, a.heads, a.batch);
-  if (cudaError_t e0 = prefer_max_shared<cache_write_kernel>(); e0 != cudaSuccess) return e0;
-  cache_write_kernel<<<grid, 128, 0, st>>>(a);
+  if (a.ring.len != 0) {
+    if (cudaError_t e0 = prefer_max_shared<cache_write_kernel<true>>(); e0 != cudaSuccess) return e0;
+    cache_write_kernel<true><<<grid, 128, 0, st>>>(a);
+  } else {
+    if (cudaError_t e0 = prefer_max_shared<cache_write_kernel<false>>(); e0 != cudaSuccess) return e0;
+    cache_write_kernel<false><<<grid, 128, 0, st>>>(a);
+  }
   return cudaGetLastError();
 }
 // `tiles` 128-token tiles from tile0, stopping at the last tile holding valid tokens: a short last
@@ -472,7 +495,10 @@ cudaError_t launch_quant_kv(const QuantKArgs& ka, const QuantVArgs& va, int tile
   // no carveout preference: the driver's choice measured fastest for this kernel (5.0 TB/s on the
   // 30-layer re-quant, 3.9 TB/s with the largest shared-memory split)
   dim3 grid(tiles * 2, ka.heads, ka.batch);
-  quant_kv_kernel<<<grid, 256, 0, st>>>(ka, va, tile0);
+  const bool ring = ka.ring.len != 0;
+  auto kern = ka.dtype ? (ring ? quant_kv_kernel<1, true> : quant_kv_kernel<1, false>)
+                       : (ring ? quant_kv_kernel<0, true> : quant_kv_kernel<0, false>);
+  kern<<<grid, 256, 0, st>>>(ka, va, tile0);
   return cudaGetLastError();
 }
 
