@@ -476,6 +476,7 @@ int lbq_fp8_gemm(const uint8_t* a, int64_t sa, const float* a_scale, const uint8
   g.tiles_m = (M + 127) / 128;
   g.tiles_n = (N + 255) / 256;
   g.status = lbq::device_status_ptr();
+  g.wide_stores = (sy % 16 == 0) && (reinterpret_cast<uintptr_t>(y) % 32 == 0);
   const int tiles = g.tiles_m * g.tiles_n;
   if (num_ctas <= 0) {
     int dev = 0, sms = 148;

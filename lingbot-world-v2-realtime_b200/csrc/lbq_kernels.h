@@ -32,6 +32,7 @@ struct Fp8GemmArgs {
   int M, N, K;
   int tiles_m, tiles_n;
   int* status;
+  int wide_stores;              // y and its row stride are 32-byte aligned: 256-bit stores
 };
 
 // Ring layout of a KV-cache buffer: logical token t (the reference's window position) lives at buffer

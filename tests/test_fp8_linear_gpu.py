@@ -53,6 +53,23 @@ def test_gemm_matches_scaled_mm_and_float64(m, n, k, with_bias):
     _check_against_exact(y, ref, exact)
 
 
+def test_gemm_into_a_strided_output():
+    """Output rows 16- but not 32-byte aligned (row stride N + 8): the epilogue's 16-byte store path, and
+    the padding columns left untouched."""
+    from lingbot_b200 import fp8_linear as L
+    g = torch.Generator().manual_seed(5)
+    m, n, k = 257, 256, 128
+    qx, sx = L.quant_rows(_rnd(g, m, k).bfloat16().cuda())
+    qw, sw = L.quant_rows(_rnd(g, n, k, scale=0.05).bfloat16().cuda())
+    big = torch.full((m, n + 8), 7.0, dtype=torch.bfloat16, device="cuda")
+    y = L.gemm(qx, sx, qw, sw, out=big[:, :n])
+    ref = torch._scaled_mm(qx, qw.t(), scale_a=sx.reshape(-1, 1), scale_b=sw.reshape(1, -1), out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert y.stride(0) == n + 8
+    assert bool((big[:, n:] == 7.0).all())
+    _check_against_exact(y, ref, F8.gemm(qx.cpu(), sx.cpu(), qw.cpu(), sw.cpu()))
+
+
 def _check_against_exact(y, ref, exact):
     """Each output within half a bf16 ulp of the float64 product plus an fp32-accumulation allowance,
     for this kernel; torch._scaled_mm's own error is reported beside it."""
