@@ -430,11 +430,5 @@ __device__ __forceinline__ uint64_t exp2_poly_x2(float x0, float x1) {
   return f2_pack(__uint_as_float(r0), __uint_as_float(r1));
 }
 
-// fp32 -> int8 code, round-half-even, saturating (cvt.rni.sat.s8.f32).
-__device__ __forceinline__ int32_t cvt_rni_sat_s8(float x) {
-  int32_t r;
-  asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
-}
 
 }  // namespace lbq

@@ -41,8 +41,15 @@ __device__ __forceinline__ void act8_to_f32(const uint4 raw, int dtype, float (&
   for (int i = 0; i < 4; ++i) act2_to_f32(w[i], dtype, f[2 * i], f[2 * i + 1]);
 }
 
-__device__ __forceinline__ uint32_t pack_s8x4(int32_t a, int32_t b, int32_t c, int32_t d) {
-  return (uint32_t(a) & 0xff) | ((uint32_t(b) & 0xff) << 8) | ((uint32_t(c) & 0xff) << 16) | (uint32_t(d) << 24);
+// Four values already in (-127.5, 127.5) to four int8 codes, round to nearest even, packed (the first in
+// the low byte): adding 1.5 * 2^23 rounds each to an integer held in the low mantissa bits, so byte 0
+// of the sum's bits is the code's two's-complement byte — the result of cvt.rni.sat.s8.f32 (no value
+// reaches the saturation bounds) on the FMA pipe instead of the conversion unit, and three byte
+// permutes instead of shifts and masks.
+__device__ __forceinline__ uint32_t pack_rn_s8x4(float a, float b, float c, float d) {
+  const uint32_t ua = __float_as_uint(__fadd_rn(a, 12582912.f)), ub = __float_as_uint(__fadd_rn(b, 12582912.f));
+  const uint32_t uc = __float_as_uint(__fadd_rn(c, 12582912.f)), ud = __float_as_uint(__fadd_rn(d, 12582912.f));
+  return __byte_perm(__byte_perm(ua, ub, 0x0040), __byte_perm(uc, ud, 0x0040), 0x5410);
 }
 
 __device__ __forceinline__ float warp_max(float x) {
@@ -281,10 +288,8 @@ __global__ void __launch_bounds__(256) quant_q_kernel(QuantQArgs a) {
     float x[8];
     act8_to_f32(raw[i], a.dtype, x);
     uint2 packed;
-    packed.x = pack_s8x4(cvt_rni_sat_s8(__fmul_rn(x[0], inv)), cvt_rni_sat_s8(__fmul_rn(x[1], inv)),
-                         cvt_rni_sat_s8(__fmul_rn(x[2], inv)), cvt_rni_sat_s8(__fmul_rn(x[3], inv)));
-    packed.y = pack_s8x4(cvt_rni_sat_s8(__fmul_rn(x[4], inv)), cvt_rni_sat_s8(__fmul_rn(x[5], inv)),
-                         cvt_rni_sat_s8(__fmul_rn(x[6], inv)), cvt_rni_sat_s8(__fmul_rn(x[7], inv)));
+    packed.x = pack_rn_s8x4(__fmul_rn(x[0], inv), __fmul_rn(x[1], inv), __fmul_rn(x[2], inv), __fmul_rn(x[3], inv));
+    packed.y = pack_rn_s8x4(__fmul_rn(x[4], inv), __fmul_rn(x[5], inv), __fmul_rn(x[6], inv), __fmul_rn(x[7], inv));
     *reinterpret_cast<uint2*>(dst + (2 * i + (l >> 4)) * 128 + c16 * 8) = packed;
   }
 }
@@ -381,8 +386,8 @@ __device__ __forceinline__ void quant_k_tile(const QuantKArgs& a, QuantKvShared&
     act8_to_f32(raw[i], kDt, x);
 #pragma unroll
     for (int j = 0; j < 8; ++j) x[j] = valid ? __fmul_rn(__fsub_rn(x[j], km[j]), inv) : 0.f;
-    packed[i].x = pack_s8x4(cvt_rni_sat_s8(x[0]), cvt_rni_sat_s8(x[1]), cvt_rni_sat_s8(x[2]), cvt_rni_sat_s8(x[3]));
-    packed[i].y = pack_s8x4(cvt_rni_sat_s8(x[4]), cvt_rni_sat_s8(x[5]), cvt_rni_sat_s8(x[6]), cvt_rni_sat_s8(x[7]));
+    packed[i].x = pack_rn_s8x4(x[0], x[1], x[2], x[3]);
+    packed[i].y = pack_rn_s8x4(x[4], x[5], x[6], x[7]);
   }
   int8_t* dst = a.k_codes + (seg_bh * a.seg_pad + int64_t(blk) * 64) * 128;
   if (t == 0) a.k_scale[seg_bh * (a.seg_pad / 64) + blk] = scale;
