@@ -715,7 +715,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               const float o1 = __fmul_rn(__fmul_rn(__uint_as_float(ov[2 * e + 1]), rd), vs[32 * c + 2 * e + 1]);
               packed[e] = pack_act2(o0, o1, a.dtype);
             }
-            if (row < a.q_len) {
+            if (row < a.q_len && a.wide_out) {         // 32-byte aligned rows: 256-bit stores
+              st_global_v8(dst + 32 * c, packed);
+              st_global_v8(dst + 32 * c + 16, packed + 8);
+            } else if (row < a.q_len) {
 #pragma unroll
               for (int e = 0; e < 4; ++e)
                 reinterpret_cast<uint4*>(dst + 32 * c)[e] =
@@ -730,7 +733,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             uint32_t ov[32];
             tmem_ld32(tO + 32 * c, ov);
             tmem_ld_wait(ov);
-            if (row < a.q_len) {
+            if (row < a.q_len && a.wide_part) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) st_global_v8(dst + 32 * c + 8 * e, ov + 8 * e);
+            } else if (row < a.q_len) {
 #pragma unroll
               for (int e = 0; e < 8; ++e)
                 reinterpret_cast<uint4*>(dst + 32 * c)[e] =

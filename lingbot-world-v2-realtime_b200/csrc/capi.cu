@@ -406,6 +406,8 @@ int lbq_attn_fwd(const int8_t* q_codes, const float* q_scale, int q_len, const i
   if (sm_scale <= 0.f) sm_scale = 0.08838834764831845f;   // 128 ** -0.5
   lbq::AttnArgs a{};
   a.dtype = dtype;
+  a.wide_out = (reinterpret_cast<uintptr_t>(out) % 32 == 0) && so_b % 16 == 0 && so_l % 16 == 0 && so_h % 16 == 0;
+  a.wide_part = o_part != nullptr && reinterpret_cast<uintptr_t>(o_part) % 32 == 0;
   a.q_scale = q_scale;
   a.k_scale = k_scale;
   a.v_scale = v_scale;

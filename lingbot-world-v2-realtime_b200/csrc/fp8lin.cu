@@ -215,11 +215,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         if (row_ok && a.wide_stores) {                 // 32-byte aligned rows: two 256-bit stores
 #pragma unroll
-          for (int q = 0; q < 2; ++q)
-            asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst + c * 32 + 16 * q),
-                         "r"(packed[8 * q]), "r"(packed[8 * q + 1]), "r"(packed[8 * q + 2]), "r"(packed[8 * q + 3]),
-                         "r"(packed[8 * q + 4]), "r"(packed[8 * q + 5]), "r"(packed[8 * q + 6]), "r"(packed[8 * q + 7])
-                         : "memory");
+          for (int q = 0; q < 2; ++q) st_global_v8(dst + c * 32 + 16 * q, packed + 8 * q);
         } else if (row_ok) {
 #pragma unroll
           for (int q = 0; q < 4; ++q)

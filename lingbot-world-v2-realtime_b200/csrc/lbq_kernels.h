@@ -170,6 +170,8 @@ struct AttnArgs {
   int64_t xchg_off;
   int64_t recv_o_off;         // heap offset of the receive slots [ranks][B*H][part][128] fp16
   int64_t recv_ml_off;        //                                  [ranks][B*H][part] float2
+  int wide_out;               // out's base and row strides are 32-byte aligned: 256-bit stores
+  int wide_part;              // o_part is 32-byte aligned: 256-bit stores of the split partials
   int dtype;                  // out: 0 bf16, 1 fp16 (one-pass and split-KV modes)
 };
 

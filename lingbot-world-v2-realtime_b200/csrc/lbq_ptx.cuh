@@ -365,6 +365,12 @@ __device__ __forceinline__ uint32_t pack_act2(float lo, float hi, int dtype) {
   const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&p);
 }
+// One 256-bit global store of eight 32-bit words (the address 32-byte aligned).
+__device__ __forceinline__ void st_global_v8(void* p, const uint32_t* w) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+               "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
 // The two activations of a 32-bit pair (dtype 0: bf16, 1: fp16) as floats (exact).
 __device__ __forceinline__ void act2_to_f32(uint32_t w, int dtype, float& lo, float& hi) {
   if (dtype) {
