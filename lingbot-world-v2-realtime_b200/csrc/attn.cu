@@ -62,10 +62,18 @@ constexpr float kMagic = 12582912.0f;    // 1.5 * 2^23
 constexpr uint32_t kMagicBits = 0x4B400000u;
 constexpr uint32_t kMaskedBits = 0x4B000000u;   // 1.5*2^23 - 2^22: below every real score
 constexpr uint32_t kColS = 0, kColO = 256;
-// Registers per thread after the split (launched with 128): softmax 160, correction 120, producer and
-// issuer warpgroup 72: 128 x (160 + 160 + 120 + 72) = 65536 = 512 x 128.
-constexpr uint32_t kRegSoftmax = 160, kRegCorrection = 120, kRegMisc = 72;
-static_assert(128 * (2 * kRegSoftmax + kRegCorrection + kRegMisc) <= kAttnThreads * 128, "register split");
+// Registers per thread after the split (launched with 128; a warpgroup's share times 128 threads, summed
+// over the four warpgroups, must stay within 512 x 128 or setmaxnreg.inc would wait for good). One-pass
+// kernel: softmax 184, correction 104, producers and issuers 40 — the split at which ptxas reports no
+// spills (measured 1179 -> 1189 TOPS against 160/120/72). Key-range kernel: 160/120/72 (184/104/40
+// spills 436 bytes there; 168/120/56, measured, is 0.5 % slower).
+template <bool kKeyRange>
+struct RegSplit {
+  static constexpr uint32_t softmax = kKeyRange ? 160 : 184;
+  static constexpr uint32_t correction = kKeyRange ? 120 : 104;
+  static constexpr uint32_t misc = kKeyRange ? 72 : 40;
+  static_assert(128 * (2 * softmax + correction + misc) <= kAttnThreads * 128, "register split");
+};
 
 // In the bulk tiles with the folded exp2 argument, of every 16 key pairs this many take the FMA-pipe
 // polynomial exp2 (relative error 7.5e-5) instead of MUFU ex2, the busiest unit (measured: 2 of 16 is
@@ -416,7 +424,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem = sh->tmem_base;
 
   if (warp >= 12) {
-    reg_dealloc<kRegMisc>();
+    reg_dealloc<RegSplit<kKeyRange>::misc>();
     if (warp == 12 && n > 0) {
       // ---------------------------------------------------------- TMA producer of Q and K (one lane issues)
       if (elect_one()) {
@@ -479,7 +487,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (!(ok = mbar_wait_role(&sh->k_full[s], (k / kStages) & 1, abort_flag, a.status, kDevTimeoutKV))) break;
         const uint64_t kdesc = kdesc0 + s * kTileDesc;
         for (int t = 0; ok && t < 2; ++t) {
-          if (!(ok = mbar_wait_role(&sh->s_free[t], k & 1, abort_flag, a.status, kDevTimeoutS))) break;
+          // polled without sleeping: the refill -> Q.K^T hand-off is on the softmax's path
+          if (!(ok = mbar_wait(&sh->s_free[t], k & 1, abort_flag, a.status, kDevTimeoutS))) break;
           tc_fence_after();
           if (elect_one()) {
 #pragma unroll
@@ -513,7 +522,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint64_t vdesc = vdesc0 + s * kTileDesc;
         for (int hh = 0; ok && hh < ns; ++hh, ++u) {
           for (int t = 0; t < 2; ++t) {
-            if (!(ok = mbar_wait_role(&sh->o_ready[t], u & 1, abort_flag, a.status, kDevTimeoutP))) break;
+            // polled without sleeping (measured 1172 -> 1181 TOPS against the 64 ns sleep of the producers)
+            if (!(ok = mbar_wait(&sh->o_ready[t], u & 1, abort_flag, a.status, kDevTimeoutP))) break;
             tc_fence_after();
             const uint64_t pdesc = pdesc0 + (kPBufs * t + pbuf(j)) * kTileDesc + 4 * hh;
             if (elect_one()) {
@@ -540,7 +550,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else if (warp < 8) {
     // ------------------------------------------------------------ softmax warpgroups
-    reg_alloc<kRegSoftmax>();
+    reg_alloc<RegSplit<kKeyRange>::softmax>();
     const int t = warp >> 2;                            // Q tile of this warpgroup
     const int quarter = warp & 3;                       // TMEM lanes [32*quarter, 32*quarter+32)
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
@@ -634,7 +644,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ correction + epilogue
-    reg_dealloc<kRegCorrection>();
+    reg_dealloc<RegSplit<kKeyRange>::correction>();
     const int quarter = warp & 3;
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
     const int rl = quarter * 32 + lane;

@@ -134,8 +134,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 #ifndef LBQ_ROLE_SLEEP_NS
 #define LBQ_ROLE_SLEEP_NS 64
 #endif
-// mbar_wait for the producer and issuer warps, which share their SM sub-partition with softmax warps:
-// between polls the warp sleeps LBQ_ROLE_SLEEP_NS, so that its polling does not take their issue slots.
+// mbar_wait for the TMA producer warps and the issuers' waits that are not on the softmax's path, which
+// share their SM sub-partition with softmax warps: between polls the warp sleeps LBQ_ROLE_SLEEP_NS, so
+// that its polling does not take their issue slots.
 __device__ __forceinline__ bool mbar_wait_role(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
                                                int code) {
   if (mbar_try_wait(bar, parity)) return true;
