@@ -164,3 +164,35 @@ def test_cross_attention_through_the_quantized_kernel():
         assert not torch.equal(masked, out)
     finally:
         attention.set_cross_attention("paper")
+
+
+@pytest.mark.parametrize("splits", [1, 3])
+def test_output_alignment_paths_agree(splits):
+    """The epilogue stores 32-byte-aligned output rows and split partials with 256-bit stores and anything
+    else with 16-byte stores: an output view and split partials 16- but not 32-byte aligned give the same
+    bits as the aligned buffers, and the padding around the view is untouched."""
+    import ctypes
+    from lingbot_b200 import _lib, ops
+    q, k, v = make_qkv(11, 1, 3, 300, 2000)
+    w = ops.quantize_qkv(q, k, v)
+    ref = ops.attn_from_codes(w, num_splits=splits)
+    big = torch.full((1, 300, 3, 128 + 8), 3.0, dtype=torch.bfloat16, device="cuda")
+    out = big[..., 8:]                                   # rows start 16 bytes past a 32-byte boundary
+    b, h, q_pad = 1, 3, w.q_codes.shape[2]
+    o_buf = torch.empty(splits * b * h * q_pad * 128 + 4, dtype=torch.float32, device="cuda")
+    ml = torch.empty(splits, b * h, q_pad, 2, dtype=torch.float32, device="cuda")
+    o_part = o_buf[4:]                                   # 16 bytes past the allocation's start
+    used = ctypes.c_int(1)
+    _lib.call("lbq_attn_fwd", ops._ptr(w.q_codes), ops._ptr(w.q_scale), w.q_len, ops._ptr(w.k_codes),
+              ops._ptr(w.k_scale), ops._ptr(w.vt_codes), ops._ptr(w.v_scale), w.kv_len, w.num_segments, w.seg_len,
+              b, h, 0.0, 0, ops._ptr(out), *out.stride()[:3], splits,
+              ops._ptr(o_part) if splits > 1 else None, ops._ptr(ml) if splits > 1 else None, ctypes.byref(used),
+              0, ops._stream())
+    if used.value > 1:
+        _lib.call("lbq_splitkv_combine", ops._ptr(o_part), ops._ptr(ml), used.value, ops._ptr(w.v_scale), b, h,
+                  w.q_len, ops._ptr(out), *out.stride()[:3], 0, ops._stream())
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    assert out.data_ptr() % 32 == 16 and (splits == 1 or o_part.data_ptr() % 32 == 16)
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+    assert bool((big[..., :8] == 3.0).all())
