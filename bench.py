@@ -960,6 +960,7 @@ def run_linear(args, world, rank, local):
     peak = 2.0 * peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
     tops = flops / (ms * 1e-3) / 1e12
     return dict(tops=tops, ms=ms, clocks=clocks, launches=2 * len(dims) * args.steps, e2e=None,
+                dtype="fp8 e4m3 x e4m3, fp32 accumulation (bf16 in/out)",
                 roofline={"bound": "tensor", "achieved": round(gemm_tops, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
                           "frac": round(gemm_tops / peak, 4), "traffic": None, "kernel": "fp8_gemm_kernel",
                           "peak_source": f"2 x bf16_tflops_sustained ({src}); B200's dense FP8 rate is twice its bf16 rate",
@@ -1006,6 +1007,7 @@ def run_evict(args, world, rank, local):
         torch.cuda.empty_cache()
     rolled = LK - sink - n
     return dict(tops=res["ring"], ms=res["ring"], clocks=clocks, launches=LAYERS * 2 * args.steps, e2e=None, unit="ms",
+                dtype="bf16 (cache rows and block statistics)",
                 higher_is_better=False,
                 roofline={"bound": "hbm", "achieved": None, "peak": None, "unit": "GB/s", "frac": None,
                           "traffic": None, "kernel": "kv_block_stats_kernel + cache_write_kernel",
@@ -1051,6 +1053,7 @@ def run_requant(args, world, rank, local):
     peaks, src = measured_peaks()
     gbs = alg_bytes / (ms * 1e-3) / 1e9
     return dict(tops=gbs, ms=ms, clocks=clocks, launches=2 * args.steps, e2e=None, unit="GB/s",
+                dtype="bf16 in, int8 K / e4m3 V codes out",
                 roofline={"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                           "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": None,
                           "kernel": "quant_kv_kernel", "peak_source": src,
@@ -1130,7 +1133,7 @@ def main():
                     "warmup": args.warmup, "ms_per_step": round(res["ms"], 3), "s_per_chunk": round(res["ms"] / 1e3, 5),
                     "higher_is_better": res.get("higher_is_better", True), "scaling": res.get("scaling", "strong"),
                     "vs_baseline": None,
-                    "dtype": "int8 QK^T / fp8 e4m3 PV (bf16 in/out)", "data": "synthetic",
+                    "dtype": res.get("dtype", "int8 QK^T / fp8 e4m3 PV (bf16 in/out)"), "data": "synthetic",
                     "config": {"workload": {"chunk": "BASELINE config 4: full chunk, 4 denoise + 1 memory-write pass x 30 layers",
                                             "call": f"BASELINE config 1: q 6032 x kv {args.call_kv}",
                                             "requant": "BASELINE config 2: bf16 cache [30, 24128, 12, 128]"}[args.workload],
