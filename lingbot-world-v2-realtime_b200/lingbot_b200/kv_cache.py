@@ -21,8 +21,6 @@ of a ring cache materialises the logical slice (a copy), for callers that need b
 """
 from __future__ import annotations
 
-import ctypes
-
 import torch
 
 from . import _lib, ops
