@@ -741,8 +741,9 @@ TEXT_LEN = 512                     # text tokens of the cross-attention (T5 cont
 
 
 def run_cross(args, world, rank, local):
-    """Cross-attention through the self-attention kernel: the chunk's 6032 query rows against the 512 text keys, 12
-    heads x 128, through the reference's cross-attention entry `flash_attention(q, k, v, k_lens=None)`
+    """Cross-attention through the self-attention kernel: the chunk's 6032 query rows against the 512
+    text keys, 12 heads x 128, through the reference's cross-attention entry
+    `flash_attention(q, k, v, k_lens=None)`
     (transformer.py:272) in the quantized mode: Q, K and V quantized and the same attention kernel as
     self-attention. Inputs cycle through 8 sets (> L2): q ~ N(0, 1), text K/V ~ N(0, 0.5). The paper's
     unquantized attention (torch SDPA, bf16) is timed on the same inputs beside it."""
